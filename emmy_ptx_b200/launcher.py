@@ -1,0 +1,240 @@
+"""ctypes binding of ``libemmy_launch.so`` (declared in ``include/emmy_launch.h``).
+
+This is the only route by which the backend touches the GPU: module loading, launches, events,
+copies and the NCCL all-reduce all go through the C ABI.  There is no fallback: if the library is
+missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libemmy_launch.so"
+
+c_u32p = ctypes.POINTER(ctypes.c_uint32)
+c_u64p = ctypes.POINTER(ctypes.c_uint64)
+vp = ctypes.c_void_p
+
+# name -> argtypes (all functions return int)
+SIGNATURES = {
+    "emmy_version": [],
+    "emmy_last_error": [ctypes.c_char_p, ctypes.c_size_t],
+    "emmy_init": [ctypes.c_int],
+    "emmy_device_attribute": [ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
+    "emmy_module_load_ptx": [ctypes.c_char_p, ctypes.POINTER(vp), ctypes.c_char_p, ctypes.c_size_t],
+    "emmy_module_load_image": [vp, ctypes.POINTER(vp)],
+    "emmy_module_unload": [vp],
+    "emmy_get_function": [vp, ctypes.c_char_p, ctypes.POINTER(vp)],
+    "emmy_set_max_dyn_smem": [vp, ctypes.c_int],
+    "emmy_func_attribute": [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
+    "emmy_launch": [vp, c_u32p, c_u32p, c_u32p, ctypes.c_uint32, vp, ctypes.POINTER(vp), ctypes.c_uint32],
+    "emmy_launch_u64": [vp, c_u32p, c_u32p, ctypes.c_uint32, vp, c_u64p, c_u32p, ctypes.c_uint32],
+    "emmy_tmap_encode_tiled": [vp, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, c_u64p, c_u64p, c_u32p,
+                               c_u32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int],
+    "emmy_event_create": [ctypes.POINTER(vp)],
+    "emmy_event_destroy": [vp],
+    "emmy_event_record": [vp, vp],
+    "emmy_event_synchronize": [vp],
+    "emmy_event_elapsed_ms": [vp, vp, ctypes.POINTER(ctypes.c_float)],
+    "emmy_stream_synchronize": [vp],
+    "emmy_ctx_synchronize": [],
+    "emmy_mem_alloc": [c_u64p, ctypes.c_size_t],
+    "emmy_mem_free": [ctypes.c_uint64],
+    "emmy_memset_d32_async": [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_size_t, vp],
+    "emmy_memcpy_htod_async": [ctypes.c_uint64, vp, ctypes.c_size_t, vp],
+    "emmy_memcpy_dtoh_async": [vp, ctypes.c_uint64, ctypes.c_size_t, vp],
+    "emmy_nccl_available": [],
+    "emmy_nccl_get_unique_id": [ctypes.c_char_p],
+    "emmy_nccl_init": [ctypes.c_int, ctypes.c_int, ctypes.c_char_p],
+    "emmy_allreduce_sum": [ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int, vp],
+    "emmy_nccl_destroy": [],
+}
+
+# CUfunction_attribute values used by the runtime
+ATTR_NUM_REGS = 4
+ATTR_LOCAL_SIZE_BYTES = 3
+ATTR_MAX_THREADS = 0
+# CUdevice_attribute
+DEV_MULTIPROCESSOR_COUNT = 16
+DEV_L2_CACHE_SIZE = 38
+
+
+class EmmyError(RuntimeError):
+    """A failing C-ABI call: ``code`` is the returned status, the message the library's."""
+
+    def __init__(self, code: int, what: str, msg: str):
+        super().__init__(f"{what}: status {code}: {msg}")
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load_library(path: Path | None = None):
+    """Open ``libemmy_launch.so`` (building it first if it is missing and nvcc is present)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = Path(path or LIB_PATH)
+        if not p.exists():
+            from . import build
+            build.build()
+        lib = ctypes.CDLL(str(p))
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(4096)
+    load_library().emmy_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        raise EmmyError(code, what, last_error())
+
+
+def dims3(v) -> ctypes.Array:
+    v = [int(x) for x in (list(v) + [1, 1, 1])[:3]]
+    return (ctypes.c_uint32 * 3)(*v)
+
+
+class Device:
+    """The launcher bound to one CUDA device (its primary context)."""
+
+    _inited: dict[int, "Device"] = {}
+
+    def __init__(self, index: int = 0):
+        self.lib = load_library()
+        self.index = index
+        check(self.lib.emmy_init(index), f"emmy_init({index})")
+        self.launches = 0
+
+    @classmethod
+    def get(cls, index: int = 0) -> "Device":
+        dev = cls._inited.get(index)
+        if dev is None:
+            dev = cls(index)
+            cls._inited[index] = dev
+        else:
+            check(dev.lib.emmy_init(index), f"emmy_init({index})")
+        return dev
+
+    def attribute(self, attr: int) -> int:
+        v = ctypes.c_int()
+        check(self.lib.emmy_device_attribute(attr, ctypes.byref(v)), "emmy_device_attribute")
+        return v.value
+
+    def load_ptx(self, ptx: str):
+        mod = vp()
+        log = ctypes.create_string_buffer(16384)
+        check(self.lib.emmy_module_load_ptx(ptx.encode("ascii"), ctypes.byref(mod), log, len(log)),
+              "emmy_module_load_ptx")
+        return mod
+
+    def load_image(self, image: bytes):
+        mod = vp()
+        buf = ctypes.create_string_buffer(image, len(image))
+        check(self.lib.emmy_module_load_image(ctypes.cast(buf, vp), ctypes.byref(mod)), "emmy_module_load_image")
+        return mod
+
+    def unload(self, mod) -> None:
+        check(self.lib.emmy_module_unload(mod), "emmy_module_unload")
+
+    def function(self, mod, entry: str):
+        fn = vp()
+        check(self.lib.emmy_get_function(mod, entry.encode(), ctypes.byref(fn)), f"emmy_get_function({entry})")
+        return fn
+
+    def func_attribute(self, fn, attr: int) -> int:
+        v = ctypes.c_int()
+        check(self.lib.emmy_func_attribute(fn, attr, ctypes.byref(v)), "emmy_func_attribute")
+        return v.value
+
+    def set_max_dyn_smem(self, fn, nbytes: int) -> None:
+        check(self.lib.emmy_set_max_dyn_smem(fn, int(nbytes)), "emmy_set_max_dyn_smem")
+
+    def launch_u64(self, fn, grid, block, dyn_smem: int, stream: int, params, align=None) -> None:
+        n = len(params)
+        p = (ctypes.c_uint64 * n)(*[int(x) for x in params])
+        a = (ctypes.c_uint32 * n)(*[int(x) for x in align]) if align is not None else None
+        check(self.lib.emmy_launch_u64(fn, dims3(grid), dims3(block), int(dyn_smem), vp(stream or 0), p, a, n),
+              "emmy_launch_u64")
+        self.launches += 1
+
+    def launch(self, fn, grid, block, dyn_smem: int, stream: int, arg_ptrs, cluster=(1, 1, 1)) -> None:
+        n = len(arg_ptrs)
+        args = (vp * n)(*arg_ptrs)
+        check(self.lib.emmy_launch(fn, dims3(grid), dims3(block), dims3(cluster), int(dyn_smem),
+                                   vp(stream or 0), args, n), "emmy_launch")
+        self.launches += 1
+
+    def tmap_encode_tiled(self, out_buf, dtype: int, gaddr: int, dims, strides_bytes, box, elem_strides=None,
+                          swizzle: int = 0, l2promo: int = 2, oob_fill: int = 0, interleave: int = 0) -> None:
+        rank = len(dims)
+        d = (ctypes.c_uint64 * rank)(*dims)
+        s = (ctypes.c_uint64 * max(rank - 1, 1))(*(list(strides_bytes) or [0]))
+        bx = (ctypes.c_uint32 * rank)(*box)
+        es = (ctypes.c_uint32 * rank)(*(elem_strides or [1] * rank))
+        check(self.lib.emmy_tmap_encode_tiled(out_buf, dtype, rank, int(gaddr), d, s, bx, es, interleave,
+                                              swizzle, l2promo, oob_fill), "emmy_tmap_encode_tiled")
+
+    def memset_d32(self, dptr: int, value: int, count: int, stream: int) -> None:
+        check(self.lib.emmy_memset_d32_async(int(dptr), value & 0xFFFFFFFF, int(count), vp(stream or 0)),
+              "emmy_memset_d32_async")
+
+    def htod(self, dst: int, src_ptr: int, nbytes: int, stream: int) -> None:
+        check(self.lib.emmy_memcpy_htod_async(int(dst), vp(src_ptr), int(nbytes), vp(stream or 0)),
+              "emmy_memcpy_htod_async")
+
+    def dtoh(self, dst_ptr: int, src: int, nbytes: int, stream: int) -> None:
+        check(self.lib.emmy_memcpy_dtoh_async(vp(dst_ptr), int(src), int(nbytes), vp(stream or 0)),
+              "emmy_memcpy_dtoh_async")
+
+    def sync(self, stream: int | None = None) -> None:
+        if stream is None:
+            check(self.lib.emmy_ctx_synchronize(), "emmy_ctx_synchronize")
+        else:
+            check(self.lib.emmy_stream_synchronize(vp(stream)), "emmy_stream_synchronize")
+
+    # events
+    def event(self):
+        ev = vp()
+        check(self.lib.emmy_event_create(ctypes.byref(ev)), "emmy_event_create")
+        return ev
+
+    def record(self, ev, stream: int) -> None:
+        check(self.lib.emmy_event_record(ev, vp(stream or 0)), "emmy_event_record")
+
+    def elapsed_ms(self, a, b) -> float:
+        check(self.lib.emmy_event_synchronize(b), "emmy_event_synchronize")
+        ms = ctypes.c_float()
+        check(self.lib.emmy_event_elapsed_ms(a, b, ctypes.byref(ms)), "emmy_event_elapsed_ms")
+        return ms.value
+
+    def destroy_event(self, ev) -> None:
+        check(self.lib.emmy_event_destroy(ev), "emmy_event_destroy")
+
+    # NCCL
+    def nccl_unique_id(self) -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(self.lib.emmy_nccl_get_unique_id(buf), "emmy_nccl_get_unique_id")
+        return buf.raw[:128]
+
+    def nccl_init(self, rank: int, nranks: int, uid: bytes) -> None:
+        check(self.lib.emmy_nccl_init(rank, nranks, ctypes.create_string_buffer(uid, 128)), "emmy_nccl_init")
+
+    def allreduce_sum(self, dptr: int, count: int, dtype: str, stream: int) -> None:
+        code = {"f32": 0, "i32": 1}[dtype]
+        check(self.lib.emmy_allreduce_sum(int(dptr), int(count), code, vp(stream or 0)), "emmy_allreduce_sum")
+
+    def nccl_destroy(self) -> None:
+        check(self.lib.emmy_nccl_destroy(), "emmy_nccl_destroy")

@@ -1,0 +1,124 @@
+"""Run compiled modules: load the PTX through the C ABI and launch each entry on torch tensors.
+
+``Executable`` is the successor of the reference's launch harness (tools/localrun.py:137-206,
+tools/bench.py:86-115): it loads a module once, then each call zeroes the outputs a kernel's
+record lists (``zero_outputs``, tools/stress.py:106-111), checks every pointer's alignment against
+what the emitted code assumes, encodes TMA descriptors for tensor-core kernels, and launches
+the entries in order on the caller's stream.  Buffers are caller-owned tensors on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+
+from .compiler import CompiledModule, compile_ir
+from .launcher import Device
+
+_TMAP_DTYPE = {"bf16": 10, "f16": 6, "f32": 7, "u8": 0}   # CUtensorMapDataType
+_SWIZZLE = {"none": 0, "32B": 1, "64B": 2, "128B": 3}
+
+
+class _TmapBlob(ctypes.Structure):
+    _pack_ = 64
+    _fields_ = [("bytes", ctypes.c_uint8 * 128)]
+
+
+class Executable:
+    """A compiled module loaded on one device."""
+
+    def __init__(self, compiled: CompiledModule | str, device: int | None = None):
+        import torch
+        if isinstance(compiled, str):
+            compiled = compile_ir(compiled)
+        self.compiled = compiled
+        self.index = torch.cuda.current_device() if device is None else device
+        self.dev = Device.get(self.index)
+        self.module = self.dev.load_ptx(compiled.ptx)
+        self.funcs = []
+        for rec in compiled.kernels:
+            fn = self.dev.function(self.module, rec["entry"])
+            if rec.get("dyn_smem", 0) > 48 * 1024:
+                self.dev.set_max_dyn_smem(fn, rec["dyn_smem"])
+            self.funcs.append(fn)
+        self._tmap_cache: dict = {}
+
+    @property
+    def records(self) -> list[dict]:
+        return self.compiled.kernels
+
+    def registers(self, i: int = 0) -> int:
+        from .launcher import ATTR_NUM_REGS
+        return self.dev.func_attribute(self.funcs[i], ATTR_NUM_REGS)
+
+    def _tmap(self, spec: dict, t) -> ctypes.Array:
+        key = (spec["name"], t.data_ptr(), tuple(t.shape))
+        hit = self._tmap_cache.get(key)
+        if hit is not None:
+            return hit
+        blob = _TmapBlob()
+        dims = spec["dims"]
+        strides = spec["strides"]
+        self.dev.tmap_encode_tiled(ctypes.byref(blob), _TMAP_DTYPE[spec["dtype"]], t.data_ptr(), dims, strides,
+                                   spec["box"], swizzle=_SWIZZLE[spec.get("swizzle", "128B")],
+                                   l2promo=spec.get("l2promo", 2))
+        self._tmap_cache[key] = blob
+        return blob
+
+    def zero_outputs(self, i: int, tensors: dict, stream: int) -> None:
+        """Zero the outputs entry ``i`` accumulates into (its record's ``zero_outputs``)."""
+        for name in self.records[i].get("zero_outputs", []):
+            t = tensors[name]
+            nbytes = t.numel() * t.element_size()
+            if nbytes % 4:
+                raise ValueError(f"zeroed output {name!r} is not a whole number of 32-bit words")
+            self.dev.memset_d32(t.data_ptr(), 0, nbytes // 4, stream)
+
+    def launch(self, i: int, tensors: dict, stream: int, grid=None, zero: bool = True) -> None:
+        """Launch entry ``i`` with its parameters taken from ``tensors`` by name."""
+        rec = self.records[i]
+        fn = self.funcs[i]
+        if zero:
+            self.zero_outputs(i, tensors, stream)
+        g = grid or rec["grid"]
+        if not g or not rec["block"]:
+            raise ValueError(f"kernel {rec['entry']!r} has no launch geometry (no meta.json record)")
+        if rec.get("tmaps") or rec.get("extra"):
+            args = []
+            keep = []
+            for name in rec["params"]:
+                v = ctypes.c_uint64(tensors[name].data_ptr())
+                keep.append(v)
+                args.append(ctypes.cast(ctypes.byref(v), ctypes.c_void_p).value)
+            for spec in rec.get("tmaps", []):
+                blob = self._tmap(spec, tensors[spec["tensor"]])
+                keep.append(blob)
+                args.append(ctypes.cast(ctypes.byref(blob), ctypes.c_void_p).value)
+            for spec in rec.get("extra", []):
+                v = ctypes.c_uint64(int(spec["value"]) if "value" in spec else tensors[spec["name"]].data_ptr())
+                keep.append(v)
+                args.append(ctypes.cast(ctypes.byref(v), ctypes.c_void_p).value)
+            self.dev.launch(fn, g, rec["block"], rec.get("dyn_smem", 0), stream, args,
+                            cluster=rec.get("cluster", (1, 1, 1)))
+            return
+        ptrs, align = [], []
+        for name in rec["params"]:
+            t = tensors[name]
+            ptrs.append(t.data_ptr() if hasattr(t, "data_ptr") else int(t))
+            align.append(int(rec.get("align", {}).get(name, 1)))
+        self.dev.launch_u64(fn, g, rec["block"], rec.get("dyn_smem", 0), stream, ptrs, align)
+
+    def __call__(self, tensors: dict, stream: int | None = None) -> None:
+        """Run every entry of the module once, in order, on ``stream`` (default: torch's current)."""
+        import torch
+        if stream is None:
+            stream = torch.cuda.current_stream(self.index).cuda_stream
+        for i in range(len(self.records)):
+            self.launch(i, tensors, stream)
+
+    @property
+    def launches(self) -> int:
+        return self.dev.launches
+
+    def close(self) -> None:
+        if self.module is not None:
+            self.dev.unload(self.module)
+            self.module = None

@@ -1,0 +1,119 @@
+/*
+ * emmy_launch.h - C ABI of the B200 launcher for kernels emitted by the emmy_ptx_b200 backend.
+ *
+ * It replaces the reference's ctypes path over nvcuda.dll (tools/localrun.py:32-105,
+ * tools/oracle.py:37-157, tools/bench.py:32-83): the same driver-API steps (load a module from
+ * PTX, look up an entry, raise the dynamic shared-memory limit, launch, time with events, copy)
+ * behind plain pointers and sizes, plus TMA descriptor encoding and one NCCL all-reduce.
+ *
+ * Conventions
+ *  - Every function returns 0 on success.  Non-zero values are the CUresult of the failing
+ *    driver call, EMMY_ERR_NCCL_BASE + ncclResult_t for NCCL, or one of the EMMY_ERR_* codes.
+ *    emmy_last_error() returns a description of the last failure on the calling thread.
+ *    Nothing in this library calls exit() or abort().
+ *  - Device pointers are CUdeviceptr values (uint64_t) owned by the caller; module, function,
+ *    event and communicator handles are owned by the library.
+ *  - One CUDA context per device: the device's primary context (the one the CUDA runtime and
+ *    PyTorch use), made current on the calling thread by emmy_init().  Multi-GPU runs use one
+ *    process per GPU.
+ *  - libcuda.so.1 and libnccl.so.2 are opened on first use, so the library itself loads on a
+ *    host without a GPU.
+ */
+#ifndef EMMY_LAUNCH_H
+#define EMMY_LAUNCH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EMMY_ERR_NO_DRIVER 10001   /* libcuda.so.1 could not be opened or lacks a symbol */
+#define EMMY_ERR_NOT_INIT 10002    /* emmy_init() has not succeeded on this thread */
+#define EMMY_ERR_BAD_ARG 10003     /* null handle, zero size, misaligned pointer, ... */
+#define EMMY_ERR_NO_NCCL 10004     /* libnccl.so.2 could not be opened or lacks a symbol */
+#define EMMY_ERR_NCCL_BASE 20000   /* + ncclResult_t */
+
+/* ABI version of this header (bumped on incompatible change). */
+int emmy_version(void);
+
+/* Copies the last error message of this thread into buf (always NUL-terminated). */
+int emmy_last_error(char* buf, size_t n);
+
+/* Opens the driver, retains device `device`'s primary context and makes it current.
+ * Replaces cuInit/cuDeviceGet/cuCtxCreate in tools/localrun.py:33-46. */
+int emmy_init(int device);
+
+/* cuDeviceGetAttribute for the initialised device. */
+int emmy_device_attribute(int attr, int* value);
+
+/* Loads a module from NUL-terminated PTX (JIT-compiled by the driver for this GPU).  On failure
+ * the JIT error log is copied into log (if non-null).  Replaces cuModuleLoadData(Ex)
+ * (tools/localrun.py:92, tools/oracle.py:131). */
+int emmy_module_load_ptx(const char* ptx, void** module, char* log, size_t log_size);
+
+/* Loads a module from a cubin image (ptxas output). */
+int emmy_module_load_image(const void* image, void** module);
+
+int emmy_module_unload(void* module);
+
+/* cuModuleGetFunction (tools/localrun.py:94). */
+int emmy_get_function(void* module, const char* entry, void** function);
+
+/* CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, needed above 48 KiB (tools/localrun.py:96-98). */
+int emmy_set_max_dyn_smem(void* function, int bytes);
+
+/* cuFuncGetAttribute (registers, local memory, max threads, ...). */
+int emmy_func_attribute(void* function, int attr, int* value);
+
+/* cuLaunchKernelEx.  args[i] points at the value of parameter i (nargs of them); cluster may be
+ * null or {1,1,1} for no cluster; stream 0 is the legacy default stream.  Replaces
+ * cuLaunchKernel (tools/localrun.py:101-103). */
+int emmy_launch(void* function, const uint32_t grid[3], const uint32_t block[3],
+                const uint32_t cluster[3], uint32_t dyn_smem, void* stream,
+                void** args, uint32_t nargs);
+
+/* Launch with every parameter a 64-bit value (the emitted kernels' ABI: .param .u64 p_<arg> in
+ * arg_order, tools/localrun.py:175-184).  Each pointer must be a multiple of align[i] bytes
+ * (align may be null); a misaligned pointer is refused with EMMY_ERR_BAD_ARG before launch. */
+int emmy_launch_u64(void* function, const uint32_t grid[3], const uint32_t block[3],
+                    uint32_t dyn_smem, void* stream, const uint64_t* params,
+                    const uint32_t* align, uint32_t nparams);
+
+/* cuTensorMapEncodeTiled into a 128-byte, 64-byte-aligned buffer.  dtype is a
+ * CUtensorMapDataType, strides are the rank-1 byte strides of dims 1..rank-1. */
+int emmy_tmap_encode_tiled(void* tmap, int dtype, uint32_t rank, uint64_t global_address,
+                           const uint64_t* dims, const uint64_t* strides_bytes,
+                           const uint32_t* box, const uint32_t* elem_strides,
+                           int interleave, int swizzle, int l2_promotion, int oob_fill);
+
+/* Events and synchronisation (tools/bench.py:66-83). */
+int emmy_event_create(void** event);
+int emmy_event_destroy(void* event);
+int emmy_event_record(void* event, void* stream);
+int emmy_event_synchronize(void* event);
+int emmy_event_elapsed_ms(void* start, void* stop, float* ms);
+int emmy_stream_synchronize(void* stream);
+int emmy_ctx_synchronize(void);
+
+/* Memory (caller-owned device pointers). */
+int emmy_mem_alloc(uint64_t* dptr, size_t bytes);
+int emmy_mem_free(uint64_t dptr);
+int emmy_memset_d32_async(uint64_t dptr, uint32_t value, size_t count, void* stream);
+int emmy_memcpy_htod_async(uint64_t dst, const void* src, size_t bytes, void* stream);
+int emmy_memcpy_dtoh_async(void* dst, uint64_t src, size_t bytes, void* stream);
+
+/* NCCL: one communicator per process (one process per GPU).  The 128-byte unique id made by
+ * rank 0 is shared with the other ranks by the caller.  dtype 0 = float32, 1 = int32. */
+int emmy_nccl_available(void);
+int emmy_nccl_get_unique_id(char uid[128]);
+int emmy_nccl_init(int rank, int nranks, const char uid[128]);
+int emmy_allreduce_sum(uint64_t buf, size_t count, int dtype, void* stream);
+int emmy_nccl_destroy(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EMMY_LAUNCH_H */

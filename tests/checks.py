@@ -1,0 +1,53 @@
+"""Tolerance policy shared by the parity tests (the bars the benchmark configurations state).
+
+* integer outputs: bit-exact;
+* f32 fused / softmax / reduction outputs: relative 1e-5 (elementwise, with an absolute floor of
+  1e-5 of the tensor's largest magnitude for entries near zero);
+* f32 matmul / attention outputs: relative 1e-4 of max(|ref|, rms(ref)) — a K-term dot product's
+  rounding error scales with the operands' norms, so entries that cancel to near zero are held to
+  the tensor's typical magnitude;
+* bf16 outputs: within one bf16 unit in the last place of the reference value (2**-7 relative)
+  plus 1e-6 absolute — bf16 keeps 8 significant bits, so two correct f32 computations that differ
+  in the last f32 bits can round to neighbouring bf16 values.
+"""
+from __future__ import annotations
+
+import torch
+
+BF16_REL = 2.0 ** -7
+
+
+def rtol_for(problem) -> float:
+    return 1e-4 if problem.family in ("bmm", "attention") else 1e-5
+
+
+def compare(got: torch.Tensor, ref: torch.Tensor, dtype: str, rtol: float, what: str = "") -> dict:
+    g = got.detach().cpu()
+    r = ref.detach().cpu()
+    assert g.shape == r.shape, f"{what}: shape {tuple(g.shape)} vs {tuple(r.shape)}"
+    if dtype in ("i32", "i64", "u32"):
+        eq = torch.equal(g.long(), r.long())
+        assert eq, f"{what}: integer result differs: {g.reshape(-1)[:4].tolist()} vs {r.reshape(-1)[:4].tolist()}"
+        return {"max_abs": 0.0}
+    g = g.double()
+    r = r.double()
+    assert torch.isfinite(g).all() == torch.isfinite(r).all() or bool((torch.isfinite(g) == torch.isfinite(r)).all()), \
+        f"{what}: non-finite pattern differs"
+    fin = torch.isfinite(r)
+    err = (g - r).abs()
+    err = torch.where(fin, err, torch.zeros_like(err))
+    scale = r[fin].abs().max().item() if fin.any() else 0.0
+    if dtype in ("bf16", "f16"):
+        rel = BF16_REL if dtype == "bf16" else 2.0 ** -10
+        bound = rel * r.abs() + 1e-6
+    elif rtol >= 1e-4:
+        rms = r[fin].pow(2).mean().sqrt().item() if fin.any() else 0.0
+        bound = rtol * torch.clamp(r.abs(), min=rms) + 1e-30
+    else:
+        bound = rtol * r.abs() + rtol * 1e-5 * scale + 1e-30
+    bad = err > bound
+    n_bad = int(bad.sum().item())
+    worst = int(torch.argmax((err / bound).reshape(-1)).item())
+    assert n_bad == 0, (f"{what}: {n_bad}/{g.numel()} outside tolerance; worst at {worst}: "
+                        f"got {g.reshape(-1)[worst].item()!r} want {r.reshape(-1)[worst].item()!r}")
+    return {"max_abs": float(err.max().item()) if err.numel() else 0.0, "scale": scale}

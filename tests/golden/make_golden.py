@@ -1,0 +1,85 @@
+"""Regenerate the golden fixtures under tests/golden (run where the reference checkout exists).
+
+    python tests/golden/make_golden.py [--reference PATH]
+
+For every small configuration in ``emmy_ptx_b200.irgen.SMALL`` it writes
+
+* ``ref_ptx/<key>.ptx`` — the PTX the *reference* emitter (``compile.py`` of
+  fanjialin8-create/emmy-ptx, run unmodified through ``emmy_shim``'s ``Graph.from_dict``) writes
+  for that IR.  On a GPU it is run on the same seeded inputs as this backend and the oracle, so
+  it pins the oracle to the reference's own behaviour.
+* ``vectors/<key>.npz`` — the float64 source-expression result (``oracle/torch_ref.py``) on the
+  seeded inputs, stored as float64, and an input checksum.
+* ``manifest.json`` — a hash of each IR, so a fixture made from a different IR is detected.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+def ir_hash(graph: dict, meta: dict) -> str:
+    blob = json.dumps({"graph": graph, "meta": meta}, sort_keys=True).encode()
+    return hashlib.sha256(blob).hexdigest()[:16]
+
+
+def input_digest(tensors: dict) -> str:
+    from emmy_ptx_b200.data import to_numpy_storage
+    h = hashlib.sha256()
+    for name in sorted(tensors):
+        h.update(name.encode())
+        h.update(to_numpy_storage(tensors[name]).tobytes())
+    return h.hexdigest()[:16]
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("EMMY_REFERENCE", "/root/reference"))
+    args = ap.parse_args()
+    import numpy as np
+    from emmy_ptx_b200 import irgen, data
+    from oracle import torch_ref
+
+    compile_py = Path(args.reference) / "compile.py"
+    if not compile_py.exists():
+        print(f"reference compile.py not found at {compile_py}", file=sys.stderr)
+        return 2
+    (HERE / "ref_ptx").mkdir(exist_ok=True)
+    (HERE / "vectors").mkdir(exist_ok=True)
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE / "emmy_shim"), str(ROOT)]))
+    manifest = {}
+    for key, mk in irgen.SMALL.items():
+        p = mk()
+        meta = p.meta()
+        with tempfile.TemporaryDirectory() as td:
+            ir = Path(td) / f"{p.entry}.ir.json"
+            ir.write_text(json.dumps(p.graph))
+            (Path(td) / "meta.json").write_text(json.dumps(meta))
+            r = subprocess.run([sys.executable, str(compile_py), str(ir)], capture_output=True, text=True, env=env)
+        if r.returncode != 0:
+            print(f"{key}: reference emitter failed:\n{r.stderr}", file=sys.stderr)
+            return 1
+        (HERE / "ref_ptx" / f"{key}.ptx").write_text(r.stdout)
+        t = data.make_inputs(p)
+        ref = torch_ref.reference(p, t)
+        np.savez_compressed(HERE / "vectors" / f"{key}.npz",
+                            **{k: v.double().numpy() for k, v in ref.items()})
+        manifest[key] = {"ir": ir_hash(p.graph, meta), "inputs": input_digest(t), "entry": p.entry,
+                         "ref_ptx_lines": r.stdout.count("\n")}
+        print(f"{key}: {p.name} ref PTX {r.stdout.count(chr(10))} lines")
+    (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,38 @@
+"""The C-ABI library loads without a GPU and exports every function include/*.h declares."""
+import ctypes
+import re
+from pathlib import Path
+
+from emmy_ptx_b200 import launcher
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared() -> set[str]:
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(re.findall(r"^\s*int\s+(emmy_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = launcher.load_library()
+    declared = _declared()
+    assert declared, "no declarations found"
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_the_header():
+    assert _declared() <= set(launcher.SIGNATURES) | {"emmy_launch_u64"}
+
+
+def test_calls_without_a_driver_fail_cleanly():
+    lib = launcher.load_library()
+    assert lib.emmy_version() == 1
+    # no emmy_init: every device call reports "not initialised" (or no driver) instead of crashing
+    rc = lib.emmy_ctx_synchronize()
+    assert rc != 0
+    assert launcher.last_error()
