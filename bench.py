@@ -45,6 +45,26 @@ CONFIGS = {
     "c5": ("causal attention bf16 [8,32,4096,128]", "tensor TFLOP/s", "TFLOP/s"),
 }
 
+def _small_for_profile():
+    from emmy_ptx_b200 import irgen
+    return {
+        "c1": lambda: irgen.softmax_ir(4096, 1024),
+        "c2": lambda: irgen.sum_ir(1 << 26, "f32"),
+        "c2i": lambda: irgen.sum_ir(1 << 26, "i32"),
+        "c3": lambda: irgen.fused_ir(4096, 8192),
+        "c4": lambda: irgen.bmm_ir(2, 4096, 4096, 4096),
+        "c5": lambda: irgen.attention_ir(1, 8, 4096, 128),
+    }
+
+
+class _Lazy(dict):
+    def __missing__(self, k):
+        self.update(_small_for_profile())
+        return dict.__getitem__(self, k)
+
+
+SMALL_FOR_PROFILE = _Lazy()
+
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
 # each kernel; see profiles/.  None until a capture exists.
 TRAFFIC = {}
@@ -259,6 +279,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--size", default="full", choices=["full", "small"],
+                    help="small: a reduced instance of the same kernel (still larger than L2) for ncu captures")
     return ap.parse_args()
 
 
@@ -318,7 +340,7 @@ def main() -> int:
     from emmy_ptx_b200.runtime import Executable
     dist = init_dist(world, local)
     key = args.config
-    p = irgen.FULL[key]()
+    p = (SMALL_FOR_PROFILE[key] if args.size == "small" else irgen.FULL[key])()
     units, kind = work_units(p)
     desc, metric, unit = CONFIGS[key]
     scale = 1e9 if unit == "GB/s" else 1e12

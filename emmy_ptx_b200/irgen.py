@@ -539,6 +539,7 @@ SMALL = {
     "c2i": lambda: sum_ir(1 << 16, "i32", blocks=8, threads=256),
     "c3": lambda: fused_ir(64, 512),
     "c4": lambda: bmm_ir(2, 128, 128, 96),
+    "c4tc": lambda: bmm_ir(2, 256, 512, 256),
     "c5": lambda: attention_ir(1, 2, 64, 128),
     "c5nc": lambda: attention_ir(1, 2, 32, 64, causal=False),
 }

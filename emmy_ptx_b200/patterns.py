@@ -1,5 +1,182 @@
-"""Pattern lowerings for dense contractions (filled in by the tcgen05 kernels)."""
+"""Tensor-core lowering of dense-contraction Accum loop nests.
+
+The IR schedules a batched matmul for CUDA cores (cp.async stripes into shared memory, a
+register micro-tile of ``Accum(add, multiply(a, b))``).  When a kernel provably computes
+
+    C[b, i, j] = sum_k X[b, i, k] * Y[b, k, j]      (X, Y bf16, C f32)
+
+it is emitted as the tcgen05/TMA kernel of :mod:`.kernels.tc_gemm` instead.  The match is
+structural and fails closed — anything not recognised exactly is left to the CUDA-core path:
+
+* exactly two inputs and one output; shapes [B,M,K] x [B,K,N] -> [B,M,N]; dtypes bf16/bf16/f32;
+* every shared buffer is filled by CpAsyncCopy from exactly one input, one buffer per input;
+* inside the K loop, the copy from X indexes X's last axis with the loop counter and Y's middle
+  axis with it (and the other axes without it) — the contraction axis is K on both sides;
+* every Accum is ``add`` of a product of one value loaded from X's buffer and one from Y's,
+  seeded with 0; every Write goes to the output and writes only accumulators; nothing else is
+  written to global memory;
+* the tile sizes divide the shapes (M % 128, N % 256, K % 64).
+"""
+from __future__ import annotations
+
+import os
+
+from .ir import dt_name, walk
+
+
+def _names_in(e, out: set) -> set:
+    """Every variable name an index expression mentions."""
+    if e is None:
+        return out
+    if isinstance(e, str):
+        out.add(e)
+        return out
+    if isinstance(e, (list, tuple)):
+        for x in e:
+            _names_in(x, out)
+        return out
+    cls = type(e).__name__
+    if cls == "Var":
+        out.add(e.name)
+    for attr in ("left", "right", "cond", "if_true", "if_false", "expr"):
+        v = getattr(e, attr, None)
+        if v is not None and not isinstance(v, (int, float)):
+            _names_in(v, out)
+    for attr in ("args", "index"):
+        for v in getattr(e, attr, None) or ():
+            _names_in(v, out)
+    return out
+
+
+def _closure(names: set, deps: dict) -> set:
+    out = set()
+    stack = list(names)
+    while stack:
+        n = stack.pop()
+        if n in out:
+            continue
+        out.add(n)
+        stack.extend(deps.get(n, ()))
+    return out
+
+
+def match_bmm(graph, node):
+    """(X, Y, C, batch, M, N, K) when the kernel is a batched bf16 matmul, else None."""
+    op = node.op
+    vals = graph.values()
+    if len(node.outputs) != 1 or len(node.inputs) != 2:
+        return None
+    C = node.outputs[0]
+    ins = [vals.get(n) for n in node.inputs]
+    if any(v is None for v in ins):
+        return None
+    if dt_name(C.dtype) != "f32" or len(C.shape) != 3:
+        return None
+    if any(dt_name(v.dtype) != "bf16" or len(v.shape) != 3 for v in ins):
+        return None
+    bt, m, n = C.shape
+    X = next((v for v in ins if v.shape[0] == bt and v.shape[1] == m), None)
+    Y = next((v for v in ins if v is not X and v.shape[0] == bt and v.shape[2] == n), None)
+    if X is None or Y is None or X.shape[2] != Y.shape[1]:
+        return None
+    k = X.shape[2]
+
+    stmts = []
+    walk(op.body, stmts.append)
+    deps: dict[str, set] = {}
+    for st in stmts:
+        cls = type(st).__name__
+        if cls == "Let":
+            deps[st.name] = _names_in(st.value, set())
+        elif cls == "Assign":
+            deps[st.name] = _names_in(list(st.args), set())
+    # shared buffers and their single global source
+    src_of: dict[str, set] = {}
+    for st in stmts:
+        if type(st).__name__ == "CpAsyncCopy":
+            src_of.setdefault(st.smem, set()).add(st.src)
+    if any(len(v) != 1 for v in src_of.values()):
+        return None
+    feeds = {next(iter(v)): s for s, v in src_of.items()}
+    if set(feeds) != {X.name, Y.name} or len(src_of) != 2:
+        return None
+    sX, sY = feeds[X.name], feeds[Y.name]
+    # the K loop: the loop whose body copies stripes; its counter must index the contraction axis
+    kloops = []
+    walk(op.body, lambda st: kloops.append(st) if type(st).__name__ in ("StridedLoop", "Loop") and any(
+        type(s).__name__ == "CpAsyncCopy" for s in _flat(st.body)) else None)
+    if len(kloops) != 1:
+        return None
+    kname = kloops[0].axis.name
+    for st in _flat(kloops[0].body):
+        if type(st).__name__ != "CpAsyncCopy":
+            continue
+        idx = list(st.src_index)
+        if len(idx) != 3:
+            return None
+        dep = [kname in _closure(_names_in(x, set()), deps) for x in idx]
+        if st.src == X.name and dep != [False, False, True]:
+            return None
+        if st.src == Y.name and dep != [False, True, False]:
+            return None
+    # loads from the shared buffers, products, accumulators
+    loaded = {}
+    for st in stmts:
+        if type(st).__name__ == "Load" and st.input in (sX, sY):
+            for nm in st.names:
+                loaded[nm] = st.input
+    products = {}
+    for st in stmts:
+        if type(st).__name__ == "Assign" and (getattr(st.op, "name", None) or str(st.op)) == "multiply":
+            args = list(st.args)
+            if len(args) == 2 and all(isinstance(x, str) for x in args):
+                srcs = {loaded.get(args[0]), loaded.get(args[1])}
+                if srcs == {sX, sY}:
+                    products[st.name] = True
+    accs = set()
+    for st in stmts:
+        cls = type(st).__name__
+        if cls == "Accum":
+            if (getattr(st.op, "name", None) or str(st.op)) != "add" or getattr(st, "base", None) not in (None, st.name):
+                return None
+            if not isinstance(st.value, str) or st.value not in products:
+                return None
+            accs.add(st.name)
+    if not accs:
+        return None
+    for st in stmts:
+        cls = type(st).__name__
+        if cls == "Init" and st.name in accs and float(st.identity) != 0.0:
+            return None
+        if cls == "Write":
+            if st.output in src_of:
+                continue
+            if st.output != C.name or getattr(st, "atomic", False):
+                return None
+            if not all(v in accs for v in st.values):
+                return None
+        if cls == "ZeroPrologue":
+            return None
+    return X, Y, C, bt, m, n, k
+
+
+def _flat(body):
+    out = []
+    walk(body, out.append)
+    return out
 
 
 def try_lower(graph, node, kmeta, prefix, options):
+    """A tensor-core build record for this kernel, or None to keep the CUDA-core lowering."""
+    if options.get("patterns") is False or os.environ.get("EMMY_B200_PATTERNS", "1") == "0":
+        return None
+    hit = match_bmm(graph, node)
+    if hit is not None:
+        X, Y, C, bt, m, n, k = hit
+        from .kernels import tc_gemm
+        if m % tc_gemm.BM or n % tc_gemm.BN or k % tc_gemm.BK:
+            return None
+        b = tc_gemm.gemm_entry(node.op.name, bt, m, n, k, sms=int(options.get("sms", 148)),
+                               names=(X.name, Y.name, C.name), prefix=prefix)
+        return b
     return None

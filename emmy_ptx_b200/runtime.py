@@ -17,9 +17,12 @@ _TMAP_DTYPE = {"bf16": 10, "f16": 6, "f32": 7, "u8": 0}   # CUtensorMapDataType
 _SWIZZLE = {"none": 0, "32B": 1, "64B": 2, "128B": 3}
 
 
-class _TmapBlob(ctypes.Structure):
-    _pack_ = 64
-    _fields_ = [("bytes", ctypes.c_uint8 * 128)]
+class _TmapBlob:
+    """A 128-byte CUtensorMap in a host buffer, at a 64-byte-aligned address."""
+
+    def __init__(self):
+        self.buf = ctypes.create_string_buffer(128 + 64)
+        self.addr = (ctypes.addressof(self.buf) + 63) & ~63
 
 
 class Executable:
@@ -40,6 +43,19 @@ class Executable:
                 self.dev.set_max_dyn_smem(fn, rec["dyn_smem"])
             self.funcs.append(fn)
         self._tmap_cache: dict = {}
+        self.err = None
+        if any(spec.get("kind") == "errword" for rec in compiled.kernels for spec in rec.get("extra", [])):
+            self.err = torch.zeros(4, dtype=torch.int32, device=f"cuda:{self.index}")
+
+    def error_code(self) -> int:
+        """The error word a tensor-core kernel writes when one of its bounded waits times out
+        (0 = no error).  Read after synchronising."""
+        return 0 if self.err is None else int(self.err[0].item())
+
+    def check(self) -> None:
+        code = self.error_code()
+        if code:
+            raise RuntimeError(f"kernel reported error code {code} (a pipeline wait timed out)")
 
     @property
     def records(self) -> list[dict]:
@@ -57,7 +73,7 @@ class Executable:
         blob = _TmapBlob()
         dims = spec["dims"]
         strides = spec["strides"]
-        self.dev.tmap_encode_tiled(ctypes.byref(blob), _TMAP_DTYPE[spec["dtype"]], t.data_ptr(), dims, strides,
+        self.dev.tmap_encode_tiled(ctypes.c_void_p(blob.addr), _TMAP_DTYPE[spec["dtype"]], t.data_ptr(), dims, strides,
                                    spec["box"], swizzle=_SWIZZLE[spec.get("swizzle", "128B")],
                                    l2promo=spec.get("l2promo", 2))
         self._tmap_cache[key] = blob
@@ -85,15 +101,22 @@ class Executable:
             args = []
             keep = []
             for name in rec["params"]:
-                v = ctypes.c_uint64(tensors[name].data_ptr())
+                ptr = tensors[name].data_ptr()
+                al = int(rec.get("align", {}).get(name, 1))
+                if al > 1 and ptr % al:
+                    raise ValueError(f"{name!r} must be {al}-byte aligned for kernel {rec['entry']!r}")
+                v = ctypes.c_uint64(ptr)
                 keep.append(v)
                 args.append(ctypes.cast(ctypes.byref(v), ctypes.c_void_p).value)
             for spec in rec.get("tmaps", []):
                 blob = self._tmap(spec, tensors[spec["tensor"]])
                 keep.append(blob)
-                args.append(ctypes.cast(ctypes.byref(blob), ctypes.c_void_p).value)
+                args.append(blob.addr)
             for spec in rec.get("extra", []):
-                v = ctypes.c_uint64(int(spec["value"]) if "value" in spec else tensors[spec["name"]].data_ptr())
+                if spec.get("kind") == "errword":
+                    v = ctypes.c_uint64(self.err.data_ptr())
+                else:
+                    v = ctypes.c_uint64(int(spec["value"]) if "value" in spec else tensors[spec["name"]].data_ptr())
                 keep.append(v)
                 args.append(ctypes.cast(ctypes.byref(v), ctypes.c_void_p).value)
             self.dev.launch(fn, g, rec["block"], rec.get("dyn_smem", 0), stream, args,

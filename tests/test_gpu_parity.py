@@ -109,3 +109,31 @@ def test_full_fused_bf16():
     a, b, c, d = (t[k].cuda() for k in "abcd")
     want = (torch.relu(a.double() * b.double() + c.double()) * torch.exp(d.double())).cpu()
     compare(got["y"], want, "bf16", 1e-5, "c3 full")
+
+
+def test_tensor_core_gemm_many_tiles_per_cta():
+    """Two CTAs walk all eight tiles: accumulator ping-pong and ring wrap-around are exercised."""
+    p = irgen.SMALL["c4tc"]()
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t, sms=2)
+    assert ex.records[0]["kind"] == "tcgen05_gemm" and ex.records[0]["grid"] == [2, 1, 1]
+    assert ex.error_code() == 0
+    compare(got["C"], want["C"], "f32", 1e-4, "c4tc sms=2")
+
+
+def test_full_bmm_tensor_core_sampled():
+    p = irgen.FULL["c4"]()
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    A = (torch.randn(p.spec("A").shape, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    B = (torch.randn(p.spec("B").shape, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    C = torch.empty(p.spec("C").shape, dtype=torch.float32, device="cuda")
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    assert mod.kernels[0]["kind"] == "tcgen05_gemm"
+    ex = Executable(mod)
+    ex({"A": A, "B": B, "C": C})
+    torch.cuda.synchronize()
+    assert ex.error_code() == 0
+    for b in (0, 7, 15):
+        want = torch.matmul(A[b].double(), B[b].double())
+        compare(C[b], want, "f32", 1e-4, f"c4 full batch {b}")

@@ -1,0 +1,70 @@
+"""The dense-contraction matcher: what it accepts and what it must refuse (CPU only)."""
+import copy
+
+from emmy_ptx_b200 import irgen
+from emmy_ptx_b200.compiler import compile_graph
+from emmy_ptx_b200.ir import Graph
+from emmy_ptx_b200.patterns import match_bmm
+
+
+def _kernel(p):
+    g = Graph.from_dict(p.graph)
+    return g, g.kernels()[0]
+
+
+def test_bmm_ir_is_recognised_as_a_contraction():
+    for p in (irgen.FULL["c4"](), irgen.SMALL["c4tc"](), irgen.SMALL["c4"]()):
+        g, k = _kernel(p)
+        hit = match_bmm(g, k)
+        assert hit is not None
+        X, Y, C, bt, m, n, kk = hit
+        assert (X.name, Y.name, C.name) == ("A", "B", "C")
+        assert (bt, m, n, kk) == (p.params["batch"], p.params["m"], p.params["n"], p.params["k"])
+
+
+def test_tile_multiples_select_the_tensor_core_kernel():
+    p = irgen.FULL["c4"]()
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    rec = mod.kernels[0]
+    assert rec["kind"] == "tcgen05_gemm" and rec["entry"] == "bmm_bf16"
+    assert rec["params"] == ["A", "B", "C"] and rec["block"] == [192, 1, 1]
+    for ins in ("tcgen05.mma.cta_group::1.kind::f16", "tcgen05.alloc", "tcgen05.dealloc",
+                "cp.async.bulk.tensor.3d", "tcgen05.ld.sync.aligned.32x32b.x32", "mbarrier.try_wait.parity"):
+        assert ins in mod.ptx
+    assert "multicast" not in mod.ptx
+    small = irgen.SMALL["c4"]()          # N = 128 is not a multiple of the 256-wide tile
+    assert compile_graph(Graph.from_dict(small.graph), small.meta()).kernels[0]["kind"] == "generic"
+
+
+def test_swapped_contraction_axis_is_refused():
+    p = irgen.SMALL["c4tc"]()
+    d = copy.deepcopy(p.graph)
+    body = d["nodes"]["bmm_bf16"]["op_fields"]["body"][2]["body"]
+    kloop = next(st for st in body if st["kind"] == "StridedLoop")
+    cond = next(st for st in kloop["body"] if st["kind"] == "Cond")
+    copy_a = next(st for st in cond["body"] if st["src"] == "A")
+    copy_a["src_index"][1], copy_a["src_index"][2] = copy_a["src_index"][2], copy_a["src_index"][1]
+    g = Graph.from_dict(d)
+    assert match_bmm(g, g.kernels()[0]) is None
+
+
+def test_non_product_accumulation_is_refused():
+    p = irgen.SMALL["c4tc"]()
+    d = copy.deepcopy(p.graph)
+
+    def edit(stmts):
+        for st in stmts:
+            if st.get("kind") == "Assign" and st.get("name") == "p00":
+                st["op"]["name"] = "add"
+            for key in ("body", "else_body"):
+                if isinstance(st.get(key), list):
+                    edit(st[key])
+    edit(d["nodes"]["bmm_bf16"]["op_fields"]["body"])
+    g = Graph.from_dict(d)
+    assert match_bmm(g, g.kernels()[0]) is None
+
+
+def test_patterns_can_be_disabled():
+    p = irgen.FULL["c4"]()
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"patterns": False})
+    assert mod.kernels[0]["kind"] == "generic"
