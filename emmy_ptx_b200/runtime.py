@@ -13,7 +13,7 @@ import ctypes
 from .compiler import CompiledModule, compile_ir
 from .launcher import Device
 
-_TMAP_DTYPE = {"bf16": 10, "f16": 6, "f32": 7, "u8": 0}   # CUtensorMapDataType
+_TMAP_DTYPE = {"u8": 0, "f16": 6, "f32": 7, "bf16": 9}   # CUtensorMapDataType (cuda.h)
 _SWIZZLE = {"none": 0, "32B": 1, "64B": 2, "128B": 3}
 
 
