@@ -967,7 +967,7 @@ class KernelEmitter:
         self.b.pop_scope()
         if getattr(st, "else_body", None):
             end = self.b.label("_endif")
-            self.b.emit(f"bra.uni {end};")
+            self.b.emit(f"bra {end};")
             self.b.place(other)
             self.b.push_scope()
             self.stmts(st.else_body)
@@ -1036,7 +1036,7 @@ class KernelEmitter:
         b.emit(f"mad.wide.u32 {a}, {r['i']}, 4, {self.preg[dst]};")
         b.emit(f"st.global.u32 [{a}], 0;")
         b.emit(f"add.u32 {r['i']}, {r['i']}, {r['stride']};")
-        b.emit(f"bra.uni {top};")
+        b.emit(f"bra {top};")
         b.place(end)
 
     # ---- loops (compile.py:1525-1618) ---------------------------------------------------------

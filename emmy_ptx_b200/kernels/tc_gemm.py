@@ -14,6 +14,8 @@ config 4).  The kernel is written here as PTX text, instruction by instruction:
   read the stage);
 * two 128x256 f32 accumulators in TMEM (all 512 columns), so the epilogue of one tile overlaps
   the MMAs of the next (``tmem_full`` / ``tmem_empty`` barriers);
+* branches are plain ``bra``: several depend on the lane (one elected thread per role), and a
+  ``bra.uni`` there would promise a warp-uniform branch that is not;
 * every mbarrier wait is bounded: on time-out the thread writes a code to the error word and
   leaves its loop; the producer then waits (bounded) for its own loads in flight, all threads meet
   at the final barrier and warp 1 frees TMEM, so the kernel always returns.
@@ -105,12 +107,12 @@ def _wait(a: Asm, bar: str, parity: str, err: str, code: int, bail: str) -> None
     a(f"mov.u32 {cnt}, 0;")
     a.label(top)
     a(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity}, {WAIT_HINT_NS};")
-    a(f"@{p} bra.uni {done};")
+    a(f"@{p} bra {done};")
     a(f"add.u32 {cnt}, {cnt}, 1;")
     a(f"setp.lt.u32 {q}, {cnt}, {WAIT_LIMIT};")
-    a(f"@{q} bra.uni {top};")
+    a(f"@{q} bra {top};")
     a(f"st.global.u32 [{err}], {code};")
-    a(f"bra.uni {bail};")
+    a(f"bra {bail};")
     a.label(done)
 
 
@@ -126,12 +128,12 @@ def _wait_warp(a: Asm, bar: str, parity: str, err: str, code: int, bail: str) ->
     a.label(top)
     a(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity}, {WAIT_HINT_NS};")
     a(f"vote.sync.all.pred {pa}, {p}, -1;")
-    a(f"@{pa} bra.uni {done};")
+    a(f"@{pa} bra {done};")
     a(f"add.u32 {cnt}, {cnt}, 1;")
     a(f"setp.lt.u32 {q}, {cnt}, {WAIT_LIMIT};")
-    a(f"@{q} bra.uni {top};")
+    a(f"@{q} bra {top};")
     a(f"st.global.u32 [{err}], {code};")
-    a(f"bra.uni {bail};")
+    a(f"bra {bail};")
     a.label(done)
 
 
@@ -182,7 +184,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     p0 = a.r("p")
     a(f"setp.eq.u32 {p0}, {tid}, 0;")
     l_init = a.L("noinit")
-    a(f"@!{p0} bra.uni {l_init};")
+    a(f"@!{p0} bra {l_init};")
     for s in range(STAGES):
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{FULL + 8 * s}], 1;")
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{EMPTY + 8 * s}], 1;")
@@ -195,7 +197,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     pw1 = a.r("p")
     a(f"setp.eq.u32 {pw1}, {warp}, 1;")
     l_noalloc = a.L("noalloc")
-    a(f"@!{pw1} bra.uni {l_noalloc};")
+    a(f"@!{pw1} bra {l_noalloc};")
     a(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{bars}+{SLOT}], {TMEM_COLS};")
     a("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
     a("tcgen05.fence::before_thread_sync;")
@@ -209,9 +211,9 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     l_prod, l_mma, l_epi = a.L("prod"), a.L("mma"), a.L("epi")
     pw0 = a.r("p")
     a(f"setp.eq.u32 {pw0}, {warp}, 0;")
-    a(f"@{pw0} bra.uni {l_prod};")
-    a(f"@{pw1} bra.uni {l_mma};")
-    a(f"bra.uni {l_epi};")
+    a(f"@{pw0} bra {l_prod};")
+    a(f"@{pw1} bra {l_mma};")
+    a(f"bra {l_epi};")
 
     def tile_coords(t):
         """(b, m0, n0) registers for tile index t (n fastest, then m, then batch)."""
@@ -228,7 +230,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a.label(l_prod)
     pl0 = a.r("p")
     a(f"setp.ne.u32 {pl0}, {lane}, 0;")
-    a(f"@{pl0} bra.uni {l_end};")
+    a(f"@{pl0} bra {l_end};")
     stage, phase, t, kb = a.r(), a.r(), a.r(), a.r()
     armed = [a.r() for _ in range(STAGES)]          # parity each stage's full barrier must reach
     for r_ in armed:
@@ -240,7 +242,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a.label(l_pt)
     pt = a.r("p")
     a(f"setp.ge.u32 {pt}, {t}, {tiles};")
-    a(f"@{pt} bra.uni {l_pdone};")
+    a(f"@{pt} bra {l_pdone};")
     bb, mm, nn = tile_coords(t)
     a(f"mov.u32 {kb}, 0;")
     l_pk = a.L("pk")
@@ -277,9 +279,9 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a(f"add.u32 {kb}, {kb}, 1;")
     pk = a.r("p")
     a(f"setp.lt.u32 {pk}, {kb}, {nk};")
-    a(f"@{pk} bra.uni {l_pk};")
+    a(f"@{pk} bra {l_pk};")
     a(f"add.u32 {t}, {t}, {ncta};")
-    a(f"bra.uni {l_pt};")
+    a(f"bra {l_pt};")
     a.label(l_pbail)
     a.label(l_pdone)
     # drain: every load this thread issued has landed before the CTA can finish
@@ -287,18 +289,18 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
         skip = a.L("dskip")
         pn = a.r("p")
         a(f"setp.eq.u32 {pn}, {armed[s]}, 2;")
-        a(f"@{pn} bra.uni {skip};")
+        a(f"@{pn} bra {skip};")
         fbs = a.r()
         a(f"add.u32 {fbs}, {bars}, {FULL + 8 * s};")
         _wait(a, fbs, armed[s], err, ERR_DRAIN, skip)
         a.label(skip)
-    a(f"bra.uni {l_end};")
+    a(f"bra {l_end};")
 
     # ---------------- MMA issuer: warp 1, lane 0 -----------------------------------------
     a.label(l_mma)
     pl1 = a.r("p")
     a(f"setp.ne.u32 {pl1}, {lane}, 0;")
-    a(f"@{pl1} bra.uni {l_end};")
+    a(f"@{pl1} bra {l_end};")
     mstage, mphase, acc, aphase, mt_, mkb = a.r(), a.r(), a.r(), a.r(), a.r(), a.r()
     a(f"mov.u32 {mstage}, 0;")
     a(f"mov.u32 {mphase}, 0;")
@@ -314,7 +316,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a.label(l_mt)
     pm = a.r("p")
     a(f"setp.ge.u32 {pm}, {mt_}, {tiles};")
-    a(f"@{pm} bra.uni {l_mdone};")
+    a(f"@{pm} bra {l_mdone};")
     teb, tpar, dcol = a.r(), a.r(), a.r()
     a(f"mad.lo.u32 {teb}, {acc}, 8, {bars};")
     a(f"add.u32 {teb}, {teb}, {TEMPTY};")
@@ -362,7 +364,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a(f"add.u32 {mkb}, {mkb}, 1;")
     pk2 = a.r("p")
     a(f"setp.lt.u32 {pk2}, {mkb}, {nk};")
-    a(f"@{pk2} bra.uni {l_mk};")
+    a(f"@{pk2} bra {l_mk};")
     tfb = a.r()
     a(f"mad.lo.u32 {tfb}, {acc}, 8, {bars};")
     a(f"add.u32 {tfb}, {tfb}, {TFULL};")
@@ -372,9 +374,9 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a(f"setp.eq.u32 {pa}, {acc}, 0;")
     a(f"@{pa} xor.b32 {aphase}, {aphase}, 1;")
     a(f"add.u32 {mt_}, {mt_}, {ncta};")
-    a(f"bra.uni {l_mt};")
+    a(f"bra {l_mt};")
     a.label(l_mdone)
-    a(f"bra.uni {l_end};")
+    a(f"bra {l_end};")
 
     # ---------------- epilogue: warps 2..5 -------------------------------------------------
     a.label(l_epi)
@@ -390,7 +392,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a.label(l_et)
     pe = a.r("p")
     a(f"setp.ge.u32 {pe}, {et}, {tiles};")
-    a(f"@{pe} bra.uni {l_edone};")
+    a(f"@{pe} bra {l_edone};")
     ebb, emm, enn = tile_coords(et)
     efb = a.r()
     a(f"mad.lo.u32 {efb}, {eacc}, 8, {bars};")
@@ -430,7 +432,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a(f"setp.eq.u32 {pa2}, {eacc}, 0;")
     a(f"@{pa2} xor.b32 {eph}, {eph}, 1;")
     a(f"add.u32 {et}, {et}, {ncta};")
-    a(f"bra.uni {l_et};")
+    a(f"bra {l_et};")
     a.label(l_edone)
 
     # ---------------- teardown -------------------------------------------------------------
@@ -438,7 +440,7 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a("barrier.sync 0;")
     a("bar.warp.sync -1;")
     l_nodealloc = a.L("nodealloc")
-    a(f"@!{pw1} bra.uni {l_nodealloc};")
+    a(f"@!{pw1} bra {l_nodealloc};")
     a("tcgen05.fence::after_thread_sync;")
     a(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {taddr}, {TMEM_COLS};")
     a.label(l_nodealloc)
