@@ -5,6 +5,7 @@
 // returns a status code; the message for the last failure is kept per thread.
 
 #include "emmy_launch.h"
+#include "internal.h"
 
 #include <cuda.h>
 #include <dlfcn.h>
@@ -171,6 +172,16 @@ int nc(int rc, const char* what) {
 }
 
 }  // namespace
+
+int emmy_internal_fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
 
 extern "C" {
 

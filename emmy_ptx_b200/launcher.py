@@ -49,6 +49,8 @@ SIGNATURES = {
     "emmy_nccl_init": [ctypes.c_int, ctypes.c_int, ctypes.c_char_p],
     "emmy_allreduce_sum": [ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int, vp],
     "emmy_nccl_destroy": [],
+    "emmy_bmm_bf16_noalloc": [vp, vp, vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
+                              ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, vp],
 }
 
 # CUfunction_attribute values used by the runtime
@@ -235,6 +237,15 @@ class Device:
     def allreduce_sum(self, dptr: int, count: int, dtype: str, stream: int) -> None:
         code = {"f32": 0, "i32": 1}[dtype]
         check(self.lib.emmy_allreduce_sum(int(dptr), int(count), code, vp(stream or 0)), "emmy_allreduce_sum")
+
+    def bmm_noalloc(self, fn, tmap_a: int, tmap_b: int, a: int, b: int, c: int, grid: int, block: int,
+                    dyn_smem: int, scratch_bytes: int, stream: int) -> None:
+        """The tensor-core bmm through the entry point that allocates nothing (its scratch is a fixed
+        array inside the library)."""
+        check(self.lib.emmy_bmm_bf16_noalloc(fn, vp(tmap_a), vp(tmap_b), int(a), int(b), int(c), int(grid),
+                                             int(block), int(dyn_smem), int(scratch_bytes), vp(stream or 0)),
+              "emmy_bmm_bf16_noalloc")
+        self.launches += 1
 
     def nccl_destroy(self) -> None:
         check(self.lib.emmy_nccl_destroy(), "emmy_nccl_destroy")

@@ -112,6 +112,22 @@ int emmy_nccl_init(int rank, int nranks, const char uid[128]);
 int emmy_allreduce_sum(uint64_t buf, size_t count, int dtype, void* stream);
 int emmy_nccl_destroy(void);
 
+/* Runs the tensor-core batched matmul (a launch record of kind "tcgen05_gemm": parameters A, B, C, the
+ * two TMA descriptors, then a scratch pointer) without allocating device memory, for callers that cannot
+ * allocate when they launch: a host whose own pool already owns the GPU's memory, or a latency-critical
+ * path where cudaMalloc/cudaFree may synchronise the device.  No counterpart in the reference.
+ *  - function: the kernel, loaded with emmy_module_load_ptx / emmy_get_function; tmap_a / tmap_b: its
+ *    descriptors from emmy_tmap_encode_tiled; a, b, c: device pointers; grid, block, dyn_smem: from the
+ *    launch record; scratch_bytes: the record's scratch need (16 for the status word), at most 256 —
+ *    larger values are refused with EMMY_ERR_BAD_ARG.
+ *  - The scratch is a fixed 256-byte array in this library's device memory, held on every GPU that loads
+ *    the library until the process exits.  The first call on a device looks up its address (with that
+ *    device current); make that first call before any stream capture.
+ *  - Every call uses the same array and clears it first; calls that overlap on the GPU race on it. */
+int emmy_bmm_bf16_noalloc(void* function, const void* tmap_a, const void* tmap_b, uint64_t a, uint64_t b,
+                          uint64_t c, uint32_t grid, uint32_t block, uint32_t dyn_smem,
+                          uint32_t scratch_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
