@@ -166,35 +166,6 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(loaded), "gpus": sorted(busy)}
 
 
-# ---- distributed plumbing -------------------------------------------------------------------------
-
-def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
-
-
-def init_dist(world: int, local: int):
-    import datetime
-    import torch
-    import torch.distributed as dist
-    torch.cuda.set_device(local)
-    if world > 1 and not dist.is_initialized():
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    return dist if world > 1 else None
-
-
-def max_over_ranks(dist, v: float) -> float:
-    if dist is None:
-        return v
-    import torch
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
 # ---- the CPU oracle (baseline and reference arm) --------------------------------------------------
 
 def _oracle_worker(args):
@@ -330,7 +301,8 @@ def reference_arm(args, world, rank):
 
 def main() -> int:
     args = parse()
-    world, rank, local = dist_env()
+    from emmy_ptx_b200 import dist as edist
+    world, rank, local = edist.env()
     if args.impl == "reference":
         return reference_arm(args, world, rank)
     import torch
@@ -338,7 +310,8 @@ def main() -> int:
     from emmy_ptx_b200.compiler import compile_graph
     from emmy_ptx_b200.ir import Graph
     from emmy_ptx_b200.runtime import Executable
-    dist = init_dist(world, local)
+    dist = edist.init(world, local)
+    max_over_ranks = edist.max_over_ranks
     key = args.config
     p = (SMALL_FOR_PROFILE[key] if args.size == "small" else irgen.FULL[key])()
     units, kind = work_units(p)
@@ -374,16 +347,12 @@ def main() -> int:
         sets.append(t)
 
     collective = p.family == "sum" and world > 1
-    if collective:
-        uid = [dev.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        dev.nccl_init(rank, world, uid[0])
+    allreduce = edist.AllReducePartials(dev, dist, rank, world) if collective else None
 
     def step(t):
         ex(t, stream)
         if collective:
-            out = t["out"]
-            dev.allreduce_sum(out.data_ptr(), out.numel(), p.params["dtype"], stream)
+            allreduce(t["out"], p.params["dtype"], stream)
 
     for i in range(max(args.warmup, 3)):
         step(sets[i % rotate])
@@ -410,8 +379,7 @@ def main() -> int:
         ex.launch(0, t, stream, zero=False)
         k1[i].record()
         if collective:
-            out = t["out"]
-            dev.allreduce_sum(out.data_ptr(), out.numel(), p.params["dtype"], stream)
+            allreduce(t["out"], p.params["dtype"], stream)
     e1.record()
     torch.cuda.synchronize()
     if dist:
@@ -433,6 +401,14 @@ def main() -> int:
         want = t["x"].double().sum().item() if p.params["dtype"] == "f32" else int(t["x"].long().sum().item())
         got = t["out"].item()
         check = {"abs_err": abs(got - want), "rel_err": abs(got - want) / max(abs(want), 1e-30)}
+        if collective:
+            # the exchange step too: kernel + ncclAllReduce against the all-reduced float64 shard sums
+            step(t)
+            torch.cuda.synchronize()
+            tot = torch.tensor([float(want)], dtype=torch.float64, device="cuda")
+            dist.all_reduce(tot)
+            g_all = t["out"].item()
+            check["global_rel_err"] = abs(g_all - tot.item()) / max(abs(tot.item()), 1e-30)
     elif p.family == "softmax":
         want = torch.softmax(t["x"].double(), -1)
         check = {"max_rel_err": ((t["y"].double() - want).abs() / want.abs().clamp_min(1e-30)).max().item()}
@@ -501,7 +477,7 @@ def main() -> int:
                          f"through the numpy oracle, one process", "seconds": dt}
 
     if collective:
-        dev.nccl_destroy()
+        allreduce.close()
     if rank == 0:
         line = {
             "metric": f"{desc} {metric}", "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,

@@ -1,0 +1,99 @@
+"""Multi-process host logic on CPU: two gloo ranks, no GPU.
+
+Covers the sharding of units, the unique-id broadcast, the max-over-ranks timing reduction, the
+weak-scaled sum (partials combined by an all-reduce, bit-exact for integers), and failure detection: a
+rank that leaves before the collective makes the others fail within the process-group timeout instead
+of hanging.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from emmy_ptx_b200 import dist as edist
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _setup(rank, world, port, timeout_s=30.0):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    return edist.init(world, rank, backend="gloo", timeout_s=timeout_s)
+
+
+def _worker_basic(rank, world, port, q):
+    d = _setup(rank, world, port)
+    try:
+        uid = edist.share_unique_id(d, rank, lambda: bytes(range(128)))
+        mx = edist.max_over_ranks(d, float(rank + 1) * 1.5)
+        # weak-scaled integer sum: each rank owns a full shard, partials all-reduced
+        g = torch.Generator().manual_seed(100 + rank)
+        x = torch.randint(-1000, 1001, (1 << 16,), generator=g, dtype=torch.int32)
+        part = torch.tensor([int(x.long().sum())], dtype=torch.int64)
+        d.all_reduce(part)
+        q.put((rank, uid == bytes(range(128)), mx, int(part.item())))
+    finally:
+        d.destroy_process_group()
+
+
+def test_two_gloo_ranks_share_uid_max_and_partials():
+    world, port = 2, _port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_basic, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    want = 0
+    for r in range(world):
+        g = torch.Generator().manual_seed(100 + r)
+        want += int(torch.randint(-1000, 1001, (1 << 16,), generator=g, dtype=torch.int32).long().sum())
+    for rank, uid_ok, mx, total in res:
+        assert uid_ok and mx == 3.0 and total == want
+
+
+def _worker_dies(rank, world, port, q):
+    d = _setup(rank, world, port, timeout_s=5.0)
+    if rank == 1:
+        os._exit(0)                      # leaves between steps, before the collective
+    try:
+        edist.max_over_ranks(d, 1.0)
+        q.put("returned")
+    except Exception as exc:             # the process-group timeout ends the collective with an error
+        q.put("error:" + type(exc).__name__)
+
+
+def test_a_rank_that_leaves_fails_the_collective_instead_of_hanging():
+    world, port = 2, _port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_dies, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=120)
+    for p in procs:
+        p.join(60)
+        if p.is_alive():
+            p.kill()
+    assert msg.startswith("error:")
+
+
+@pytest.mark.parametrize("n,world", [(4096, 2), (4096, 8), (16, 3), (7, 4), (256, 8)])
+def test_shards_cover_every_unit_once(n, world):
+    seen = np.zeros(n, dtype=int)
+    for r in range(world):
+        for i in edist.shard(n, world, r):
+            seen[i] += 1
+    assert (seen == 1).all()
