@@ -65,9 +65,15 @@ class _Lazy(dict):
 
 SMALL_FOR_PROFILE = _Lazy()
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
-# each kernel; see profiles/.  None until a capture exists.
-TRAFFIC = {}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
+# kernel on a reduced instance, scaled to the full launch by the units processed (traffic grows in
+# proportion for these streaming / tiled kernels); the captures are summarised under profiles/.
+TRAFFIC = {
+    "c2": (268.443904e6 + 4.902912e6) * 4,       # 2^26 -> 2^28 elements
+    "c2i": (268.443904e6 + 4.902912e6) * 4,      # same kernel shape, i32 elements
+    "c3": (201.394176e6 + 44.741632e6) * 2,      # 4096 -> 8192 rows
+    "c4": (192.727040e6 + 105.907456e6) * 8,     # 2 -> 16 batches
+}
 
 
 def work_units(p) -> tuple[float, str]:
