@@ -541,5 +541,7 @@ SMALL = {
     "c4": lambda: bmm_ir(2, 128, 128, 96),
     "c4tc": lambda: bmm_ir(2, 256, 512, 256),
     "c5": lambda: attention_ir(1, 2, 64, 128),
+    "c5tc": lambda: attention_ir(1, 2, 512, 128),
+    "c5tcnc": lambda: attention_ir(1, 1, 256, 128, causal=False),
     "c5nc": lambda: attention_ir(1, 2, 32, 64, causal=False),
 }

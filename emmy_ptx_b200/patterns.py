@@ -160,6 +160,153 @@ def match_bmm(graph, node):
     return X, Y, C, bt, m, n, k
 
 
+def _is_var(e, name=None) -> bool:
+    return type(e).__name__ == "Var" and (name is None or e.name == name)
+
+
+def _index_vars(index) -> list:
+    """Variable names per coordinate of an index list (None where a coordinate is not a lone Var)."""
+    out = []
+    for e in index:
+        if isinstance(e, str):
+            out.append(e)
+        elif _is_var(e):
+            out.append(e.name)
+        else:
+            out.append(None)
+    return out
+
+
+def match_attention(graph, node):
+    """(Q, K, V, O, batch, heads, seq, dim, causal, scale) when the kernel is the online-softmax
+    attention nest, else None.
+
+    Recognised form (the attention IR): a Tile over (b, h, q, lane); Q loaded at [b, h, q, d0]; one
+    kv loop from 0 to S with step 1 whose body loads K and V at [b, h, kv, d0], reduces the lane
+    products of Q and K with an ``add`` WarpShuffle, multiplies by a float literal (the scale), masks
+    with a Select whose first branch is ``kv > q -> -inf`` (causal) or has no mask, keeps the running
+    max as ``Accum(maximum)`` and the row sum / output as ``Accum(add, base=...)``; after the loop
+    every written value is ``divide(o, l)`` to O at [b, h, q, d0]."""
+    op = node.op
+    vals = graph.values()
+    if len(node.outputs) != 1 or len(node.inputs) != 3:
+        return None
+    O = node.outputs[0]
+    ins = [vals.get(n) for n in node.inputs]
+    if any(v is None or dt_name(v.dtype) != "bf16" or tuple(v.shape) != tuple(O.shape) for v in ins):
+        return None
+    if dt_name(O.dtype) != "bf16" or len(O.shape) != 4:
+        return None
+    bt, hd, seq, dim = O.shape
+    tiles = [st for st in op.body if type(st).__name__ == "Tile"]
+    if len(tiles) != 1 or len(tiles[0].axes) != 4:
+        return None
+    tile = tiles[0]
+    ax = [a.name for a in tile.axes]
+    from .ir import dim_int
+    if [dim_int(a.extent) for a in tile.axes] != [bt, hd, seq, 32] or dim % 32:
+        return None
+    stmts = []
+    walk(op.body, stmts.append)
+    loops = [st for st in stmts if type(st).__name__ in ("StridedLoop", "Loop")]
+    if len(loops) != 1 or type(loops[0]).__name__ != "StridedLoop":
+        return None
+    lp = loops[0]
+    kv = lp.axis.name
+    if lp.start != 0 or lp.step != 1 or (lp.end if lp.end is not None else dim_int(lp.axis.extent)) != seq:
+        return None
+    inner = []
+    walk(lp.body, inner.append)
+    loads_in = {st.input: st for st in inner if type(st).__name__ == "Load"}
+    loads_out = [st for st in stmts if type(st).__name__ == "Load" and st not in inner]
+    if len(loads_in) != 2 or len(loads_out) != 1:
+        return None
+    qload = loads_out[0]
+    Q = vals.get(qload.input)
+    kv_inputs = [n for n in loads_in if n != qload.input]
+    if Q is None or len(kv_inputs) != 2:
+        return None
+    d0 = _index_vars(qload.index)[3]
+    if _index_vars(qload.index)[:3] != ax[:3] or d0 is None:
+        return None
+    for ld in loads_in.values():
+        if _index_vars(ld.index) != [ax[0], ax[1], kv, d0]:
+            return None
+    shuffles = [st for st in inner if type(st).__name__ == "WarpShuffle"]
+    if len(shuffles) != 1 or shuffles[0].length != 32:
+        return None
+    comb = list(shuffles[0].combine_states or ())
+    if len(comb) != 1 or (getattr(comb[0].op, "name", None) or str(comb[0].op)) != "add":
+        return None
+    dot = shuffles[0].state[0]
+    # which loaded input meets Q in the dot product: K; the other one feeds the output Accums: V
+    assign = {st.name: st for st in stmts if type(st).__name__ == "Assign"}
+    qnames = set(qload.names)
+
+    def sources(name, seen=None):
+        seen = set() if seen is None else seen
+        if name in seen:
+            return set()
+        seen.add(name)
+        out = set()
+        for ld in list(loads_in.values()) + [qload]:
+            if name in ld.names:
+                out.add(ld.input)
+        a = assign.get(name)
+        if a is not None:
+            for x in a.args:
+                if isinstance(x, str):
+                    out |= sources(x, seen)
+        return out
+
+    dsrc = sources(dot)
+    if Q.name not in dsrc:
+        return None
+    kname = next((n for n in kv_inputs if n in dsrc), None)
+    vname = next((n for n in kv_inputs if n != kname), None)
+    if kname is None or vname is None or vname in dsrc:
+        return None
+    scale = None
+    for st in inner:
+        if type(st).__name__ == "Assign" and (getattr(st.op, "name", None) or str(st.op)) == "multiply":
+            args = list(st.args)
+            if len(args) == 2 and args[0] == dot and type(args[1]).__name__ == "Literal":
+                scale = float(args[1].value)
+    if scale is None:
+        return None
+    sels = [st for st in inner if type(st).__name__ == "Select"]
+    causal = False
+    if len(sels) > 1:
+        return None
+    if sels and len(sels[0].branches) == 1:
+        sels = []                        # only the catch-all branch: no mask
+    if sels:
+        if len(sels[0].branches) != 2:
+            return None
+        br = sels[0].branches[0]
+        c = br.select
+        v = br.value
+        if not (type(c).__name__ == "BinaryExpr" and c.op == ">" and _is_var(c.left, kv) and _is_var(c.right, ax[2])):
+            return None
+        if not (type(v).__name__ == "Literal" and float(v.value) == float("-inf")):
+            return None
+        causal = True
+    accs = [st for st in inner if type(st).__name__ == "Accum"]
+    ops = sorted((getattr(a.op, "name", None) or str(a.op)) for a in accs)
+    if ops.count("maximum") != 1 or ops.count("add") != 1 + dim // 32:
+        return None
+    writes = [st for st in stmts if type(st).__name__ == "Write"]
+    if len(writes) != 1 or writes[0].output != O.name or _index_vars(writes[0].index) != [ax[0], ax[1], ax[2], d0]:
+        return None
+    for v in writes[0].values:
+        a = assign.get(v)
+        if a is None or (getattr(a.op, "name", None) or str(a.op)) != "divide":
+            return None
+    K = vals[kname]
+    V = vals[vname]
+    return Q, K, V, O, bt, hd, seq, dim, causal, scale
+
+
 def _flat(body):
     out = []
     walk(body, out.append)
@@ -179,4 +326,12 @@ def try_lower(graph, node, kmeta, prefix, options):
         b = tc_gemm.gemm_entry(node.op.name, bt, m, n, k, sms=int(options.get("sms", 148)),
                                names=(X.name, Y.name, C.name), prefix=prefix)
         return b
+    hit = match_attention(graph, node)
+    if hit is not None:
+        Q, K, V, O, bt, hd, seq, dim, causal, scale = hit
+        from .kernels import tc_attention
+        if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES):
+            return None
+        return tc_attention.attention_entry(node.op.name, bt, hd, seq, causal, scale,
+                                            names=(Q.name, K.name, V.name, O.name), prefix=prefix)
     return None

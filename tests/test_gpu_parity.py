@@ -17,7 +17,7 @@ from emmy_ptx_b200.ir import Graph
 from emmy_ptx_b200.runtime import Executable
 from emmy_ptx_b200.launcher import Device
 from oracle.run import oracle_outputs
-from tests.checks import compare, rtol_for
+from tests.checks import compare, rtol_for, rms_floor_for
 
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -37,9 +37,10 @@ def test_small_config_matches_oracle(key):
     p = irgen.SMALL[key]()
     t = data.make_inputs(p)
     want = oracle_outputs(p, t)
-    got, _ = _run_ours(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.error_code() == 0
     for a in p.outputs:
-        compare(got[a.name], want[a.name], a.dtype, rtol_for(p), f"{key}.{a.name}")
+        compare(got[a.name], want[a.name], a.dtype, rtol_for(p), f"{key}.{a.name}", rms_floor=rms_floor_for(p))
 
 
 @pytest.mark.parametrize("key", sorted(irgen.SMALL))
@@ -137,3 +138,26 @@ def test_full_bmm_tensor_core_sampled():
     for b in (0, 7, 15):
         want = torch.matmul(A[b].double(), B[b].double())
         compare(C[b], want, "f32", 1e-4, f"c4 full batch {b}")
+
+
+def test_full_attention_tensor_core_sampled():
+    """Config 5 at full size through the tcgen05 kernel; sampled heads against float64 attention."""
+    import math
+    p = irgen.FULL["c5"]()
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    shape = p.spec("Q").shape
+    Q, K, V = ((torch.randn(shape, generator=gen, device="cuda")).to(torch.bfloat16) for _ in range(3))
+    O = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    assert mod.kernels[0]["kind"] == "tcgen05_attention"
+    ex = Executable(mod)
+    ex({"Q": Q, "K": K, "V": V, "O": O})
+    torch.cuda.synchronize()
+    assert ex.error_code() == 0
+    scale = 1.0 / math.sqrt(shape[-1])
+    for b, h in ((0, 0), (3, 17), (7, 31)):
+        q, k, v = Q[b, h].double(), K[b, h].double(), V[b, h].double()
+        s_ = (q @ k.T) * scale
+        s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
+        want = torch.softmax(s_, -1) @ v
+        compare(O[b, h], want, "bf16", 1e-4, f"c5 full ({b},{h})", rms_floor=True)

@@ -4,7 +4,7 @@ import copy
 from emmy_ptx_b200 import irgen
 from emmy_ptx_b200.compiler import compile_graph
 from emmy_ptx_b200.ir import Graph
-from emmy_ptx_b200.patterns import match_bmm
+from emmy_ptx_b200.patterns import match_bmm, match_attention
 
 
 def _kernel(p):
@@ -68,3 +68,39 @@ def test_patterns_can_be_disabled():
     p = irgen.FULL["c4"]()
     mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"patterns": False})
     assert mod.kernels[0]["kind"] == "generic"
+
+
+def test_attention_ir_is_recognised():
+    for key, tab, causal in (("c5", irgen.FULL, True), ("c5tc", irgen.SMALL, True), ("c5tcnc", irgen.SMALL, False)):
+        p = tab[key]()
+        g, k = _kernel(p)
+        hit = match_attention(g, k)
+        assert hit is not None, key
+        Q, K, V, O, bt, hd, seq, dim, c, scale = hit
+        assert (Q.name, K.name, V.name, O.name) == ("Q", "K", "V", "O")
+        assert (bt, hd, seq, dim, c) == (p.params["batch"], p.params["heads"], p.params["seq"], p.params["dim"], causal)
+        assert abs(scale - p.params["scale"]) < 1e-7
+    full = irgen.FULL["c5"]()
+    rec = compile_graph(Graph.from_dict(full.graph), full.meta()).kernels[0]
+    assert rec["kind"] == "tcgen05_attention" and rec["block"] == [384, 1, 1] and rec["grid"] == [4096, 1, 1]
+
+
+def test_attention_with_a_different_mask_is_refused():
+    p = irgen.SMALL["c5tc"]()
+    d = copy.deepcopy(p.graph)
+
+    def edit(stmts):
+        for st in stmts:
+            if st.get("kind") == "Select":
+                st["branches"][0]["select"]["op"] = ">="          # excludes the diagonal: not causal
+            for key in ("body", "else_body"):
+                if isinstance(st.get(key), list):
+                    edit(st[key])
+    edit(d["nodes"]["attention_causal"]["op_fields"]["body"])
+    g = Graph.from_dict(d)
+    assert match_attention(g, g.kernels()[0]) is None
+
+
+def test_small_head_dim_stays_on_cuda_cores():
+    p = irgen.SMALL["c5nc"]()                 # D = 64: not the 128-wide tensor-core tile
+    assert compile_graph(Graph.from_dict(p.graph), p.meta()).kernels[0]["kind"] == "generic"
