@@ -1,23 +1,27 @@
-"""Causal / full attention on the 5th-generation tensor cores: QK^T and PV with tcgen05, S and O in TMEM.
+"""Causal / full attention on the 5th-generation tensor cores: QK^T and PV with tcgen05, S, P and O in TMEM.
 
 O = softmax(Q K^T * scale [+ causal mask]) V for Q, K, V, O bf16 [batch, heads, S, 128] — the online-softmax
 Accum loop nest of the attention IR (config 5).  One CTA owns 256 query rows of one (batch, head) as two
 128-row tiles that take turns on the tensor core:
 
-* warp 0 issues TMA: both Q tiles once, then K_0, V_0, K_1, V_1, ... through a 3-stage ring of 32 KiB;
+* warp 0 issues TMA: both Q tiles once, then K_0, V_0, K_1, V_1, ... through a 4-stage ring of 32 KiB;
 * warp 1 owns TMEM (512 columns: S_0, S_1, O_0, O_1, 128 each) and issues, from one thread,
-  S_i = Q_i K_j^T (M=128, N=128, K=128 as 8 MMAs, both operands K-major) and O_i += P_i V_j
-  (P K-major in shared memory, V MN-major), interleaved PV_0(j), S_0(j+1), PV_1(j), S_1(j+1);
+  S_i = Q_i K_j^T (M=128, N=128, K=128 as 8 MMAs, both operands K-major in shared memory) and
+  O_i += P_i V_j with P_i read from TMEM (V MN-major in shared memory), in the order
+  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): the tensor core runs one tile while the other is in softmax;
 * warps 4-7 (tile 0) and 8-11 (tile 1) run the online softmax, one thread per row: load the row of S
   from TMEM, mask the diagonal block, take the row max, compute p = 2^(s*scale*log2e - m) with the MUFU
-  ``ex2``, accumulate the row sum, write P as bf16 into the K-major 128-byte-swizzled layout the MMA
-  reads, and rescale the O row in TMEM only when the running max grew by more than 2^8 (a stale max
-  is exact as long as P and the row sum use the same one);
+  ``ex2``, accumulate the row sum, and write P back into S's TMEM columns (S_i(j+1) is issued after
+  PV_i(j), and MMAs from one thread execute in order, so the next S never overwrites a P still being
+  read).  O is rescaled in TMEM only when a row's running max grew by more than 2^8 (a stale max is
+  exact as long as P and the row sum use the same one);
 * blocks above the diagonal are never computed; CTAs start with the longest rows (causal work grows
   with the query index).
 
-P is rounded to bf16 for the PV product (kind::f16 multiplies bf16 by bf16), which adds up to 2^-9
-relative error per term before the f32 accumulation.
+The tensor core multiplies bf16 by bf16, so P is written as two bf16 parts, P = P_hi + P_lo
+(P_lo = bf16(p - P_hi)), and O_i += P_hi V + P_lo V: the product keeps ~16 significant bits of p,
+so the result matches an f32-P computation to within the output's bf16 rounding.  ``precise=False``
+drops P_lo (one PV pass, 2^-9 relative error per term).
 
 Every mbarrier wait is bounded (see :mod:`.ptxasm`); a time-out writes a code to the status word and
 leaves the loop, the producer waits (bounded) for its own loads, and TMEM is always freed.
@@ -32,9 +36,9 @@ BQ = 128
 BKV = 128
 D = 128
 TILES = 2
-STAGES = 3
-TILE_BYTES = BQ * D * 2          # 32 KiB: a Q, K, V or P tile
-HALF = TILE_BYTES // 2           # one 64-column TMA box (or P half)
+STAGES = 4
+TILE_BYTES = BQ * D * 2          # 32 KiB: a Q, K or V tile
+HALF = TILE_BYTES // 2           # one 64-column TMA box
 THREADS = 384
 TMEM_COLS = 512
 LOG2E = 1.4426950408889634
@@ -43,7 +47,7 @@ RESCALE_THRESHOLD = 8.0          # log2 units: rescale O only when the max grew 
 ERR_PRODUCER, ERR_MMA, ERR_SOFTMAX, ERR_EPILOGUE, ERR_DRAIN = 11, 12, 13, 14, 15
 
 # barrier offsets (bytes from the barrier area)
-QFULL, FULL, EMPTY, SFULL, SFREE, PFULL, PFREE, SLOT = 0, 8, 32, 56, 72, 88, 104, 120
+QFULL, FULL, EMPTY, SFULL, PFULL, PFREE, SLOT = 0, 8, 40, 72, 88, 104, 120
 
 
 def _f32(v: float) -> str:
@@ -52,7 +56,7 @@ def _f32(v: float) -> str:
 
 
 def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, scale: float,
-                    names=("Q", "K", "V", "O"), prefix: str = "") -> dict:
+                    names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True) -> dict:
     if seq % (BQ * TILES) or seq % BKV:
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     nt = seq // (BQ * TILES)
@@ -60,7 +64,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a = Asm()
     idesc_qk = idesc_f16(BQ, BKV, False, False)
     idesc_pv = idesc_f16(BQ, D, False, True)
-    kdesc_hi = smem_desc_hi(16, 1024)            # K-major SW128 (Q, K, P)
+    kdesc_hi = smem_desc_hi(16, 1024)            # K-major SW128 (Q, K)
     vdesc_hi = smem_desc_hi(HALF, 1024)          # MN-major SW128 (V): 64-column atoms 16 KiB apart
     cscale = _f32(scale * LOG2E)
 
@@ -99,11 +103,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mov.u32 {raw}, {smem_sym};")
     a(f"add.u32 {base}, {raw}, 1023;")
     a(f"and.b32 {base}, {base}, -1024;")
-    sQ, sP, sKV, bars = a.r(), a.r(), a.r(), a.r()
+    sQ, sKV, bars = a.r(), a.r(), a.r()
     a(f"mov.u32 {sQ}, {base};")
-    a(f"add.u32 {sP}, {base}, {TILES * TILE_BYTES};")
-    a(f"add.u32 {sKV}, {base}, {2 * TILES * TILE_BYTES};")
-    a(f"add.u32 {bars}, {base}, {2 * TILES * TILE_BYTES + STAGES * TILE_BYTES};")
+    a(f"add.u32 {sKV}, {base}, {TILES * TILE_BYTES};")
+    a(f"add.u32 {bars}, {base}, {TILES * TILE_BYTES + STAGES * TILE_BYTES};")
 
     p0 = a.r("p")
     a(f"setp.eq.u32 {p0}, {tid}, 0;")
@@ -115,7 +118,6 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{EMPTY + 8 * s}], 1;")
     for i in range(TILES):
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{SFULL + 8 * i}], 1;")
-        a(f"mbarrier.init.shared::cta.b64 [{bars}+{SFREE + 8 * i}], 4;")
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFULL + 8 * i}], 4;")
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFREE + 8 * i}], 1;")
     a("fence.mbarrier_init.release.cluster;")
@@ -278,18 +280,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         return sb, ebr
 
     def qk(i, kbase, jreg):
-        """S_i = Q_i K^T for the K block at ``kbase``; waits for the softmax to free S_i first."""
-        skip_w = a.L("qkw")
-        pz = a.r("p")
-        a(f"setp.eq.u32 {pz}, {jreg}, 0;")
-        a(f"@{pz} bra {skip_w};")
-        sfb, par_ = a.r(), a.r()
-        a(f"add.u32 {sfb}, {bars}, {SFREE + 8 * i};")
-        a(f"sub.u32 {par_}, {jreg}, 1;")
-        a(f"and.b32 {par_}, {par_}, 1;")
-        wait_bar(a, sfb, par_, err, ERR_MMA, l_mdone)
-        a.label(skip_w)
-        a("tcgen05.fence::after_thread_sync;")
+        """S_i = Q_i K^T for the K block at ``kbase``.  Issued after PV_i of the previous block, which
+        read P_i from the same TMEM columns; the tensor core runs one thread's MMAs in order."""
         dcol = a.r()
         a(f"add.u32 {dcol}, {taddr}, {BKV * i};")
         qbase = a.r()
@@ -304,7 +296,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{sfull}];")
 
     def pv(i, vbase, jreg):
-        """O_i += P_i V for the V block at ``vbase``, once the softmax has written P_i."""
+        """O_i += P_i V for the V block at ``vbase`` (P_i in TMEM: hi part in S_i's columns 0-63, lo
+        part in 64-127, two bf16 per column), once the softmax has written P_i."""
         pfb, par_ = a.r(), a.r()
         a(f"add.u32 {pfb}, {bars}, {PFULL + 8 * i};")
         a(f"and.b32 {par_}, {jreg}, 1;")
@@ -312,17 +305,17 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a("tcgen05.fence::after_thread_sync;")
         dcol = a.r()
         a(f"add.u32 {dcol}, {taddr}, {2 * BKV + D * i};")
-        pbase = a.r()
-        a(f"add.u32 {pbase}, {sP}, {TILE_BYTES * i};")
-        for k in range(BKV // 16):
-            da = desc(pbase, (k // 4) * HALF + (k % 4) * 32, khi)
-            db = desc(vbase, 2048 * k, vhi)
-            if k == 0:
-                pacc = a.r("p")
-                a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
-            else:
-                pacc = ptrue
-            a(f"tcgen05.mma.cta_group::1.kind::f16 [{dcol}], {da}, {db}, {ipv}, {pacc};")
+        for part in range(2 if precise else 1):
+            for k in range(BKV // 16):
+                at = a.r()
+                a(f"add.u32 {at}, {taddr}, {BKV * i + 64 * part + 8 * k};")
+                db = desc(vbase, 2048 * k, vhi)
+                if k == 0 and part == 0:
+                    pacc = a.r("p")
+                    a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
+                else:
+                    pacc = ptrue
+                a(f"tcgen05.mma.cta_group::1.kind::f16 [{dcol}], [{at}], {db}, {ipv}, {pacc};")
         pfree = a.r()
         a(f"add.u32 {pfree}, {bars}, {PFREE + 8 * i};")
         a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{pfree}];")
@@ -399,17 +392,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"add.u32 {last}, {last}, {ti};")                # tile i's last (diagonal) kv block
     else:
         a(f"sub.u32 {last}, {nb}, 1;")
-    sfb, sfr, pfb, pfr = a.r(), a.r(), a.r(), a.r()
+    sfb, pfb, pfr = a.r(), a.r(), a.r()
     a(f"mad.lo.u32 {sfb}, {ti}, 8, {bars};")
-    a(f"add.u32 {sfr}, {sfb}, {SFREE};")
     a(f"add.u32 {pfb}, {sfb}, {PFULL};")
     a(f"add.u32 {pfr}, {sfb}, {PFREE};")
     a(f"add.u32 {sfb}, {sfb}, {SFULL};")
-    # this row's 16-byte slots of P in the K-major 128-byte-swizzled layout
-    pbase, sw = a.r(), a.r()
-    a(f"mad.lo.u32 {pbase}, {ti}, {TILE_BYTES}, {sP};")
-    a(f"mad.lo.u32 {pbase}, {rowl}, 128, {pbase};")
-    a(f"and.b32 {sw}, {lane}, 7;")
     s_ = [a.r("f") for _ in range(BKV)]
     mref, lsum, jj = a.r("f"), a.r("f"), a.r()
     a(f"mov.b32 {mref}, 0fFF800000;")
@@ -429,11 +416,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"add.u32 {src}, {scol}, {32 * c};")
         a(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(s_[32 * c:32 * c + 32])}}}, [{src}];")
     a("tcgen05.wait::ld.sync.aligned;")
-    a("tcgen05.fence::before_thread_sync;")
-    a("bar.warp.sync -1;")
     ple = a.r("p")
     a(f"setp.eq.u32 {ple}, {lane}, 0;")
-    a(f"@{ple} mbarrier.arrive.shared::cta.b64 _, [{sfr}];")
     if causal:
         l_nomask = a.L("nomask")
         pdiag = a.r("p")
@@ -488,28 +472,38 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mov.b32 {mref}, {mnew};")
     a(f"setp.ne.u32 {anyneed}, {lane}, {lane};")
     a.label(l_after)
-    # p = 2^(s*c - m), row sum, P as bf16 into shared memory
+    # p = 2^(s*c - m), row sum, and P back into S_i's TMEM columns as bf16 pairs (hi, then lo)
     negm = a.r("f")
     a(f"neg.f32 {negm}, {mref};")
     parts = [a.r("f") for _ in range(4)]
     for pp in parts:
         a(f"mov.b32 {pp}, 0f00000000;")
-    for c8 in range(16):
-        words = []
-        for k in range(8):
-            idx = 8 * c8 + k
-            a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
-            a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
-            a(f"add.f32 {parts[k & 3]}, {parts[k & 3]}, {s_[idx]};")
-        for k in range(4):
+    for c16 in range(BKV // 32):                        # 32 values -> 16 packed columns per part
+        hi_w, lo_w = [], []
+        for k in range(16):
+            i0, i1 = 32 * c16 + 2 * k, 32 * c16 + 2 * k + 1
+            for idx in (i0, i1):
+                a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
+                a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
+                a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {s_[idx]};")
             w = a.r()
-            a(f"cvt.rn.bf16x2.f32 {w}, {s_[8 * c8 + 2 * k + 1]}, {s_[8 * c8 + 2 * k]};")
-            words.append(w)
-        x, ad = a.r(), a.r()
-        a(f"xor.b32 {x}, {sw}, {c8 & 7};")
-        a(f"shl.b32 {x}, {x}, 4;")
-        a(f"add.u32 {ad}, {pbase}, {x};")
-        a(f"st.shared.v4.b32 [{ad}+{(c8 >> 3) * HALF}], {{{', '.join(words)}}};")
+            a(f"cvt.rn.bf16x2.f32 {w}, {s_[i1]}, {s_[i0]};")
+            hi_w.append(w)
+            if precise:
+                h0, h1, r0, r1, wl = a.r("f"), a.r("f"), a.r("f"), a.r("f"), a.r()
+                a(f"shl.b32 {h0}, {w}, 16;")
+                a(f"and.b32 {h1}, {w}, -65536;")
+                a(f"sub.f32 {r0}, {s_[i0]}, {h0};")
+                a(f"sub.f32 {r1}, {s_[i1]}, {h1};")
+                a(f"cvt.rn.bf16x2.f32 {wl}, {r1}, {r0};")
+                lo_w.append(wl)
+        dst = a.r()
+        a(f"add.u32 {dst}, {scol}, {16 * c16};")
+        a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dst}], {{{', '.join(hi_w)}}};")
+        if precise:
+            dst2 = a.r()
+            a(f"add.u32 {dst2}, {scol}, {64 + 16 * c16};")
+            a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dst2}], {{{', '.join(lo_w)}}};")
     p01, p23 = a.r("f"), a.r("f")
     a(f"add.f32 {p01}, {parts[0]}, {parts[1]};")
     a(f"add.f32 {p23}, {parts[2]}, {parts[3]};")
@@ -528,9 +522,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         for r_ in regs:
             a(f"mul.f32 {r_}, {r_}, {alpha};")
         a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{src}], {{{', '.join(regs)}}};")
-    a("tcgen05.wait::st.sync.aligned;")
     a.label(l_norescale2)
-    a("fence.proxy.async.shared::cta;")
+    a("tcgen05.wait::st.sync.aligned;")
     a("tcgen05.fence::before_thread_sync;")
     a("bar.warp.sync -1;")
     a(f"@{ple} mbarrier.arrive.shared::cta.b64 _, [{pfb}];")
@@ -581,7 +574,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {taddr}, {TMEM_COLS};")
     a.label(l_nodealloc)
 
-    dyn = 2 * TILES * TILE_BYTES + STAGES * TILE_BYTES + 256 + 1024
+    dyn = TILES * TILE_BYTES + STAGES * TILE_BYTES + 256 + 1024
     entry = [f".visible .entry {name}(",
              "\t.param .u64 p_Q,", "\t.param .u64 p_K,", "\t.param .u64 p_V,", "\t.param .u64 p_O,",
              "\t.param .align 64 .b8 p_tmQ[128],", "\t.param .align 64 .b8 p_tmK[128],",
