@@ -249,8 +249,17 @@ def _combine(name, other, op, dtype):
 # ---- config 1: row softmax ------------------------------------------------------------------
 
 
-def softmax_ir(rows: int = 4096, cols: int = 1024) -> Problem:
-    """y = softmax(x, -1) for x f32 [rows, cols]: one block of cols/4 threads per row."""
+def softmax_ir(rows: int = 4096, cols: int = 1024, schedule: str | None = None) -> Problem:
+    """y = softmax(x, -1) for x f32 [rows, cols].
+
+    ``schedule="warp"`` (the default up to 1024 columns): one warp per row, each lane holding cols/32
+    values from cols/128 coalesced 16-byte loads issued back to back, both reductions inside the warp.
+    ``schedule="block"``: one block of cols/4 threads per row, WarpShuffle then TreeHalve across warps.
+    """
+    if schedule is None:
+        schedule = "warp" if cols <= 1024 else "block"
+    if schedule == "warp":
+        return _softmax_warp_ir(rows, cols)
     if cols % 128 or cols // 4 > 1024:
         raise ValueError("softmax_ir needs cols % 128 == 0 and cols <= 4096")
     t = cols // 4
@@ -288,6 +297,51 @@ def softmax_ir(rows: int = 4096, cols: int = 1024) -> Problem:
             TensorSpec("y", (rows, cols), "f32", output=True)]
     return Problem(f"softmax_{rows}x{cols}", "softmax", "row_softmax", _graph("row_softmax", args, body),
                    args, grid=rows, block=t, rtol=1e-5, atol=1e-7, params={"rows": rows, "cols": cols})
+
+
+def _tree(op: str, names: list, prefix: str, final: str) -> list:
+    """Pairwise Assigns combining ``names`` (at least two) with ``op``; the last one is named ``final``."""
+    stmts, lvl, k = [], list(names), 0
+    while len(lvl) > 1:
+        nxt = []
+        for j in range(0, len(lvl) - 1, 2):
+            nm = final if len(lvl) == 2 else f"{prefix}{k}_{j // 2}"
+            stmts.append(Assign(nm, op, [lvl[j], lvl[j + 1]]))
+            nxt.append(nm)
+        if len(lvl) % 2:
+            nxt.append(lvl[-1])
+        lvl, k = nxt, k + 1
+    return stmts
+
+
+def _softmax_warp_ir(rows: int, cols: int) -> Problem:
+    if cols % 128 or cols > 1024:
+        raise ValueError("the warp-per-row softmax needs cols % 128 == 0 and cols <= 1024")
+    chunks = cols // 128
+    xs = [[f"x{c}_{k}" for k in range(4)] for c in range(chunks)]
+    flat = [n for ch in xs for n in ch]
+    loads = []
+    for c in range(chunks):
+        loads.append(Let(f"col{c}", Bin("+", Bin("*", V("ln"), 4), 128 * c)))
+        loads.append(Load(xs[c], "x", [V("row"), V(f"col{c}")], "f32"))
+    es = [f"e_{n}" for n in flat]
+    body = [Tile([Axis("row", rows), Axis("ln", 32)], [
+        *loads,
+        *_tree("maximum", flat, "mx", "m"),
+        WarpShuffle(["m"], ["m_o"], _combine("m", "m_o", "maximum", "f32")),
+        *[Assign(f"z_{n}", "subtract", [n, "m"]) for n in flat],
+        *[Assign(f"e_{n}", "exp", [f"z_{n}"]) for n in flat],
+        *_tree("add", es, "sm", "s"),
+        WarpShuffle(["s"], ["s_o"], _combine("s", "s_o", "add", "f32")),
+        *[Assign(f"y_{n}", "divide", [f"e_{n}", "s"]) for n in flat],
+        *[Write("y", [f"y_{n}" for n in xs[c]], [V("row"), V(f"col{c}")], "f32") for c in range(chunks)],
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)),
+            TensorSpec("y", (rows, cols), "f32", output=True)]
+    threads = 128
+    return Problem(f"softmax_{rows}x{cols}", "softmax", "row_softmax", _graph("row_softmax", args, body),
+                   args, grid=(rows * 32 + threads - 1) // threads, block=threads, rtol=1e-5, atol=1e-7,
+                   params={"rows": rows, "cols": cols, "schedule": "warp"})
 
 
 # ---- config 2: full-array sum ---------------------------------------------------------------
@@ -533,7 +587,8 @@ FULL = {
 #: Small instances of the same kernels, sized so the CPU oracle finishes in seconds.
 SMALL = {
     "c1": lambda: softmax_ir(64, 1024),
-    "c1b": lambda: softmax_ir(33, 256),
+    "c1b": lambda: softmax_ir(33, 256, schedule="block"),
+    "c1w": lambda: softmax_ir(37, 384),
     "c2": lambda: sum_ir(1 << 16, "f32", blocks=8, threads=256),
     "c2odd": lambda: sum_ir(997, "f32", blocks=2, threads=128),
     "c2i": lambda: sum_ir(1 << 16, "i32", blocks=8, threads=256),

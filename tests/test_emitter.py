@@ -58,13 +58,22 @@ def test_fused_uses_packed_128bit_traffic_and_single_narrowing():
     assert "ld.global.b16" not in ptx and "div" not in ptx              # no scalar 16-bit, no index div
 
 
-def test_softmax_reductions_use_redux_and_one_smem_pass():
-    _, mod = _compile("c1", irgen.FULL)
+def test_block_softmax_reductions_use_redux_and_one_smem_pass():
+    block = {"b": lambda: irgen.softmax_ir(4096, 1024, schedule="block")}
+    _, mod = _compile("b", block)
     ptx = mod.ptx
     assert "redux.sync.max.f32" in ptx
     assert ptx.count("bar.sync") == 2                                    # the IR's two Syncs, no tree barriers
-    _, ref = _compile("c1", irgen.FULL, tree_barriers=True)
+    _, ref = _compile("b", block, tree_barriers=True)
     assert ref.ptx.count("bar.sync") == 2 + 2 * 3                        # log2(8 warps) per TreeHalve
+
+
+def test_warp_softmax_keeps_eight_loads_in_flight_without_barriers():
+    p, mod = _compile("c1", irgen.FULL)
+    ptx = mod.ptx
+    assert p.params["schedule"] == "warp"
+    assert ptx.count("ld.global.nc.v4.f32") == 8 and ptx.count("st.global.v4.f32") == 8
+    assert "bar.sync" not in ptx and "redux.sync.max.f32" in ptx
 
 
 def test_sum_kernel_unrolls_grid_stride_loads():
