@@ -94,7 +94,7 @@ def test_launch_record_round_trips_through_the_ptx_text():
 
 
 def test_multi_kernel_module_namespaces_shared_symbols():
-    a, b = irgen.SMALL["c1"](), irgen.SMALL["c2"]()
+    a, b = irgen.SMALL["c1b"](), irgen.SMALL["c2"]()
     g = dict(a.graph)
     g["nodes"] = {**a.graph["nodes"], **{k: v for k, v in b.graph["nodes"].items()}}
     mod = compile_graph(Graph.from_dict(g), None)
