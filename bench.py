@@ -256,6 +256,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every step from the host instead of CUDA graphs")
     ap.add_argument("--size", default="full", choices=["full", "small"],
                     help="small: a reduced instance of the same kernel (still larger than L2) for ncu captures")
     return ap.parse_args()
@@ -355,10 +356,11 @@ def main() -> int:
     collective = p.family == "sum" and world > 1
     allreduce = edist.AllReducePartials(dev, dist, rank, world) if collective else None
 
-    def step(t):
-        ex(t, stream)
+    def step(t, s=None):
+        s = stream if s is None else s
+        ex(t, s)
         if collective:
-            allreduce(t["out"], p.params["dtype"], stream)
+            allreduce(t["out"], p.params["dtype"], s)
 
     for i in range(max(args.warmup, 3)):
         step(sets[i % rotate])
@@ -367,35 +369,60 @@ def main() -> int:
         dist.barrier()
 
     launches0 = dev.launches
-    k0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    k1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    reps = args.steps if units * 1.0 > 1e11 or kind == "FLOP" else max(args.steps, 200)
+    graphs = []
+    if not args.no_graph:
+        # launch-bound steps are replayed from CUDA graphs: exactly K steps in one graph, and a
+        # kernel-only graph of `reps` back-to-back launches for the per-launch duration
+        g_steps = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_steps):
+            cs = torch.cuda.current_stream().cuda_stream
+            for i in range(args.steps):
+                step(sets[i % rotate], cs)
+        g_kern = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_kern):
+            cs = torch.cuda.current_stream().cuda_stream
+            for i in range(reps):
+                ex.launch(0, sets[i % rotate], cs, zero=False)
+        graphs = [g_steps, g_kern]
+        g_steps.replay()
+        g_kern.replay()
+        torch.cuda.synchronize()
+    gpu_launches = args.steps * len(mod.kernels)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler() if local == 0 else None
     if clocks:
         clocks.start()
+        time.sleep(0.3)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     e0.record()
-    for i in range(args.steps):
-        t = sets[i % rotate]
-        ex.zero_outputs(0, t, stream)
-        k0[i].record()
-        ex.launch(0, t, stream, zero=False)
-        k1[i].record()
-        if collective:
-            allreduce(t["out"], p.params["dtype"], stream)
+    if graphs:
+        graphs[0].replay()
+    else:
+        for i in range(args.steps):
+            step(sets[i % rotate])
     e1.record()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    clock = clocks.stop() if clocks else None
-    gpu_launches = dev.launches - launches0
     ms = e0.elapsed_time(e1)
+    # the kernel alone, back to back on the same stream (CUDA events around the whole sequence)
+    k0 = torch.cuda.Event(enable_timing=True)
+    k1 = torch.cuda.Event(enable_timing=True)
+    k0.record()
+    if graphs:
+        graphs[1].replay()
+    else:
+        for i in range(reps):
+            ex.launch(0, sets[i % rotate], stream, zero=False)
+    k1.record()
+    torch.cuda.synchronize()
+    clock = clocks.stop() if clocks else None
     ms_step = max_over_ranks(dist, ms / args.steps)
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(k0, k1))
-    kern_ms = max_over_ranks(dist, kern_ms)
+    kern_ms = max_over_ranks(dist, k0.elapsed_time(k1) / reps)
     value = world * units / (ms_step / 1000.0) / scale
 
     # correctness of what was timed (rank-local shard)
@@ -465,7 +492,7 @@ def main() -> int:
     traffic = TRAFFIC.get(key)
     roof = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
             "traffic": traffic, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
-            "kernel": mod.kernels[0]["entry"], "kernel_ms": kern_ms,
+            "kernel": mod.kernels[0]["entry"], "kernel_ms": kern_ms, "kernel_launches_timed": reps,
             "algorithmic_per_launch": units, "algorithmic_unit": kind}
 
     cpu = None
@@ -482,6 +509,10 @@ def main() -> int:
                "sample": f"{pool.sample_blocks} of {p.grid} thread blocks ({100 * frac:.1f}% of one step) "
                          f"through the numpy oracle, one process", "seconds": dt}
 
+    for g in graphs:
+        del g
+    graphs = []
+    torch.cuda.synchronize()
     if collective:
         allreduce.close()
     if rank == 0:
@@ -493,7 +524,9 @@ def main() -> int:
                        "parallelism": f"dp{world} ({'sharded + ncclAllReduce of the partial' if collective else 'sharded, no collective'})",
                        "l2": ("inputs exceed L2 (126 MB)" if rotate == 1 else f"{rotate} rotating buffer sets exceed 2x L2"),
                        "grid": p.grid, "block": p.block},
-            "gpu_launches": gpu_launches, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clock,
+            "gpu_launches": gpu_launches, "timing": ("CUDA graph replay of the K steps" if not args.no_graph
+                                                     else "host launches"),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clock,
             "check": check, "kernel_kind": mod.kernels[0].get("kind"),
         }
         print(json.dumps(line), flush=True)
