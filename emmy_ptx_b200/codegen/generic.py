@@ -362,8 +362,6 @@ class KernelEmitter:
             return Sym("s32", aff=Affine.const(e))
         if isinstance(e, float):
             return Sym("f32", op=f32_imm(e))
-        if isinstance(e, str):
-            return self.value(e)
         if cls == "BinaryExpr":
             return self.binary(e.op, self.expr(e.left), self.expr(e.right))
         if cls == "TernaryExpr":
@@ -1085,9 +1083,11 @@ class KernelEmitter:
             span = (unroll - 1) * step_c
             last = b.reg("b32")
             b.emit(f"add.s32 {last}, {cur}, {span};")
+            # the preheader (hoisted loop invariants) sits before the zero-trip guard, so what it
+            # defines exists on every path past the loop, including the one that skips it
+            b.open_loop()
             b.emit(f"setp.ge.s32 {p}, {last}, {endop};")
             b.emit(f"@{p} bra {rem_l};")
-            frame = b.open_loop()
             top = b.label("_lu")
             b.place(top)
             ctr = Affine.of(reg_atom(cur, lo, hi, depth=b.depth))
@@ -1101,9 +1101,9 @@ class KernelEmitter:
             b.emit(f"@{q} bra {top};")
             b.place(rem_l)
         p = b.reg("pred")
+        b.open_loop()
         b.emit(f"setp.ge.s32 {p}, {cur}, {endop};")
         b.emit(f"@{p} bra {exit_l};")
-        frame = b.open_loop()
         top = b.label("_l")
         b.place(top)
         body_pass(Affine.of(reg_atom(cur, lo, hi, depth=b.depth)))

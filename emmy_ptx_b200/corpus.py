@@ -1,0 +1,440 @@
+"""A coverage corpus of small Emmy-IR kernels in the categories of the reference's case files.
+
+The reference grows its tests from torch expressions lowered by Emmy (cases.txt, cases_matmul.txt,
+cases_fused.txt, cases_attention.txt: pointwise, reductions, normalisations, odd shapes, integer /
+half / double dtypes, masks).  Emmy is not installed, so these kernels are authored directly in the
+lowered IR vocabulary.  With the benchmark configurations (:mod:`.irgen`) they exercise every
+statement the reference lowers:
+
+* Tile, Let, Init, Accum, Assign (integer, float, predicate results and the math library);
+* Load / Write in f32, f16, bf16, f64, i32 and u8 (a predicate stored as a byte), atomic adds;
+* Select with several branches (first true branch wins), Cond with an else branch;
+* Loop (rolled and unrolled), StridedLoop (block-strided and with a thread-dependent end);
+* WarpShuffle as a reduction over one or two states and as an inclusive prefix scan, WarpBroadcast;
+* Smem + Sync + TreeHalve block reductions;
+* ZeroPrologue in a kernel that runs before the one accumulating into the zeroed buffer, and graphs
+  of several kernels chained through an intermediate buffer.
+
+Each builder returns a :class:`~.irgen.Problem` whose ``params["expr"]`` names the source expression
+(the float64 torch form lives with the test oracle).
+"""
+from __future__ import annotations
+
+from .irgen import (Problem, TensorSpec, Tile, Axis, Load, Write, Assign, Let, Accum, Select, Cond, Loop,
+                    StridedLoop, WarpShuffle, TreeHalve, Smem, Sync, Lit, V, Bin, _graph)
+
+
+def _problem(expr, name, entry, args, body, grid, block, rtol=1e-5, atol=1e-6, **params):
+    return Problem(name, "corpus", entry, _graph(entry, args, body), args, grid=grid, block=block, rtol=rtol,
+                   atol=atol, params={"expr": expr, **params})
+
+
+def _block_reduce(states, bufs, ops, nwarps):
+    """WarpShuffle over ``states``; lane 0 of each warp stores them to shared memory; Sync; a
+    TreeHalve over the warps leaves the block's result in every thread."""
+    others = [f"{s}_o" for s in states]
+    second = [f"{s}_b" for s in states]
+    return [
+        WarpShuffle(states, others, [Assign(s, ops[s], [s, o]) for s, o in zip(states, others)]),
+        Cond(Bin("==", V("lane"), 0), [Write(bf, [s], [V("warp")], "f32") for s, bf in zip(states, bufs)]),
+        Sync(),
+        TreeHalve(bufs, states, second, [Assign(s, ops[s], [s, b]) for s, b in zip(states, second)], nwarps, "t"),
+    ]
+
+
+# ---- normalisations: a block per row, block-strided loops over the columns ------------------------
+
+
+def rmsnorm(rows=33, cols=512, eps=1e-6, threads=128):
+    """y = x / sqrt(mean(x^2) + eps) * w."""
+    nw = threads // 32
+    body = [
+        Smem("red", [nw], "f32", 16),
+        Tile([Axis("row", rows), Axis("t", threads)], [
+            StridedLoop("c", cols, V("t"), threads, [
+                Load(["x"], "x", [V("row"), V("c")], "f32"),
+                Assign("sq", "multiply", ["x", "x"]),
+                Accum("ss", "add", "sq"),
+            ], end=cols),
+            *_block_reduce(["ss"], ["red"], {"ss": "add"}, nw),
+            Assign("ms", "multiply", ["ss", Lit(1.0 / cols)]),
+            Assign("d", "add", ["ms", Lit(eps)]),
+            Assign("rs", "sqrt", ["d"]),
+            StridedLoop("c2", cols, V("t"), threads, [
+                Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+                Load(["w"], "w", [V("c2")], "f32"),
+                Assign("xn", "divide", ["x2", "rs"]),
+                Assign("y", "multiply", ["xn", "w"]),
+                Write("y", ["y"], [V("row"), V("c2")], "f32"),
+            ], end=cols),
+        ]),
+    ]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("w", (cols,), "f32", ("normal", 1.0)),
+            TensorSpec("y", (rows, cols), "f32", output=True)]
+    return _problem("rmsnorm", f"rmsnorm_{rows}x{cols}", "rms_norm", args, body, rows, threads, eps=eps)
+
+
+def layernorm(rows=16, cols=256, eps=1e-5, threads=64):
+    """y = (x - mean) / sqrt(var + eps) * g + b, mean and E[x^2] reduced together (two states)."""
+    nw = threads // 32
+    body = [
+        Smem("red_s", [nw], "f32", 16),
+        Smem("red_q", [nw], "f32", 16),
+        Tile([Axis("row", rows), Axis("t", threads)], [
+            StridedLoop("c", cols, V("t"), threads, [
+                Load(["x"], "x", [V("row"), V("c")], "f32"),
+                Accum("s", "add", "x"),
+                Assign("xx", "multiply", ["x", "x"]),
+                Accum("q", "add", "xx"),
+            ], end=cols),
+            *_block_reduce(["s", "q"], ["red_s", "red_q"], {"s": "add", "q": "add"}, nw),
+            Assign("mean", "multiply", ["s", Lit(1.0 / cols)]),
+            Assign("ex2_", "multiply", ["q", Lit(1.0 / cols)]),
+            Assign("m2", "multiply", ["mean", "mean"]),
+            Assign("var", "subtract", ["ex2_", "m2"]),
+            Assign("ve", "add", ["var", Lit(eps)]),
+            Assign("sd", "sqrt", ["ve"]),
+            StridedLoop("c2", cols, V("t"), threads, [
+                Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+                Load(["g"], "g", [V("c2")], "f32"),
+                Load(["b"], "b", [V("c2")], "f32"),
+                Assign("xc", "subtract", ["x2", "mean"]),
+                Assign("xn", "divide", ["xc", "sd"]),
+                Assign("xg", "multiply", ["xn", "g"]),
+                Assign("y", "add", ["xg", "b"]),
+                Write("y", ["y"], [V("row"), V("c2")], "f32"),
+            ], end=cols),
+        ]),
+    ]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("g", (cols,), "f32", ("normal", 1.0)),
+            TensorSpec("b", (cols,), "f32", ("normal", 1.0)), TensorSpec("y", (rows, cols), "f32", output=True)]
+    return _problem("layernorm", f"layernorm_{rows}x{cols}", "layer_norm", args, body, rows, threads, eps=eps)
+
+
+def log_softmax(rows=8, cols=512, threads=128):
+    """y = x - max - log(sum(exp(x - max))), three passes over the row."""
+    nw = threads // 32
+    body = [
+        Smem("red_m", [nw], "f32", 16),
+        Smem("red_s", [nw], "f32", 16),
+        Tile([Axis("row", rows), Axis("t", threads)], [
+            StridedLoop("c", cols, V("t"), threads, [
+                Load(["x"], "x", [V("row"), V("c")], "f32"),
+                Accum("m", "maximum", "x"),
+            ], end=cols),
+            *_block_reduce(["m"], ["red_m"], {"m": "maximum"}, nw),
+            StridedLoop("c1", cols, V("t"), threads, [
+                Load(["x1"], "x", [V("row"), V("c1")], "f32"),
+                Assign("z", "subtract", ["x1", "m"]),
+                Assign("e", "exp", ["z"]),
+                Accum("s", "add", "e"),
+            ], end=cols),
+            *_block_reduce(["s"], ["red_s"], {"s": "add"}, nw),
+            Assign("ls", "log", ["s"]),
+            StridedLoop("c2", cols, V("t"), threads, [
+                Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+                Assign("z2", "subtract", ["x2", "m"]),
+                Assign("y", "subtract", ["z2", "ls"]),
+                Write("y", ["y"], [V("row"), V("c2")], "f32"),
+            ], end=cols),
+        ]),
+    ]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("y", (rows, cols), "f32", output=True)]
+    return _problem("logsoftmax", f"logsoftmax_{rows}x{cols}", "log_softmax", args, body, rows, threads)
+
+
+# ---- reductions along other axes, scans, data-dependent loop bounds -------------------------------
+
+
+def col_sum(rows=100, cols=96):
+    """out[c] = sum over r of x[r, c]: a thread per column walks down the rows in a rolled Loop."""
+    body = [Tile([Axis("c", cols)], [
+        Loop("r", rows, [Load(["x"], "x", [V("r"), V("c")], "f32"), Accum("s", "add", "x")]),
+        Write("out", ["s"], [V("c")], "f32"),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("out", (cols,), "f32", output=True)]
+    return _problem("colsum", f"colsum_{rows}x{cols}", "col_sum", args, body, (cols + 63) // 64, 64)
+
+
+def mid_sum(a=2, b=64, c=32):
+    """out[i, k] = sum over j of x[i, j, k]: the middle axis, reduced in a fully unrolled Loop."""
+    body = [Tile([Axis("i", a), Axis("k", c)], [
+        Loop("j", b, [Load(["x"], "x", [V("i"), V("j"), V("k")], "f32"), Accum("s", "add", "x")], unroll=True),
+        Write("out", ["s"], [V("i"), V("k")], "f32"),
+    ])]
+    args = [TensorSpec("x", (a, b, c), "f32", ("normal", 1.0)), TensorSpec("out", (a, c), "f32", output=True)]
+    return _problem("midsum", f"midsum_{a}x{b}x{c}", "mid_sum", args, body, (a * c + 63) // 64, 64)
+
+
+def prefix_sum_tri(n=96):
+    """y[i] = sum over j <= i of x[j]: each thread's loop ends at its own index plus one."""
+    body = [Tile([Axis("i", n)], [
+        StridedLoop("j", n, 0, 1, [Load(["x"], "x", [V("j")], "f32"), Accum("s", "add", "x")],
+                    end=Bin("+", V("i"), 1)),
+        Write("y", ["s"], [V("i")], "f32"),
+    ])]
+    args = [TensorSpec("x", (n,), "f32", ("normal", 1.0)), TensorSpec("y", (n,), "f32", output=True)]
+    return _problem("tri", f"tri_{n}", "tri_sum", args, body, (n + 31) // 32, 32)
+
+
+def _scan(state):
+    return {"kind": "WarpShuffle", "state": [state], "state_b": [f"{state}_o"],
+            "combine_states": [Assign(state, "add", [state, f"{state}_o"])], "length": 32, "prefix": True}
+
+
+def cumsum_rows(rows=4, cols=64):
+    """y = cumsum(x, -1) for rows of 64: a warp per row, an inclusive prefix WarpShuffle over each
+    32-column half, the first half's total (lane 31) carried into the second by a WarpBroadcast."""
+    if cols != 64:
+        raise ValueError("cumsum_rows is written for rows of 64")
+    body = [Tile([Axis("row", rows), Axis("ln", 32)], [
+        Load(["a"], "x", [V("row"), V("ln")], "f32"),
+        Let("c1", Bin("+", V("ln"), 32)),
+        Load(["b"], "x", [V("row"), V("c1")], "f32"),
+        _scan("a"),
+        _scan("b"),
+        Assign("tot", "copy", ["a"]),
+        {"kind": "WarpBroadcast", "state": ["tot"], "length": 32},
+        Assign("b2", "add", ["b", "tot"]),
+        Write("y", ["a"], [V("row"), V("ln")], "f32"),
+        Write("y", ["b2"], [V("row"), V("c1")], "f32"),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("y", (rows, cols), "f32", output=True)]
+    return _problem("cumsum", f"cumsum_{rows}x{cols}", "cumsum_rows", args, body, rows, 32)
+
+
+# ---- dtypes, predicates, branches -------------------------------------------------------------------
+
+
+def int_ops(n=1000):
+    """Integer elementwise work with a two-way and a three-way Select (first true branch wins);
+    division and remainder truncate toward zero as in C."""
+    body = [Tile([Axis("i", n)], [
+        Load(["x"], "x", [V("i")], "i32"),
+        Load(["y"], "y", [V("i")], "i32"),
+        Assign("a", "bitwise_and", ["x", "y"], "i32"),
+        Assign("o", "bitwise_or", ["x", "y"], "i32"),
+        Assign("o3", "subtract", ["o", 3], "i32"),
+        Assign("gt", "greater", ["x", 4], "bool"),
+        Select("z", [(V("gt"), "a"), (None, "o3")]),
+        Select("sg", [(Bin("<", V("x"), 0), -1), (Bin("==", V("x"), 0), 0), (None, 1)]),
+        Assign("q", "divide", ["x", 3], "i32"),
+        Assign("r", "modulo", ["x", 3], "i32"),
+        Assign("sh", "left_shift", ["y", 2], "i32"),
+        Assign("mx", "maximum", ["q", "r"], "i32"),
+        Assign("w", "add", ["mx", "sh"], "i32"),
+        Write("z", ["z"], [V("i")], "i32"),
+        Write("s", ["sg"], [V("i")], "i32"),
+        Write("w", ["w"], [V("i")], "i32"),
+    ])]
+    args = [TensorSpec("x", (n,), "i32", ("randint", -20, 21)), TensorSpec("y", (n,), "i32", ("randint", 0, 9)),
+            TensorSpec("z", (n,), "i32", output=True), TensorSpec("s", (n,), "i32", output=True),
+            TensorSpec("w", (n,), "i32", output=True)]
+    return _problem("intops", f"intops_{n}", "int_ops", args, body, (n + 127) // 128, 128, rtol=0.0, atol=0.0)
+
+
+def half_gelu(rows=16, cols=256):
+    """f16 in and out: exact (erf) and tanh GELU over 8-wide (16-byte) vectors."""
+    ks = range(8)
+    body = [Tile([Axis("i", rows), Axis("j8", cols // 8)], [
+        Let("j", Bin("*", V("j8"), 8)),
+        Load([f"x{k}" for k in ks], "x", [V("i"), V("j")], "f16"),
+        *[Assign(f"g{k}", "gelu", [f"x{k}"], "f16") for k in ks],
+        *[Assign(f"h{k}", "gelu_tanh", [f"x{k}"], "f16") for k in ks],
+        Write("y", [f"g{k}" for k in ks], [V("i"), V("j")], "f16"),
+        Write("yt", [f"h{k}" for k in ks], [V("i"), V("j")], "f16"),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f16", ("normal", 1.0)), TensorSpec("y", (rows, cols), "f16", output=True),
+            TensorSpec("yt", (rows, cols), "f16", output=True)]
+    return _problem("gelu_f16", f"gelu_f16_{rows}x{cols}", "gelu_f16", args, body, rows * cols // 8 // 64, 64)
+
+
+def mask_where(n=777):
+    """A predicate stored as a u8 mask, and where(mask, x, 0)."""
+    body = [Tile([Axis("i", n)], [
+        Load(["x"], "x", [V("i")], "f32"),
+        Assign("m", "greater", ["x", Lit(0.0)], "bool"),
+        Assign("y", "where", ["m", "x", Lit(0.0)], "f32"),
+        Write("mask", ["m"], [V("i")], "u8"),
+        Write("y", ["y"], [V("i")], "f32"),
+    ])]
+    args = [TensorSpec("x", (n,), "f32", ("normal", 1.0)), TensorSpec("mask", (n,), "u8", output=True),
+            TensorSpec("y", (n,), "f32", output=True)]
+    return _problem("mask", f"mask_{n}", "mask_where", args, body, (n + 127) // 128, 128)
+
+
+def f64_affine(rows=2, cols=32):
+    """f64 buffers: narrowed to f32 in registers, widened at the store."""
+    body = [Tile([Axis("i", rows), Axis("j", cols)], [
+        Load(["x"], "x", [V("i"), V("j")], "f64"),
+        Assign("a", "multiply", ["x", Lit(2.5)]),
+        Assign("y", "add", ["a", Lit(1.0)], "f64"),
+        Write("y", ["y"], [V("i"), V("j")], "f64"),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f64", ("normal", 1.0)), TensorSpec("y", (rows, cols), "f64", output=True)]
+    return _problem("f64", f"f64_{rows}x{cols}", "f64_affine", args, body, 1, rows * cols)
+
+
+def cond_else(n=300):
+    """y = sqrt(x) where x >= 0, else -x/2: a Cond whose two sides each write."""
+    body = [Tile([Axis("i", n)], [
+        Load(["x"], "x", [V("i")], "f32"),
+        Cond(Bin(">=", V("x"), Lit(0.0)),
+             [Assign("r", "sqrt", ["x"]), Write("y", ["r"], [V("i")], "f32")],
+             [Assign("h", "multiply", ["x", Lit(-0.5)]), Write("y", ["h"], [V("i")], "f32")]),
+    ])]
+    args = [TensorSpec("x", (n,), "f32", ("normal", 1.0)), TensorSpec("y", (n,), "f32", output=True)]
+    return _problem("cond", f"cond_{n}", "cond_else", args, body, (n + 127) // 128, 128)
+
+
+MATH_UNARY = ("tanh", "sigmoid", "silu", "softplus", "erf", "absolute", "reciprocal", "sign", "square", "floor")
+MATH_BINARY = (("log", ("p1",)), ("log2", ("p1",)), ("rsqrt", ("p1",)), ("power", ("p1", "z")),
+               ("floor_divide", ("x", "p1")), ("fmod", ("x", "p1")),
+               ("maximum", ("x", "z")), ("minimum", ("x", "z")))
+
+
+def math_zoo(n=256):
+    """The rest of the math library on one vector; output [n, ops] flattened (p1 = |x| + 0.5)."""
+    stmts = [Load(["x"], "x", [V("i")], "f32"), Load(["z"], "z", [V("i")], "f32"),
+             Assign("ax", "absolute", ["x"]), Assign("p1", "add", ["ax", Lit(0.5)])]
+    outs = []
+    for k, op in enumerate(MATH_UNARY):
+        stmts.append(Assign(f"u{k}", op, ["x"]))
+        outs.append(f"u{k}")
+    for k, (op, a) in enumerate(MATH_BINARY):
+        stmts.append(Assign(f"v{k}", op, list(a)))
+        outs.append(f"v{k}")
+    nops = len(outs)
+    stmts += [Write("y", [o], [Bin("+", Bin("*", V("i"), nops), k)], "f32") for k, o in enumerate(outs)]
+    args = [TensorSpec("x", (n,), "f32", ("normal", 1.0)), TensorSpec("z", (n,), "f32", ("normal", 1.0)),
+            TensorSpec("y", (n * nops,), "f32", output=True)]
+    return _problem("mathzoo", f"mathzoo_{n}", "math_zoo", args, [Tile([Axis("i", n)], stmts)],
+                    (n + 127) // 128, 128, ops=nops)
+
+
+def hypot(n=256):
+    """y = hypot(x, z) = sqrt(x*x + z*z).  The reference emitter has this op in its table but raises a
+    TypeError building it (compile.py:973 passes one operand to a two-operand helper), so this case has
+    no reference PTX; the source expression pins it."""
+    body = [Tile([Axis("i", n)], [Load(["x"], "x", [V("i")], "f32"), Load(["z"], "z", [V("i")], "f32"),
+                                  Assign("h", "hypot", ["x", "z"]), Write("y", ["h"], [V("i")], "f32")])]
+    args = [TensorSpec("x", (n,), "f32", ("normal", 1.0)), TensorSpec("z", (n,), "f32", ("normal", 1.0)),
+            TensorSpec("y", (n,), "f32", output=True)]
+    return _problem("hypot", f"hypot_{n}", "hypot", args, body, (n + 127) // 128, 128)
+
+
+def exprs(rows=8, cols=64):
+    """The expression forms inside statements: FlatIndex, CastExpr (int to float), TernaryExpr, Dim,
+    FuncCallExpr, and logical_and / logical_not predicates feeding a where.
+
+    lin = r*cols + c;  t = (c < 32 ? x : 0) + 0.01*lin;  e = 0.5*exp(x);
+    y = where(not (x > 0 and c < 48), e, t)
+    """
+    body = [Tile([Axis("r", rows), Axis("c", cols)], [
+        Load(["x"], "x", [V("r"), V("c")], "f32"),
+        Let("lin", {"kind": "FlatIndex", "buffer": "x", "index": [V("r"), V("c")]}),
+        Assign("w", "multiply", [{"kind": "CastExpr", "expr": V("lin"), "dtype": "f32"}, Lit(0.01)]),
+        Assign("t", "add", [{"kind": "TernaryExpr", "cond": Bin("<", V("c"), {"kind": "Dim", "value": 32}),
+                             "if_true": V("x"), "if_false": Lit(0.0)}, "w"]),
+        Assign("e", "multiply", [{"kind": "FuncCallExpr", "name": "exp", "args": [V("x")]}, Lit(0.5)]),
+        Assign("pa", "logical_and", [Bin(">", V("x"), Lit(0.0)), Bin("<", V("c"), 48)], "bool"),
+        Assign("pn", "logical_not", ["pa"], "bool"),
+        Assign("y", "where", ["pn", "e", "t"]),
+        Write("y", ["y"], [V("r"), V("c")], "f32"),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("y", (rows, cols), "f32", output=True)]
+    return _problem("exprs", f"exprs_{rows}x{cols}", "expr_forms", args, body, rows * cols // 128, 128)
+
+
+# ---- graphs of several kernels ----------------------------------------------------------------------
+
+
+class MultiProblem(Problem):
+    """A problem whose graph holds several kernels, launched in ``launches`` order; each launch is
+    ``(entry, grid, block, zero_outputs, arg_order)``."""
+
+    def __init__(self, *a, launches=(), **kw):
+        super().__init__(*a, **kw)
+        self.launches = [tuple(x) for x in launches]
+
+    def meta(self) -> dict:
+        ks = []
+        for entry, grid, block, zero, order in self.launches:
+            recs = []
+            for name in order:
+                s = self.spec(name)
+                rec = {"name": s.name, "dtype": s.dtype, "shape": list(s.shape)}
+                if s.output:
+                    rec["output"] = True
+                recs.append(rec)
+            ks.append({"entry": entry, "arg_order": list(order), "args": recs, "grid": [grid, 1, 1],
+                       "block": [block, 1, 1], "smem_bytes": 0, "zero_outputs": list(zero)})
+        return {"kernels": ks, "rtol": self.rtol, "atol": self.atol}
+
+
+def _kernel_node(entry, inputs, outputs, body):
+    return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
+            "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
+
+
+def _multi_graph(inputs, kernels, outputs):
+    nodes = {a.name: {"op": "InputOp", "op_fields": {}, "inputs": [],
+                      "outputs": [{"name": a.name, "shape": list(a.shape), "dtype": a.dtype}]} for a in inputs}
+    for entry, ins, outs, body in kernels:
+        nodes[entry] = _kernel_node(entry, ins, outs, body)
+    return {"nodes": nodes, "inputs": [a.name for a in inputs], "outputs": [a.name for a in outputs]}
+
+
+def chain_mul_relu(n=1024):
+    """Kernel 1: t = a * b into an intermediate buffer; kernel 2: y = relu(t + c)."""
+    a, b, c = (TensorSpec(nm, (n,), "f32", ("normal", 1.0)) for nm in "abc")
+    t = TensorSpec("t", (n,), "f32", output=True)
+    y = TensorSpec("y", (n,), "f32", output=True)
+    k1 = [Tile([Axis("i", n)], [Load(["a"], "a", [V("i")], "f32"), Load(["b"], "b", [V("i")], "f32"),
+                                Assign("p", "multiply", ["a", "b"]), Write("t", ["p"], [V("i")], "f32")])]
+    k2 = [Tile([Axis("i", n)], [Load(["t"], "t", [V("i")], "f32"), Load(["c"], "c", [V("i")], "f32"),
+                                Assign("q", "add", ["t", "c"]), Assign("r", "relu", ["q"]),
+                                Write("y", ["r"], [V("i")], "f32")])]
+    g = _multi_graph([a, b, c], [("mul_kernel", ["a", "b"], [t], k1), ("relu_kernel", ["t", "c"], [y], k2)], [y])
+    return MultiProblem(f"chain_{n}", "corpus", "mul_kernel", g, [a, b, c, t, y], grid=n // 128, block=128,
+                        params={"expr": "chain"},
+                        launches=[("mul_kernel", n // 128, 128, [], ["a", "b", "t"]),
+                                  ("relu_kernel", n // 128, 128, [], ["t", "c", "y"])])
+
+
+def zero_then_histogram(n=4096, bins=16):
+    """Kernel 1 zeroes the histogram with a ZeroPrologue (no host memset); kernel 2 adds one per
+    element atomically into bin x % bins."""
+    x = TensorSpec("x", (n,), "i32", ("randint", 0, 1000))
+    h = TensorSpec("hist", (bins,), "i32", output=True)
+    k1 = [{"kind": "ZeroPrologue", "dst": "hist", "words": bins}]
+    k2 = [Tile([Axis("i", n)], [Load(["x"], "x", [V("i")], "i32"),
+                                Assign("bn", "modulo", ["x", bins], "i32"),
+                                Let("one", 1),
+                                Write("hist", ["one"], [V("bn")], "i32", atomic=True)])]
+    g = _multi_graph([x], [("zero_kernel", ["x"], [h], k1), ("hist_kernel", ["x", "hist"], [], k2)], [h])
+    return MultiProblem(f"hist_{n}", "corpus", "zero_kernel", g, [x, h], grid=2, block=64, rtol=0.0, atol=0.0,
+                        params={"expr": "hist", "bins": bins},
+                        launches=[("zero_kernel", 2, 64, [], ["x", "hist"]),
+                                  ("hist_kernel", n // 128, 128, [], ["x", "hist"])])
+
+
+CORPUS = {
+    "k_rmsnorm": rmsnorm,
+    "k_layernorm": layernorm,
+    "k_logsoftmax": log_softmax,
+    "k_colsum": col_sum,
+    "k_midsum": mid_sum,
+    "k_tri": prefix_sum_tri,
+    "k_cumsum": cumsum_rows,
+    "k_intops": int_ops,
+    "k_gelu_f16": half_gelu,
+    "k_mask": mask_where,
+    "k_f64": f64_affine,
+    "k_cond": cond_else,
+    "k_mathzoo": math_zoo,
+    "k_hypot": hypot,
+    "k_exprs": exprs,
+    "k_chain": chain_mul_relu,
+    "k_hist": zero_then_histogram,
+}

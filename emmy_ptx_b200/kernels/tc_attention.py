@@ -444,6 +444,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mul.f32 {mblk}, {lvl[0]}, {cscale};")
     a(f"max.f32 {mnew}, {mref}, {mblk};")
     l_first, l_after = a.L("first"), a.L("after")
+    # alpha (the O rescale factor) is 1 unless this block raises the running max past the
+    # threshold; it is written on both paths so every later read has a definition
+    alpha = a.r("f")
+    a(f"mov.b32 {alpha}, 0f3F800000;")
     pfirst = a.r("p")
     a(f"setp.eq.u32 {pfirst}, {jj}, 0;")
     a(f"@{pfirst} bra {l_first};")
@@ -457,8 +461,6 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"add.f32 {thr}, {mref}, {_f32(RESCALE_THRESHOLD)};")
     a(f"setp.gt.f32 {need}, {mnew}, {thr};")
     a(f"vote.sync.any.pred {anyneed}, {need}, -1;")
-    alpha = a.r("f")
-    a(f"mov.b32 {alpha}, 0f3F800000;")
     l_norescale = a.L("norescale")
     a(f"@!{anyneed} bra {l_norescale};")
     dm = a.r("f")

@@ -764,8 +764,6 @@ class Interpreter:
             return Val(np.int32(e), "i")
         if isinstance(e, float):
             return Val(np.float32(e), "f")
-        if isinstance(e, str):
-            return self.value(e)
         if cls == "BinaryExpr":
             return self.binary(e)
         if cls == "TernaryExpr":

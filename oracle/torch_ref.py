@@ -58,4 +58,100 @@ def reference(problem, tensors: dict):
     if fam == "attention":
         return {"O": attention(tensors["Q"], tensors["K"], tensors["V"], problem.params.get("causal", True),
                                problem.params.get("scale"))}
+    if fam == "corpus":
+        return CORPUS[problem.params["expr"]](tensors, problem.params)
     raise ValueError(f"no source expression for family {fam!r}")
+
+
+# ---- the coverage corpus (emmy_ptx_b200/corpus.py): each kernel's torch source expression ----------
+
+
+def _rmsnorm(t, p):
+    import torch
+    x = t["x"].double()
+    return {"y": x / torch.sqrt((x * x).mean(-1, keepdim=True) + p["eps"]) * t["w"].double()}
+
+
+def _layernorm(t, p):
+    import torch
+    x = t["x"].double()
+    return {"y": torch.nn.functional.layer_norm(x, (x.shape[-1],), t["g"].double(), t["b"].double(), p["eps"])}
+
+
+def _intops(t, p):
+    import torch
+    x, y = t["x"].long(), t["y"].long()
+    q = torch.div(x, 3, rounding_mode="trunc")
+    r = x - q * 3
+    return {"z": torch.where(x > 4, x & y, (x | y) - 3), "s": torch.sign(x), "w": torch.maximum(q, r) + (y << 2)}
+
+
+def _mathzoo(t, p):
+    import torch
+    F = torch.nn.functional
+    x, z = t["x"].double(), t["z"].double()
+    p1 = x.abs() + 0.5
+    cols = [torch.tanh(x), torch.sigmoid(x), F.silu(x), F.softplus(x), torch.erf(x), x.abs(), 1 / x,
+            torch.sign(x), x * x, torch.floor(x), torch.log(p1), torch.log2(p1), torch.rsqrt(p1),
+            torch.pow(p1, z), torch.floor(x / p1), torch.fmod(x, p1),
+            torch.maximum(x, z), torch.minimum(x, z)]
+    return {"y": torch.stack(cols, 1).reshape(-1)}
+
+
+def _chain(t, p):
+    import torch
+    prod = t["a"].double() * t["b"].double()
+    return {"t": prod, "y": torch.relu(prod + t["c"].double())}
+
+
+def _where_pos(t, p):
+    import torch
+    x = t["x"].double()
+    return {"mask": (x > 0).to(torch.uint8), "y": torch.where(x > 0, x, torch.zeros_like(x))}
+
+
+def _cond(t, p):
+    import torch
+    x = t["x"].double()
+    return {"y": torch.where(x >= 0, torch.sqrt(x.clamp_min(0)), -0.5 * x)}
+
+
+def _gelu(t, p):
+    import torch
+    x = t["x"].double()
+    return {"y": torch.nn.functional.gelu(x), "yt": torch.nn.functional.gelu(x, approximate="tanh")}
+
+
+def _exprs(t, p):
+    import torch
+    x = t["x"].double()
+    rows, cols = x.shape
+    r = torch.arange(rows, dtype=torch.float64)[:, None]
+    c = torch.arange(cols, dtype=torch.float64)[None, :]
+    w = (r * cols + c).float().double() * 0.01
+    tt = torch.where(c < 32, x, torch.zeros_like(x)) + w
+    e = 0.5 * torch.exp(x)
+    pa = (x > 0) & (c < 48)
+    return {"y": torch.where(~pa, e, tt)}
+
+
+CORPUS = {
+    "rmsnorm": _rmsnorm,
+    "layernorm": _layernorm,
+    "logsoftmax": lambda t, p: {"y": __import__("torch").log_softmax(t["x"].double(), -1)},
+    "colsum": lambda t, p: {"out": t["x"].double().sum(0)},
+    "midsum": lambda t, p: {"out": t["x"].double().sum(1)},
+    "tri": lambda t, p: {"y": t["x"].double().cumsum(0)},
+    "cumsum": lambda t, p: {"y": t["x"].double().cumsum(-1)},
+    "intops": _intops,
+    "gelu_f16": _gelu,
+    "mask": _where_pos,
+    # f64 buffers are computed in f32 registers by the reference (narrowed at the load)
+    "f64": lambda t, p: {"y": (t["x"].float() * 2.5 + 1.0).double()},
+    "cond": _cond,
+    "mathzoo": _mathzoo,
+    "hypot": lambda t, p: {"y": __import__("torch").hypot(t["x"].double(), t["z"].double())},
+    "exprs": _exprs,
+    "chain": _chain,
+    "hist": lambda t, p: {"hist": __import__("torch").bincount(t["x"].long() % p["bins"], minlength=p["bins"])},
+}

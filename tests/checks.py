@@ -1,6 +1,6 @@
 """Tolerance policy shared by the parity tests (the bars the benchmark configurations state).
 
-* integer outputs: bit-exact;
+* integer and byte outputs (including predicates stored as u8): bit-exact;
 * f32 fused / softmax / reduction outputs: relative 1e-5 (elementwise, with an absolute floor of
   1e-5 of the tensor's largest magnitude for entries near zero);
 * f32 matmul / attention outputs: relative 1e-4 of max(|ref|, rms(ref)) — a K-term dot product's
@@ -22,6 +22,13 @@ import torch
 BF16_REL = 2.0 ** -7
 
 
+def atol_for(problem) -> float:
+    """An absolute floor for the coverage kernels (their ``atol``, 1e-6): approximate hardware math
+    (ex2/lg2/rsqrt ``.approx``) near a zero of the function leaves an absolute error of a few f32
+    units of 1.0, which no relative bound covers."""
+    return problem.atol if problem.family == "corpus" else 0.0
+
+
 def rtol_for(problem) -> float:
     return 1e-4 if problem.family in ("bmm", "attention") else 1e-5
 
@@ -31,11 +38,11 @@ def rms_floor_for(problem) -> bool:
 
 
 def compare(got: torch.Tensor, ref: torch.Tensor, dtype: str, rtol: float, what: str = "",
-            rms_floor: bool = False) -> dict:
+            rms_floor: bool = False, atol: float = 0.0) -> dict:
     g = got.detach().cpu()
     r = ref.detach().cpu()
     assert g.shape == r.shape, f"{what}: shape {tuple(g.shape)} vs {tuple(r.shape)}"
-    if dtype in ("i32", "i64", "u32"):
+    if dtype in ("i32", "i64", "u32", "u8", "i8", "bool"):
         eq = torch.equal(g.long(), r.long())
         assert eq, f"{what}: integer result differs: {g.reshape(-1)[:4].tolist()} vs {r.reshape(-1)[:4].tolist()}"
         return {"max_abs": 0.0}
@@ -59,6 +66,7 @@ def compare(got: torch.Tensor, ref: torch.Tensor, dtype: str, rtol: float, what:
         bound = rtol * torch.clamp(r.abs(), min=rms) + 1e-30
     else:
         bound = rtol * r.abs() + rtol * 1e-5 * scale + 1e-30
+    bound = bound + atol
     bad = err > bound
     n_bad = int(bad.sum().item())
     worst = int(torch.argmax((err / bound).reshape(-1)).item())

@@ -2,12 +2,16 @@
 
     python tests/golden/make_golden.py [--reference PATH]
 
-For every small configuration in ``emmy_ptx_b200.irgen.SMALL`` it writes
+For every small configuration in ``emmy_ptx_b200.irgen.SMALL`` and every coverage kernel in
+``emmy_ptx_b200.corpus.CORPUS`` it writes
 
 * ``ref_ptx/<key>.ptx`` — the PTX the *reference* emitter (``compile.py`` of
   fanjialin8-create/emmy-ptx, run unmodified through ``emmy_shim``'s ``Graph.from_dict``) writes
   for that IR.  On a GPU it is run on the same seeded inputs as this backend and the oracle, so
-  it pins the oracle to the reference's own behaviour.
+  it pins the oracle to the reference's own behaviour.  PTX that fails the static def-use check
+  (``emmy_ptx_b200.codegen.ptxcheck``: a register read before any write on some path) is not
+  kept, and neither is PTX for IR the reference rejects; the manifest records why
+  (``ref_unsafe`` / ``ref_error``).
 * ``vectors/<key>.npz`` — the float64 source-expression result (``oracle/torch_ref.py``) on the
   seeded inputs, stored as float64, and an input checksum.
 * ``manifest.json`` — a hash of each IR, so a fixture made from a different IR is detected.
@@ -42,12 +46,28 @@ def input_digest(tensors: dict) -> str:
     return h.hexdigest()[:16]
 
 
+def _ptxas_error(ptx: str) -> str:
+    """The first error line ptxas prints for ``ptx`` targeting sm_100a, or '' when it assembles."""
+    import shutil
+    ptxas = shutil.which("ptxas") or "/usr/local/cuda/bin/ptxas"
+    with tempfile.TemporaryDirectory() as td:
+        src = Path(td) / "k.ptx"
+        src.write_text(ptx)
+        r = subprocess.run([ptxas, "-arch=sm_100a", str(src), "-o", str(Path(td) / "k.cubin")],
+                           capture_output=True, text=True)
+    if r.returncode == 0:
+        return ""
+    lines = [ln.split("k.ptx", 1)[-1].strip(" ,") for ln in r.stderr.splitlines() if "error" in ln]
+    return lines[0] if lines else f"exit status {r.returncode}"
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("EMMY_REFERENCE", "/root/reference"))
     args = ap.parse_args()
     import numpy as np
-    from emmy_ptx_b200 import irgen, data
+    from emmy_ptx_b200 import irgen, corpus, data
+    from emmy_ptx_b200.codegen.ptxcheck import undefined_uses
     from oracle import torch_ref
 
     compile_py = Path(args.reference) / "compile.py"
@@ -58,7 +78,7 @@ def main() -> int:
     (HERE / "vectors").mkdir(exist_ok=True)
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE / "emmy_shim"), str(ROOT)]))
     manifest = {}
-    for key, mk in irgen.SMALL.items():
+    for key, mk in {**irgen.SMALL, **corpus.CORPUS}.items():
         p = mk()
         meta = p.meta()
         with tempfile.TemporaryDirectory() as td:
@@ -66,17 +86,41 @@ def main() -> int:
             ir.write_text(json.dumps(p.graph))
             (Path(td) / "meta.json").write_text(json.dumps(meta))
             r = subprocess.run([sys.executable, str(compile_py), str(ir)], capture_output=True, text=True, env=env)
+        rec = {"ir": ir_hash(p.graph, meta), "entry": p.entry}
         if r.returncode != 0:
-            print(f"{key}: reference emitter failed:\n{r.stderr}", file=sys.stderr)
-            return 1
-        (HERE / "ref_ptx" / f"{key}.ptx").write_text(r.stdout)
+            # the reference rejects (or crashes on) this IR: record its last error line, keep no PTX
+            last = (r.stderr.strip().splitlines() or ["exit status %d" % r.returncode])[-1]
+            rec["ref_error"] = last
+            stale = HERE / "ref_ptx" / f"{key}.ptx"
+            if stale.exists():
+                stale.unlink()
+            print(f"{key}: reference emitter failed: {last}")
+        elif _ptxas_error(r.stdout):
+            # the reference wrote PTX that does not assemble for the GPU (the JIT rejects it the same way)
+            rec["ref_error"] = "ptxas: " + _ptxas_error(r.stdout)
+            stale = HERE / "ref_ptx" / f"{key}.ptx"
+            if stale.exists():
+                stale.unlink()
+            print(f"{key}: reference PTX does not assemble: {rec['ref_error']}")
+        elif undefined_uses(r.stdout):
+            # a register read before any write on some path: running it could fault the GPU, so the
+            # PTX is not kept (nothing can launch it) and the finding is recorded instead
+            entry, _, reg, text = undefined_uses(r.stdout)[0]
+            rec["ref_unsafe"] = f"{entry}: {reg} read before any write on some path: {text.strip()}"
+            stale = HERE / "ref_ptx" / f"{key}.ptx"
+            if stale.exists():
+                stale.unlink()
+            print(f"{key}: reference PTX not kept: {rec['ref_unsafe']}")
+        else:
+            (HERE / "ref_ptx" / f"{key}.ptx").write_text(r.stdout)
+            rec["ref_ptx_lines"] = r.stdout.count("\n")
+            print(f"{key}: {p.name} ref PTX {r.stdout.count(chr(10))} lines")
         t = data.make_inputs(p)
         ref = torch_ref.reference(p, t)
         np.savez_compressed(HERE / "vectors" / f"{key}.npz",
                             **{k: v.double().numpy() for k, v in ref.items()})
-        manifest[key] = {"ir": ir_hash(p.graph, meta), "inputs": input_digest(t), "entry": p.entry,
-                         "ref_ptx_lines": r.stdout.count("\n")}
-        print(f"{key}: {p.name} ref PTX {r.stdout.count(chr(10))} lines")
+        rec["inputs"] = input_digest(t)
+        manifest[key] = rec
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
     return 0
 
