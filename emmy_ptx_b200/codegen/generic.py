@@ -78,6 +78,9 @@ class KernelEmitter:
         self.sbase: dict[str, str] = {}          # smem buffer -> b32 shared-window base register
         self.written: set[str] = set()
         self.dyn_smem = 0
+        # programmatic dependent launch is opt-in: on the benchmark kernels it measured no better
+        # than plain stream order, and slower for the one-wave softmax
+        self.pdl = bool(self.opts.get("pdl", os.environ.get("EMMY_B200_PDL", "0") == "1"))
         self.uses_tid_const = False
 
     # ---- set-up (compile.py:476-519) ---------------------------------------------------
@@ -145,6 +148,12 @@ class KernelEmitter:
             b.emit(f"cvta.to.global.u64 {r}, {r};")
             self.preg[name] = r
             self.palign[name] = 16
+        if self.pdl:
+            # programmatic dependent launch: this grid may be scheduled while the previous kernel
+            # in the stream is still running; wait for it (and its memory) before the first global
+            # access, then let the next kernel's grid be scheduled onto SMs as they free up
+            b.emit("griddepcontrol.wait;")
+            b.emit("griddepcontrol.launch_dependents;")
         tid = b.reg("b32")
         b.emit(f"mov.u32 {tid}, %tid.x;")
         ctaid = b.reg("b32")
@@ -1329,4 +1338,5 @@ class KernelEmitter:
             "reqntid": self.T,
             "align": dict(self.palign),
             "zero_outputs": list(self.kmeta.get("zero_outputs") or []),
+            "pdl": self.pdl,
         }

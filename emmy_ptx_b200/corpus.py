@@ -203,6 +203,29 @@ def cumsum_rows(rows=4, cols=64):
     return _problem("cumsum", f"cumsum_{rows}x{cols}", "cumsum_rows", args, body, rows, 32)
 
 
+def cumsum_1d(n=128):
+    """y = cumsum(x) for one row of ``n`` (a multiple of 32): one warp walks the row in 32-element
+    chunks in a rolled Loop; each chunk is an inclusive prefix WarpShuffle plus the carry of the
+    chunks before it, and the chunk's total (lane 31, by WarpBroadcast) is added into the carry by an
+    Accum.  This is the 1-D scan the reference lists as wrong past the first chunk."""
+    if n % 32:
+        raise ValueError("cumsum_1d needs n % 32 == 0")
+    body = [Tile([Axis("row", 1), Axis("ln", 32)], [
+        Loop("ch", n // 32, [
+            Let("col", Bin("+", Bin("*", V("ch"), 32), V("ln"))),
+            Load(["v"], "x", [V("row"), V("col")], "f32"),
+            _scan("v"),
+            Assign("y", "add", ["v", "carry"]),
+            Write("y", ["y"], [V("row"), V("col")], "f32"),
+            Assign("tot", "copy", ["v"]),
+            {"kind": "WarpBroadcast", "state": ["tot"], "length": 32},
+            Accum("carry", "add", "tot"),
+        ]),
+    ])]
+    args = [TensorSpec("x", (1, n), "f32", ("normal", 1.0)), TensorSpec("y", (1, n), "f32", output=True)]
+    return _problem("cumsum", f"cumsum1d_{n}", "cumsum_1d", args, body, 1, 32)
+
+
 # ---- dtypes, predicates, branches -------------------------------------------------------------------
 
 
@@ -427,6 +450,7 @@ CORPUS = {
     "k_midsum": mid_sum,
     "k_tri": prefix_sum_tri,
     "k_cumsum": cumsum_rows,
+    "k_cumsum1d": cumsum_1d,
     "k_intops": int_ops,
     "k_gelu_f16": half_gelu,
     "k_mask": mask_where,

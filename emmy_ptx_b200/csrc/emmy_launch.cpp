@@ -278,7 +278,14 @@ int emmy_func_attribute(void* function, int attr, int* value) {
 int emmy_launch(void* function, const uint32_t grid[3], const uint32_t block[3],
                 const uint32_t cluster[3], uint32_t dyn_smem, void* stream, void** args,
                 uint32_t nargs) {
+  return emmy_launch_ex(function, grid, block, cluster, dyn_smem, stream, args, nargs, 0);
+}
+
+int emmy_launch_ex(void* function, const uint32_t grid[3], const uint32_t block[3],
+                   const uint32_t cluster[3], uint32_t dyn_smem, void* stream, void** args,
+                   uint32_t nargs, uint32_t flags) {
   if (!function || !grid || !block) return fail(EMMY_ERR_BAD_ARG, "null function/grid/block");
+  if (flags & ~static_cast<uint32_t>(EMMY_LAUNCH_PDL)) return fail(EMMY_ERR_BAD_ARG, "unknown launch flags 0x%x", flags);
   if (nargs && !args) return fail(EMMY_ERR_BAD_ARG, "null args with nargs > 0");
   if (int rc = ready()) return rc;
   CUlaunchConfig cfg;
@@ -291,14 +298,26 @@ int emmy_launch(void* function, const uint32_t grid[3], const uint32_t block[3],
   cfg.blockDimZ = block[2];
   cfg.sharedMemBytes = dyn_smem;
   cfg.hStream = static_cast<CUstream>(stream);
-  CUlaunchAttribute attr[1];
+  CUlaunchAttribute attr[2];
+  std::memset(attr, 0, sizeof(attr));
+  unsigned n_attr = 0;
   if (cluster && (cluster[0] > 1 || cluster[1] > 1 || cluster[2] > 1)) {
-    attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-    attr[0].value.clusterDim.x = cluster[0];
-    attr[0].value.clusterDim.y = cluster[1];
-    attr[0].value.clusterDim.z = cluster[2];
+    attr[n_attr].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr[n_attr].value.clusterDim.x = cluster[0];
+    attr[n_attr].value.clusterDim.y = cluster[1];
+    attr[n_attr].value.clusterDim.z = cluster[2];
+    ++n_attr;
+  }
+  if (flags & EMMY_LAUNCH_PDL) {
+    // the kernel executes griddepcontrol.wait before touching global memory, so it may be
+    // scheduled while the previous work in the stream is still finishing
+    attr[n_attr].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attr[n_attr].value.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
+  }
+  if (n_attr) {
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = n_attr;
   }
   return cu(g_drv.LaunchKernelEx(&cfg, static_cast<CUfunction>(function), args, nullptr),
             "cuLaunchKernelEx");
@@ -307,6 +326,12 @@ int emmy_launch(void* function, const uint32_t grid[3], const uint32_t block[3],
 int emmy_launch_u64(void* function, const uint32_t grid[3], const uint32_t block[3],
                     uint32_t dyn_smem, void* stream, const uint64_t* params,
                     const uint32_t* align, uint32_t nparams) {
+  return emmy_launch_u64_ex(function, grid, block, dyn_smem, stream, params, align, nparams, 0);
+}
+
+int emmy_launch_u64_ex(void* function, const uint32_t grid[3], const uint32_t block[3],
+                       uint32_t dyn_smem, void* stream, const uint64_t* params,
+                       const uint32_t* align, uint32_t nparams, uint32_t flags) {
   if (nparams > 256) return fail(EMMY_ERR_BAD_ARG, "too many parameters (%u)", nparams);
   if (nparams && !params) return fail(EMMY_ERR_BAD_ARG, "null params");
   void* args[256];
@@ -319,7 +344,7 @@ int emmy_launch_u64(void* function, const uint32_t grid[3], const uint32_t block
     args[i] = &vals[i];
   }
   const uint32_t one[3] = {1, 1, 1};
-  return emmy_launch(function, grid, block, one, dyn_smem, stream, args, nparams);
+  return emmy_launch_ex(function, grid, block, one, dyn_smem, stream, args, nparams, flags);
 }
 
 int emmy_tmap_encode_tiled(void* tmap, int dtype, uint32_t rank, uint64_t global_address,

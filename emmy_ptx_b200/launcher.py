@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libemmy_launch.so"
 c_u32p = ctypes.POINTER(ctypes.c_uint32)
 c_u64p = ctypes.POINTER(ctypes.c_uint64)
 vp = ctypes.c_void_p
+LAUNCH_PDL = 1          # EMMY_LAUNCH_PDL in include/emmy_launch.h
 
 # name -> argtypes (all functions return int)
 SIGNATURES = {
@@ -30,6 +31,10 @@ SIGNATURES = {
     "emmy_func_attribute": [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
     "emmy_launch": [vp, c_u32p, c_u32p, c_u32p, ctypes.c_uint32, vp, ctypes.POINTER(vp), ctypes.c_uint32],
     "emmy_launch_u64": [vp, c_u32p, c_u32p, ctypes.c_uint32, vp, c_u64p, c_u32p, ctypes.c_uint32],
+    "emmy_launch_ex": [vp, c_u32p, c_u32p, c_u32p, ctypes.c_uint32, vp, ctypes.POINTER(vp), ctypes.c_uint32,
+                       ctypes.c_uint32],
+    "emmy_launch_u64_ex": [vp, c_u32p, c_u32p, ctypes.c_uint32, vp, c_u64p, c_u32p, ctypes.c_uint32,
+                           ctypes.c_uint32],
     "emmy_tmap_encode_tiled": [vp, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, c_u64p, c_u64p, c_u32p,
                                c_u32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int],
     "emmy_event_create": [ctypes.POINTER(vp)],
@@ -164,19 +169,23 @@ class Device:
     def set_max_dyn_smem(self, fn, nbytes: int) -> None:
         check(self.lib.emmy_set_max_dyn_smem(fn, int(nbytes)), "emmy_set_max_dyn_smem")
 
-    def launch_u64(self, fn, grid, block, dyn_smem: int, stream: int, params, align=None) -> None:
+    def launch_u64(self, fn, grid, block, dyn_smem: int, stream: int, params, align=None, pdl: bool = False) -> None:
+        """Launch a kernel whose parameters are all 64-bit values.  ``pdl`` launches it as a
+        programmatic dependent of the stream's previous work (the kernel must begin with
+        ``griddepcontrol.wait``, as the launch record's ``pdl`` says)."""
         n = len(params)
         p = (ctypes.c_uint64 * n)(*[int(x) for x in params])
         a = (ctypes.c_uint32 * n)(*[int(x) for x in align]) if align is not None else None
-        check(self.lib.emmy_launch_u64(fn, dims3(grid), dims3(block), int(dyn_smem), vp(stream or 0), p, a, n),
-              "emmy_launch_u64")
+        check(self.lib.emmy_launch_u64_ex(fn, dims3(grid), dims3(block), int(dyn_smem), vp(stream or 0), p, a, n,
+                                          LAUNCH_PDL if pdl else 0), "emmy_launch_u64_ex")
         self.launches += 1
 
-    def launch(self, fn, grid, block, dyn_smem: int, stream: int, arg_ptrs, cluster=(1, 1, 1)) -> None:
+    def launch(self, fn, grid, block, dyn_smem: int, stream: int, arg_ptrs, cluster=(1, 1, 1),
+               pdl: bool = False) -> None:
         n = len(arg_ptrs)
         args = (vp * n)(*arg_ptrs)
-        check(self.lib.emmy_launch(fn, dims3(grid), dims3(block), dims3(cluster), int(dyn_smem),
-                                   vp(stream or 0), args, n), "emmy_launch")
+        check(self.lib.emmy_launch_ex(fn, dims3(grid), dims3(block), dims3(cluster), int(dyn_smem),
+                                      vp(stream or 0), args, n, LAUNCH_PDL if pdl else 0), "emmy_launch_ex")
         self.launches += 1
 
     def tmap_encode_tiled(self, out_buf, dtype: int, gaddr: int, dims, strides_bytes, box, elem_strides=None,

@@ -127,7 +127,8 @@ class Executable:
             t = tensors[name]
             ptrs.append(t.data_ptr() if hasattr(t, "data_ptr") else int(t))
             align.append(int(rec.get("align", {}).get(name, 1)))
-        self.dev.launch_u64(fn, g, rec["block"], rec.get("dyn_smem", 0), stream, ptrs, align)
+        self.dev.launch_u64(fn, g, rec["block"], rec.get("dyn_smem", 0), stream, ptrs, align,
+                            pdl=bool(rec.get("pdl")))
 
     def __call__(self, tensors: dict, stream: int | None = None) -> None:
         """Run every entry of the module once, in order, on ``stream`` (default: torch's current)."""

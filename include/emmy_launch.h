@@ -74,12 +74,30 @@ int emmy_launch(void* function, const uint32_t grid[3], const uint32_t block[3],
                 const uint32_t cluster[3], uint32_t dyn_smem, void* stream,
                 void** args, uint32_t nargs);
 
+/* Launch flags for the _ex variants. */
+#define EMMY_LAUNCH_PDL 1u  /* programmatic dependent launch (CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_
+                               STREAM_SERIALIZATION): the kernel may start while the previous work
+                               in the stream finishes; it must run griddepcontrol.wait before its
+                               first global memory access, as every generic kernel this backend
+                               emits does (launch record "pdl": true) */
+
+/* emmy_launch with flags (EMMY_LAUNCH_*); unknown bits are refused with EMMY_ERR_BAD_ARG.
+ * No reference counterpart: the reference launches with cuLaunchKernel only. */
+int emmy_launch_ex(void* function, const uint32_t grid[3], const uint32_t block[3],
+                   const uint32_t cluster[3], uint32_t dyn_smem, void* stream,
+                   void** args, uint32_t nargs, uint32_t flags);
+
 /* Launch with every parameter a 64-bit value (the emitted kernels' ABI: .param .u64 p_<arg> in
  * arg_order, tools/localrun.py:175-184).  Each pointer must be a multiple of align[i] bytes
  * (align may be null); a misaligned pointer is refused with EMMY_ERR_BAD_ARG before launch. */
 int emmy_launch_u64(void* function, const uint32_t grid[3], const uint32_t block[3],
                     uint32_t dyn_smem, void* stream, const uint64_t* params,
                     const uint32_t* align, uint32_t nparams);
+
+/* emmy_launch_u64 with flags (EMMY_LAUNCH_*). */
+int emmy_launch_u64_ex(void* function, const uint32_t grid[3], const uint32_t block[3],
+                       uint32_t dyn_smem, void* stream, const uint64_t* params,
+                       const uint32_t* align, uint32_t nparams, uint32_t flags);
 
 /* cuTensorMapEncodeTiled into a 128-byte, 64-byte-aligned buffer.  dtype is a
  * CUtensorMapDataType, strides are the rank-1 byte strides of dims 1..rank-1. */

@@ -36,3 +36,13 @@ def test_calls_without_a_driver_fail_cleanly():
     rc = lib.emmy_ctx_synchronize()
     assert rc != 0
     assert launcher.last_error()
+
+
+def test_launch_flags_are_checked_before_the_driver():
+    lib = launcher.load_library()
+    grid = (ctypes.c_uint32 * 3)(1, 1, 1)
+    block = (ctypes.c_uint32 * 3)(32, 1, 1)
+    fake_fn = ctypes.c_void_p(0x1000)        # never reaches the driver: the flag check fails first
+    rc = lib.emmy_launch_ex(fake_fn, grid, block, None, 0, None, None, 0, 0x80)
+    assert rc != 0
+    assert "unknown launch flags" in launcher.last_error()

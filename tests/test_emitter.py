@@ -156,3 +156,14 @@ def test_vector_width_falls_back_when_alignment_is_unprovable():
     mod = compile_graph(Graph.from_dict(_graph("k", args, body)), meta)
     assert "ld.global.nc.v4" not in mod.ptx and "ld.global.nc.v2.f32" in mod.ptx
     assert "st.global.v4.f32" in mod.ptx
+
+
+def test_programmatic_dependent_launch_is_opt_in_and_waits_before_memory():
+    p = irgen.SMALL["c3"]()
+    plain = compile_graph(Graph.from_dict(p.graph), p.meta())
+    assert "griddepcontrol" not in plain.ptx and not plain.kernels[0].get("pdl")
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"pdl": True})
+    assert mod.kernels[0]["pdl"] is True
+    body = mod.ptx.split("griddepcontrol.wait;", 1)
+    assert len(body) == 2 and "ld.global" not in body[0] and "st.global" not in body[0]
+    assert "griddepcontrol.launch_dependents;" in body[1]
