@@ -2,52 +2,71 @@
 
 O = softmax(Q K^T * scale [+ causal mask]) V for Q, K, V, O bf16 [batch, heads, S, 128] — the online-softmax
 Accum loop nest of the attention IR (config 5).  One CTA owns 256 query rows of one (batch, head) as two
-128-row tiles that take turns on the tensor core:
+128-row tiles and walks the key/value sequence in 64-row blocks:
 
-* warp 0 issues TMA: both Q tiles once, then K_0, V_0, K_1, V_1, ... through a 4-stage ring of 32 KiB;
-* warp 1 owns TMEM (512 columns: S_0, S_1, O_0, O_1, 128 each) and issues, from one thread,
-  S_i = Q_i K_j^T (M=128, N=128, K=128 as 8 MMAs, both operands K-major in shared memory) and
-  O_i += P_i V_j with P_i read from TMEM (V MN-major in shared memory), in the order
-  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): the tensor core runs one tile while the other is in softmax;
-* warps 4-7 (tile 0) and 8-11 (tile 1) run the online softmax, one thread per row: load the row of S
-  from TMEM, mask the diagonal block, take the row max, compute p = 2^(s*scale*log2e - m) with the MUFU
-  ``ex2``, accumulate the row sum, and write P back into S's TMEM columns (S_i(j+1) is issued after
-  PV_i(j), and MMAs from one thread execute in order, so the next S never overwrites a P still being
-  read).  O is rescaled in TMEM only when a row's running max grew by more than 2^8 (a stale max is
-  exact as long as P and the row sum use the same one);
-* blocks above the diagonal are never computed; CTAs start with the longest rows (causal work grows
-  with the query index).
+* warp 0 issues TMA: both Q tiles once, then K_0, V_0, K_1, V_1, ... through an 8-stage ring of 16 KiB;
+* warp 1 owns TMEM; one thread of warp 1 issues tile 0's ``tcgen05.mma`` and one thread of warp 2
+  tile 1's, so one issuer's waits and bookkeeping overlap the other's MMAs (the tensor core's
+  instruction queue is shallow).  TMEM holds O_0 | O_1 (128 columns each) and, per tile, two
+  64-column score buffers S_i[0], S_i[1]: the scores of block j+1 are computed into the other
+  buffer while the softmax of block j runs, so a tile's softmax never waits for its own previous
+  PV.  Per block j each issuer runs S_i(j+1) (M=128, N=64, K=128, both operands K-major in shared
+  memory), then O_i += P_i(j) V_j (M=128, N=128, K=64, P read from TMEM, V MN-major in shared
+  memory);
+* warps 4-7 (tile 0) and 8-11 (tile 1) run the online softmax, one thread per row: load the row of
+  S_i(j) from TMEM, mask the diagonal blocks, take the row max, compute p = 2^(s*scale*log2e - m)
+  with the MUFU ``ex2``, accumulate the row sum, and write P over the same TMEM columns.  O is
+  rescaled in TMEM only when a row's running max grew by more than 2^8 (a stale max is exact as
+  long as P and the row sum use the same one), after the previous PV has completed;
+* blocks above the diagonal are never computed; CTAs start with the longest rows.
 
-The tensor core multiplies bf16 by bf16, so P is written as two bf16 parts, P = P_hi + P_lo
-(P_lo = bf16(p - P_hi)), and O_i += P_hi V + P_lo V: the product keeps ~16 significant bits of p,
-so the result matches an f32-P computation to within the output's bf16 rounding.  ``precise=False``
-drops P_lo (one PV pass, 2^-9 relative error per term).
+The tensor core multiplies bf16 by bf16, so P is written as two bf16 parts, P = P_hi + P_lo: P_hi is
+p truncated to bf16 and P_lo the exact remainder p - P_hi truncated to bf16, both taken with integer
+masks and byte permutes (the conversion unit stays free for ``ex2``), and O_i += P_hi V + P_lo V.  The
+sum keeps p to within 2^-14 relative, so the result matches an f32-P computation to within the
+output's bf16 rounding.  ``precise=False`` drops P_lo (one PV pass, P rounded to nearest bf16, 2^-9
+relative error per term).
 
 Every mbarrier wait is bounded (see :mod:`.ptxasm`); a time-out writes a code to the status word and
 leaves the loop, the producer waits (bounded) for its own loads, and TMEM is always freed.
 """
 from __future__ import annotations
 
-import math
-
 from .ptxasm import Asm, idesc_f16, smem_desc_hi, wait_bar, wait_bar_warp
 
-BQ = 128
-BKV = 128
+BQ = 128                         # query rows per tile
+BKV = 64                         # key/value rows per block
 D = 128
 TILES = 2
-STAGES = 4
-TILE_BYTES = BQ * D * 2          # 32 KiB: a Q, K or V tile
-HALF = TILE_BYTES // 2           # one 64-column TMA box
+STAGES = 8
+Q_BYTES = BQ * D * 2             # 32 KiB: one Q tile
+Q_HALF = Q_BYTES // 2            # one 64-column TMA box of a Q tile
+KV_BYTES = BKV * D * 2           # 16 KiB: one K or V block
+KV_HALF = KV_BYTES // 2          # one 64-column TMA box of a K/V block
 THREADS = 384
 TMEM_COLS = 512
+S_COL0 = TILES * D               # S_i[b] at S_COL0 + 2*BKV*i + BKV*b
 LOG2E = 1.4426950408889634
 RESCALE_THRESHOLD = 8.0          # log2 units: rescale O only when the max grew by more than 2^8
 
 ERR_PRODUCER, ERR_MMA, ERR_SOFTMAX, ERR_EPILOGUE, ERR_DRAIN = 11, 12, 13, 14, 15
 
-# barrier offsets (bytes from the barrier area)
-QFULL, FULL, EMPTY, SFULL, PFULL, PFREE, SLOT = 0, 8, 40, 72, 88, 104, 120
+# barrier offsets (bytes from the barrier area): QFULL, FULL[8], EMPTY[8], SFULL[tile][buf],
+# PFULL[tile][buf], PFREE[tile][buf], then the TMEM address slot.  The S, P and PV-done handovers
+# have one barrier per buffer: the softmax runs up to two blocks ahead of the PVs (its next scores
+# are already computed), and a single barrier per tile could then be two phases away from a
+# parity wait, which cannot tell those phases apart.
+QFULL = 0
+FULL = 8
+EMPTY = FULL + 8 * STAGES
+SFULL = EMPTY + 8 * STAGES
+PFULL = SFULL + 8 * 2 * TILES
+PFREE = PFULL + 8 * 2 * TILES
+SLOT = PFREE + 8 * 2 * TILES
+BAR_BYTES = 256
+
+TRACE_SLOTS = 66                 # per-CTA trace rows: kv blocks 0..64, then one row of CTA facts
+TRACE_EVENTS = 24
 
 
 def _f32(v: float) -> str:
@@ -56,16 +75,21 @@ def _f32(v: float) -> str:
 
 
 def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, scale: float,
-                    names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True) -> dict:
-    if seq % (BQ * TILES) or seq % BKV:
+                    names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True,
+                    trace: bool = False) -> dict:
+    """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
+    grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`)."""
+    if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
+    if trace and seq // BKV + 1 >= TRACE_SLOTS:
+        raise ValueError("trace supports at most 64 key/value blocks")
     nt = seq // (BQ * TILES)
     grid = batch * heads * nt
     a = Asm()
     idesc_qk = idesc_f16(BQ, BKV, False, False)
     idesc_pv = idesc_f16(BQ, D, False, True)
-    kdesc_hi = smem_desc_hi(16, 1024)            # K-major SW128 (Q, K)
-    vdesc_hi = smem_desc_hi(HALF, 1024)          # MN-major SW128 (V): 64-column atoms 16 KiB apart
+    kdesc_hi = smem_desc_hi(16, 1024)            # K-major SW128 (Q, K): 8-row groups 1 KiB apart
+    vdesc_hi = smem_desc_hi(KV_HALF, 1024)       # MN-major SW128 (V): 64-column atoms 8 KiB apart
     cscale = _f32(scale * LOG2E)
 
     tid, warp, lane, cta = a.r(), a.r(), a.r(), a.r()
@@ -78,6 +102,31 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"cvta.to.global.u64 {o_ptr}, {o_ptr};")
     a(f"ld.param.u64 {err}, [p_err];")
     a(f"cvta.to.global.u64 {err}, {err};")
+    trc = None
+    if trace:
+        trc = a.r("rd")
+        a(f"ld.param.u64 {trc}, [p_trace];")
+        a(f"cvta.to.global.u64 {trc}, {trc};")
+        tcta = a.r("rd")
+        a(f"mul.wide.u32 {tcta}, {cta}, {TRACE_SLOTS * TRACE_EVENTS * 8};")
+        a(f"add.s64 {trc}, {trc}, {tcta};")          # this CTA's trace rows
+
+    def stamp(event, jreg, guard=None):
+        """clock64 into trace[cta][j][event] (j = TRACE_SLOTS-1 for per-CTA facts)."""
+        if not trace:
+            return
+        off, ck, ad = a.r(), a.r("rd"), a.r("rd")
+        if isinstance(jreg, int):
+            a(f"mov.u32 {off}, {jreg * TRACE_EVENTS};")
+        else:
+            a(f"mul.lo.u32 {off}, {jreg}, {TRACE_EVENTS};")
+        if not isinstance(event, int) or event:
+            a(f"add.u32 {off}, {off}, {event};")
+        a(f"mul.wide.u32 {ad}, {off}, 8;")
+        a(f"add.s64 {ad}, {ad}, {trc};")
+        a(f"mov.u64 {ck}, %clock64;")
+        a(f"{'@' + guard + ' ' if guard else ''}st.global.u64 [{ad}], {ck};")
+
     tq, tk, tv = a.r("rd"), a.r("rd"), a.r("rd")
     for reg, pname in ((tq, "p_tmQ"), (tk, "p_tmK"), (tv, "p_tmV")):
         a(f"mov.u64 {reg}, {pname};")
@@ -92,8 +141,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"rem.u32 {hh}, {bh}, {heads};")
     nb, row0 = a.r(), a.r()
     if causal:
-        a(f"shl.b32 {nb}, {t}, 1;")
-        a(f"add.u32 {nb}, {nb}, 2;")                    # tile 1 sees kv blocks 0..2t+1, tile 0 0..2t
+        a(f"shl.b32 {nb}, {t}, 2;")
+        a(f"add.u32 {nb}, {nb}, 4;")                    # tile 1 sees kv blocks 0..4t+3, tile 0 0..4t+1
     else:
         a(f"mov.u32 {nb}, {seq // BKV};")
     a(f"shl.b32 {row0}, {t}, 8;")                        # first query row of this CTA
@@ -105,8 +154,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"and.b32 {base}, {base}, -1024;")
     sQ, sKV, bars = a.r(), a.r(), a.r()
     a(f"mov.u32 {sQ}, {base};")
-    a(f"add.u32 {sKV}, {base}, {TILES * TILE_BYTES};")
-    a(f"add.u32 {bars}, {base}, {TILES * TILE_BYTES + STAGES * TILE_BYTES};")
+    a(f"add.u32 {sKV}, {base}, {TILES * Q_BYTES};")
+    a(f"add.u32 {bars}, {base}, {TILES * Q_BYTES + STAGES * KV_BYTES};")
 
     p0 = a.r("p")
     a(f"setp.eq.u32 {p0}, {tid}, 0;")
@@ -115,11 +164,12 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mbarrier.init.shared::cta.b64 [{bars}+{QFULL}], 1;")
     for s in range(STAGES):
         a(f"mbarrier.init.shared::cta.b64 [{bars}+{FULL + 8 * s}], 1;")
-        a(f"mbarrier.init.shared::cta.b64 [{bars}+{EMPTY + 8 * s}], 1;")
+        a(f"mbarrier.init.shared::cta.b64 [{bars}+{EMPTY + 8 * s}], {TILES};")
     for i in range(TILES):
-        a(f"mbarrier.init.shared::cta.b64 [{bars}+{SFULL + 8 * i}], 1;")
-        a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFULL + 8 * i}], 4;")
-        a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFREE + 8 * i}], 1;")
+        for b_ in range(2):
+            a(f"mbarrier.init.shared::cta.b64 [{bars}+{SFULL + 8 * (2 * i + b_)}], 1;")
+            a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFULL + 8 * (2 * i + b_)}], 4;")
+            a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFREE + 8 * (2 * i + b_)}], 1;")
     a("fence.mbarrier_init.release.cluster;")
     a("fence.proxy.async.shared::cta;")
     a.label(l_init)
@@ -135,16 +185,27 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a("tcgen05.fence::after_thread_sync;")
     taddr = a.r()
     a(f"ld.shared.b32 {taddr}, [{bars}+{SLOT}];")
+    if trace:
+        pt0 = a.r("p")
+        a(f"setp.eq.u32 {pt0}, {tid}, 0;")
+        stamp(0, TRACE_SLOTS - 1, pt0)
+        smid, sm64, sad = a.r(), a.r("rd"), a.r("rd")
+        a(f"mov.u32 {smid}, %smid;")
+        a(f"cvt.u64.u32 {sm64}, {smid};")
+        a(f"add.s64 {sad}, {trc}, {((TRACE_SLOTS - 1) * TRACE_EVENTS + 2) * 8};")
+        a(f"@{pt0} st.global.u64 [{sad}], {sm64};")
 
     l_end = a.L("end")
-    l_prod, l_mma, l_soft = a.L("prod"), a.L("mma"), a.L("soft")
-    pw0, pws = a.r("p"), a.r("p")
+    l_prod, l_mma, l_mma1, l_soft = a.L("prod"), a.L("mma"), a.L("mma1"), a.L("soft")
+    pw0, pw2, pws = a.r("p"), a.r("p"), a.r("p")
     a(f"setp.eq.u32 {pw0}, {warp}, 0;")
+    a(f"setp.eq.u32 {pw2}, {warp}, 2;")
     a(f"setp.ge.u32 {pws}, {warp}, 4;")
     a(f"@{pw0} bra {l_prod};")
     a(f"@{pw1} bra {l_mma};")
+    a(f"@{pw2} bra {l_mma1};")
     a(f"@{pws} bra {l_soft};")
-    a(f"bra {l_end};")                                   # warps 2-3: no role
+    a(f"bra {l_end};")                                   # warp 3: no role
 
     def tma4(dst, tmap, c0, c1, mbar):
         a(f"cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
@@ -157,13 +218,13 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"@{pl0} bra {l_end};")
     qb = a.r()
     a(f"add.u32 {qb}, {bars}, {QFULL};")
-    a(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qb}], {TILES * TILE_BYTES};")
+    a(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qb}], {TILES * Q_BYTES};")
     for i in range(TILES):
         r_i = a.r()
         a(f"add.u32 {r_i}, {row0}, {BQ * i};")
         for half in range(2):
             d_ = a.r()
-            a(f"add.u32 {d_}, {sQ}, {TILE_BYTES * i + HALF * half};")
+            a(f"add.u32 {d_}, {sQ}, {Q_BYTES * i + Q_HALF * half};")
             tma4(d_, tq, 64 * half, r_i, qb)
     n_, stage, phase = a.r(), a.r(), a.r()
     armed = [a.r() for _ in range(STAGES)]
@@ -185,15 +246,15 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"add.u32 {fb}, {fb}, {FULL};")
     a(f"xor.b32 {par}, {phase}, 1;")
     wait_bar(a, eb, par, err, ERR_PRODUCER, l_pdone)
-    a(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {TILE_BYTES};")
+    a(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {KV_BYTES};")
     for s in range(STAGES):
         ps = a.r("p")
         a(f"setp.eq.u32 {ps}, {stage}, {s};")
         a(f"@{ps} mov.u32 {armed[s]}, {phase};")
     kvrow, dst, isv = a.r(), a.r(), a.r("p")
     a(f"shr.u32 {kvrow}, {n_}, 1;")
-    a(f"shl.b32 {kvrow}, {kvrow}, 7;")
-    a(f"mad.lo.u32 {dst}, {stage}, {TILE_BYTES}, {sKV};")
+    a(f"shl.b32 {kvrow}, {kvrow}, 6;")
+    a(f"mad.lo.u32 {dst}, {stage}, {KV_BYTES}, {sKV};")
     tsel = a.r("rd")
     andn = a.r()
     a(f"and.b32 {andn}, {n_}, 1;")
@@ -201,7 +262,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"selp.b64 {tsel}, {tv}, {tk}, {isv};")
     tma4(dst, tsel, 0, kvrow, fb)
     dst2 = a.r()
-    a(f"add.u32 {dst2}, {dst}, {HALF};")
+    a(f"add.u32 {dst2}, {dst}, {KV_HALF};")
     tma4(dst2, tsel, 64, kvrow, fb)
     pw = a.r("p")
     a(f"add.u32 {stage}, {stage}, 1;")
@@ -227,150 +288,175 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a.label(wait_q)
     a(f"bra {l_end};")
 
-    # ---------------- MMA issuer --------------------------------------------------------------
-    a.label(l_mma)
-    pl1 = a.r("p")
-    a(f"setp.ne.u32 {pl1}, {lane}, 0;")
-    a(f"@{pl1} bra {l_end};")
-    l_mdone = a.L("mdone")
-    qb2, zero2 = a.r(), a.r()
-    a(f"add.u32 {qb2}, {bars}, {QFULL};")
-    a(f"mov.u32 {zero2}, 0;")
-    wait_bar(a, qb2, zero2, err, ERR_MMA, l_mdone)
-    a("tcgen05.fence::after_thread_sync;")
-    iqk, ipv = a.r(), a.r()
-    a(f"mov.u32 {iqk}, {idesc_qk};")
-    a(f"mov.u32 {ipv}, {idesc_pv};")
-    ptrue, pfalse = a.r("p"), a.r("p")
-    a(f"setp.eq.u32 {ptrue}, {lane}, {lane};")
-    a(f"setp.ne.u32 {pfalse}, {lane}, {lane};")
-    khi, vhi = a.r("rd"), a.r("rd")
-    a(f"mov.b64 {khi}, {kdesc_hi};")
-    a(f"mov.b64 {vhi}, {vdesc_hi};")
-    last0 = a.r()
-    a(f"sub.u32 {last0}, {nb}, {2 if causal else 1};")   # tile 0's last kv block
-
-    def desc(addr_reg, off, hi):
-        r1 = a.r()
-        d_ = a.r("rd")
-        a(f"add.u32 {r1}, {addr_reg}, {off};")
-        a(f"shr.u32 {r1}, {r1}, 4;")
-        a(f"cvt.u64.u32 {d_}, {r1};")
-        a(f"or.b64 {d_}, {d_}, {hi};")
-        return d_
-
-    def item_stage(item):
-        """(stage base address, full barrier, empty barrier) of ring item ``item``."""
-        st_, fbr, ebr = a.r(), a.r(), a.r()
-        a(f"rem.u32 {st_}, {item}, {STAGES};")
-        a(f"mad.lo.u32 {fbr}, {st_}, 8, {bars};")
-        a(f"add.u32 {ebr}, {fbr}, {EMPTY};")
-        a(f"add.u32 {fbr}, {fbr}, {FULL};")
-        sb = a.r()
-        a(f"mad.lo.u32 {sb}, {st_}, {TILE_BYTES}, {sKV};")
-        return sb, fbr, ebr
-
-    def item_wait(item):
-        sb, fbr, ebr = item_stage(item)
-        par_ = a.r()
-        a(f"div.u32 {par_}, {item}, {STAGES};")
-        a(f"and.b32 {par_}, {par_}, 1;")
-        wait_bar(a, fbr, par_, err, ERR_MMA, l_mdone)
+    # ---------------- MMA issuers ---------------------------------------------------------------
+    # one issuing thread per query tile (warp 1: tile 0, warp 2: tile 1).  The tensor core's
+    # instruction queue is shallow, so while one issuer waits for its P or does its bookkeeping the
+    # other's MMAs keep the tensor core busy; each ring stage is released when both issuers' MMAs
+    # that read it have completed (empty barriers count two arrivals).
+    def issuer(i, l_label):
+        a.label(l_label)
+        pl = a.r("p")
+        a(f"setp.ne.u32 {pl}, {lane}, 0;")
+        a(f"@{pl} bra {l_end};")
+        l_mdone = a.L(f"mdone{i}")
+        qb2, zero2 = a.r(), a.r()
+        a(f"add.u32 {qb2}, {bars}, {QFULL};")
+        a(f"mov.u32 {zero2}, 0;")
+        wait_bar(a, qb2, zero2, err, ERR_MMA, l_mdone)
         a("tcgen05.fence::after_thread_sync;")
-        return sb, ebr
+        iqk, ipv = a.r(), a.r()
+        a(f"mov.u32 {iqk}, {idesc_qk};")
+        a(f"mov.u32 {ipv}, {idesc_pv};")
+        ptrue, pfalse = a.r("p"), a.r("p")
+        a(f"setp.eq.u32 {ptrue}, {lane}, {lane};")
+        a(f"setp.ne.u32 {pfalse}, {lane}, {lane};")
+        khi, vhi = a.r("rd"), a.r("rd")
+        a(f"mov.b64 {khi}, {kdesc_hi};")
+        a(f"mov.b64 {vhi}, {vdesc_hi};")
+        lasti = a.r()                                      # this tile's last kv block
+        a(f"sub.u32 {lasti}, {nb}, {(3 if causal else 1) if i == 0 else 1};")
 
-    def qk(i, kbase, jreg):
-        """S_i = Q_i K^T for the K block at ``kbase``.  Issued after PV_i of the previous block, which
-        read P_i from the same TMEM columns; the tensor core runs one thread's MMAs in order."""
-        dcol = a.r()
-        a(f"add.u32 {dcol}, {taddr}, {BKV * i};")
-        qbase = a.r()
-        a(f"add.u32 {qbase}, {sQ}, {TILE_BYTES * i};")
-        for k in range(D // 16):
-            off = (k // 4) * HALF + (k % 4) * 32
-            da = desc(qbase, off, khi)
-            db = desc(kbase, off, khi)
-            a(f"tcgen05.mma.cta_group::1.kind::f16 [{dcol}], {da}, {db}, {iqk}, {ptrue if k else pfalse};")
-        sfull = a.r()
-        a(f"add.u32 {sfull}, {bars}, {SFULL + 8 * i};")
-        a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{sfull}];")
+        def base_desc(addr_reg, hi):
+            """The shared-memory matrix descriptor of ``addr_reg``; a byte offset ``off`` within the
+            same operand is the descriptor plus off >> 4 (the start-address field holds addr >> 4)."""
+            r1 = a.r()
+            d_ = a.r("rd")
+            a(f"shr.u32 {r1}, {addr_reg}, 4;")
+            a(f"cvt.u64.u32 {d_}, {r1};")
+            a(f"or.b64 {d_}, {d_}, {hi};")
+            return d_
 
-    def pv(i, vbase, jreg):
-        """O_i += P_i V for the V block at ``vbase`` (P_i in TMEM: hi part in S_i's columns 0-63, lo
-        part in 64-127, two bf16 per column), once the softmax has written P_i."""
-        pfb, par_ = a.r(), a.r()
-        a(f"add.u32 {pfb}, {bars}, {PFULL + 8 * i};")
-        a(f"and.b32 {par_}, {jreg}, 1;")
-        wait_bar(a, pfb, par_, err, ERR_MMA, l_mdone)
-        a("tcgen05.fence::after_thread_sync;")
-        dcol = a.r()
-        a(f"add.u32 {dcol}, {taddr}, {2 * BKV + D * i};")
-        for part in range(2 if precise else 1):
-            for k in range(BKV // 16):
-                at = a.r()
-                a(f"add.u32 {at}, {taddr}, {BKV * i + 64 * part + 8 * k};")
-                db = desc(vbase, 2048 * k, vhi)
-                if k == 0 and part == 0:
-                    pacc = a.r("p")
-                    a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
-                else:
-                    pacc = ptrue
-                a(f"tcgen05.mma.cta_group::1.kind::f16 [{dcol}], [{at}], {db}, {ipv}, {pacc};")
-        pfree = a.r()
-        a(f"add.u32 {pfree}, {bars}, {PFREE + 8 * i};")
-        a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{pfree}];")
+        def plus(d0, off):
+            if not off:
+                return d0
+            d_ = a.r("rd")
+            a(f"add.s64 {d_}, {d0}, {off >> 4};")
+            return d_
 
-    def commit(bar_reg):
-        a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{bar_reg}];")
+        # the Q operand never changes: its 8 descriptors once; every ring stage's descriptors, the
+        # S/O TMEM columns and the barrier offsets are fixed, and the issue loop is unrolled over the
+        # 8 ring stages (4 kv blocks), so each MMA costs at most one add
+        qb_i = a.r()
+        a(f"add.u32 {qb_i}, {sQ}, {Q_BYTES * i};")
+        q0 = base_desc(qb_i, khi)
+        qdesc = [plus(q0, (k // 4) * Q_HALF + (k % 4) * 32) for k in range(D // 16)]
+        kd, vd = [], []
+        for st_ in range(STAGES):
+            sb = a.r()
+            a(f"add.u32 {sb}, {sKV}, {st_ * KV_BYTES};")
+            kd.append(base_desc(sb, khi))
+            vd.append(base_desc(sb, vhi))
+        scol_c = [a.r() for _ in range(2)]
+        ocol_c = a.r()
+        a(f"add.u32 {ocol_c}, {taddr}, {D * i};")
+        for b_ in range(2):
+            a(f"add.u32 {scol_c[b_]}, {taddr}, {S_COL0 + 2 * BKV * i + BKV * b_};")
 
-    # prologue: S_0(0), S_1(0) from K_0 (ring item 0)
-    j = a.r()
-    item0 = a.r()
-    a(f"mov.u32 {j}, 0;")
-    a(f"mov.u32 {item0}, 0;")
-    kb0, ke0 = item_wait(item0)
-    qk(0, kb0, j)
-    qk(1, kb0, j)
-    commit(ke0)
-    l_mj, l_mjend = a.L("mj"), a.L("mjend")
-    a.label(l_mj)
-    itv = a.r()
-    a(f"shl.b32 {itv}, {j}, 1;")
-    a(f"add.u32 {itv}, {itv}, 1;")                          # V_j is ring item 2j+1
-    vb, ve = item_wait(itv)
-    jn = a.r()
-    a(f"add.u32 {jn}, {j}, 1;")
-    have_next = a.r("p")
-    a(f"setp.lt.u32 {have_next}, {jn}, {nb};")
-    l_pv0 = a.L("nopv0")
-    p0j = a.r("p")
-    a(f"setp.gt.u32 {p0j}, {j}, {last0};")
-    a(f"@{p0j} bra {l_pv0};")
-    pv(0, vb, j)
-    a.label(l_pv0)
-    l_nok = a.L("nok")
-    a(f"@!{have_next} bra {l_nok};")
-    itk = a.r()
-    a(f"shl.b32 {itk}, {jn}, 1;")                           # K_{j+1} is ring item 2j+2
-    kb_, ke_ = item_wait(itk)
-    l_qk0 = a.L("noqk0")
-    p0n = a.r("p")
-    a(f"setp.gt.u32 {p0n}, {jn}, {last0};")
-    a(f"@{p0n} bra {l_qk0};")
-    qk(0, kb_, jn)
-    a.label(l_qk0)
-    pv(1, vb, j)
-    commit(ve)
-    qk(1, kb_, jn)
-    commit(ke_)
-    a(f"mov.u32 {j}, {jn};")
-    a(f"bra {l_mj};")
-    a.label(l_nok)
-    pv(1, vb, j)                                           # last block: no K_{j+1}
-    commit(ve)
-    a.label(l_mjend)
-    a.label(l_mdone)
-    a(f"bra {l_end};")
+        def ring_wait(stage_c, par):
+            wait_bar(a, f"{bars}+{FULL + 8 * stage_c}", par, err, ERR_MMA, l_mdone)
+            a("tcgen05.fence::after_thread_sync;")
+
+        def qk(stage_c, buf_c):
+            """S_i(j) = Q_i K_j^T into S_i[j & 1] (K_j in ring stage ``stage_c``); the buffer's previous
+            P (block j-2) was read by a PV issued earlier from this thread, and the tensor core runs
+            one thread's MMAs in order."""
+            for k in range(D // 16):
+                db = plus(kd[stage_c], (k // 4) * KV_HALF + (k % 4) * 32)
+                a(f"tcgen05.mma.cta_group::1.kind::f16 [{scol_c[buf_c]}], {qdesc[k]}, {db}, {iqk}, "
+                  f"{ptrue if k else pfalse};")
+            a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bars}+{SFULL + 16 * i + 8 * buf_c}];")
+
+        def pv(stage_c, buf_c, u, jreg):
+            """O_i += P_i(j) V_j (V_j in ring stage ``stage_c``) once the softmax has written P_i(j)
+            over S_i[j & 1] (hi part in the buffer's columns 0-31, lo part in 32-63, two bf16 per
+            column).  The P-full barrier of a buffer completes once per use, so block j = 4g + u
+            waits for phase j >> 1, whose parity is (u >> 1) & 1."""
+            vds = [plus(vd[stage_c], 2048 * k) for k in range(BKV // 16)]
+            pacc = a.r("p")
+            a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
+            wait_bar(a, f"{bars}+{PFULL + 16 * i + 8 * buf_c}", str((u >> 1) & 1), err, ERR_MMA, l_mdone)
+            stamp(4 + 2 * i, jreg)
+            a("tcgen05.fence::after_thread_sync;")
+            for part in range(2 if precise else 1):
+                for k in range(BKV // 16):
+                    acc = pacc if (k == 0 and part == 0) else ptrue
+                    a(f"tcgen05.mma.cta_group::1.kind::f16 [{ocol_c}], [{scol_c[buf_c]}+{(BKV // 2) * part + 8 * k}], "
+                      f"{vds[k]}, {ipv}, {acc};")
+            a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bars}+{PFREE + 16 * i + 8 * buf_c}];")
+            stamp(5 + 2 * i, jreg)
+
+        def release(stage_c, used):
+            """This issuer's arrival on the stage's empty barrier: after its MMAs that read the stage
+            complete, or at once (``used`` False) for a block this tile does not compute."""
+            if used:
+                a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+                  f"[{bars}+{EMPTY + 8 * stage_c}];")
+            else:
+                a(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{EMPTY + 8 * stage_c}];")
+
+        # prologue: S_i(0) from K_0 (ring item 0, stage 0)
+        j, gp, gpn = a.r(), a.r(), a.r()
+        a(f"mov.u32 {j}, 0;")
+        a(f"mov.u32 {gp}, 0;")
+        ring_wait(0, gp)
+        qk(0, 0)
+        release(0, True)
+        l_mg = a.L(f"mg{i}")
+        a.label(l_mg)
+        a(f"xor.b32 {gpn}, {gp}, 1;")
+        for u in range(4):                                 # block j = 4g + u
+            if i == 0:
+                stamp(0, j)
+            # scores of the next block first (K_{j+1} = item 2j+2, stage 2u+2 mod 8), so the softmax
+            # of block j+1 can start as soon as block j's ends
+            have_next = a.r("p")
+            jn = a.r()
+            a(f"add.u32 {jn}, {j}, 1;")
+            a(f"setp.lt.u32 {have_next}, {jn}, {nb};")
+            l_nok = a.L("nok")
+            a(f"@!{have_next} bra {l_nok};")
+            ks = (2 * u + 2) % STAGES
+            ring_wait(ks, gpn if u == 3 else gp)
+            if i == 0:
+                stamp(1, j)
+            l_qk, l_qkd = a.L("noqk"), a.L("qkd")
+            pn_ = a.r("p")
+            a(f"setp.gt.u32 {pn_}, {jn}, {lasti};")
+            a(f"@{pn_} bra {l_qk};")
+            qk(ks, (u + 1) & 1)
+            release(ks, True)
+            a(f"bra {l_qkd};")
+            a.label(l_qk)
+            release(ks, False)
+            a.label(l_qkd)
+            if i == 0:
+                stamp(2, j)
+            a.label(l_nok)
+            vs = 2 * u + 1                                 # V_j = item 2j+1
+            ring_wait(vs, gp)
+            if i == 0:
+                stamp(3, j)
+            l_pv, l_pvd = a.L("nopv"), a.L("pvd")
+            pj_ = a.r("p")
+            a(f"setp.gt.u32 {pj_}, {j}, {lasti};")
+            a(f"@{pj_} bra {l_pv};")
+            pv(vs, u & 1, u, j)
+            release(vs, True)
+            a(f"bra {l_pvd};")
+            a.label(l_pv)
+            release(vs, False)
+            a.label(l_pvd)
+            a(f"@!{have_next} bra {l_mdone};")
+            a(f"mov.u32 {j}, {jn};")
+        a(f"mov.u32 {gp}, {gpn};")
+        a(f"bra {l_mg};")
+        a.label(l_mdone)
+        a(f"bra {l_end};")
+
+    issuer(0, l_mma)
+    issuer(1, l_mma1)
 
     # ---------------- softmax warps ------------------------------------------------------------
     a.label(l_soft)
@@ -382,50 +468,91 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     lanebase = a.r()
     a(f"shl.b32 {lanebase}, {q}, 21;")
     a(f"add.u32 {lanebase}, {lanebase}, {taddr};")
-    scol, ocol = a.r(), a.r()
-    a(f"mad.lo.u32 {scol}, {ti}, {BKV}, {lanebase};")
+    scol0, ocol = a.r(), a.r()
+    a(f"mad.lo.u32 {scol0}, {ti}, {2 * BKV}, {lanebase};")
+    a(f"add.u32 {scol0}, {scol0}, {S_COL0};")              # S_ti[0]; S_ti[1] is BKV columns on
     a(f"mad.lo.u32 {ocol}, {ti}, {D}, {lanebase};")
-    a(f"add.u32 {ocol}, {ocol}, {2 * BKV};")
-    last = a.r()
+    last, grow0 = a.r(), a.r()
     if causal:
-        a(f"shl.b32 {last}, {t}, 1;")
-        a(f"add.u32 {last}, {last}, {ti};")                # tile i's last (diagonal) kv block
+        a(f"shl.b32 {last}, {t}, 2;")
+        a(f"mad.lo.u32 {last}, {ti}, 2, {last};")
+        a(f"add.u32 {last}, {last}, 1;")                   # tile i's last kv block: 4t + 2i + 1
     else:
         a(f"sub.u32 {last}, {nb}, 1;")
-    sfb, pfb, pfr = a.r(), a.r(), a.r()
-    a(f"mad.lo.u32 {sfb}, {ti}, 8, {bars};")
-    a(f"add.u32 {pfb}, {sfb}, {PFULL};")
-    a(f"add.u32 {pfr}, {sfb}, {PFREE};")
-    a(f"add.u32 {sfb}, {sfb}, {SFULL};")
+    a(f"mad.lo.u32 {grow0}, {ti}, {BQ}, {row0};")
+    a(f"add.u32 {grow0}, {grow0}, {rowl};")                # this thread's query row
+    sfb0, pfb0, pfr0 = a.r(), a.r(), a.r()
+    a(f"mad.lo.u32 {sfb0}, {ti}, 16, {bars};")
+    a(f"add.u32 {pfb0}, {sfb0}, {PFULL};")
+    a(f"add.u32 {pfr0}, {sfb0}, {PFREE};")
+    a(f"add.u32 {sfb0}, {sfb0}, {SFULL};")
+
+    def pv_done(blk, bail, code):
+        """Wait until PV_ti(blk) has completed (its buffer's PV-done barrier, phase blk >> 1)."""
+        bb_, br_, pr_ = a.r(), a.r(), a.r()
+        a(f"and.b32 {bb_}, {blk}, 1;")
+        a(f"mad.lo.u32 {br_}, {bb_}, 8, {pfr0};")
+        a(f"shr.u32 {pr_}, {blk}, 1;")
+        a(f"and.b32 {pr_}, {pr_}, 1;")
+        wait_bar_warp(a, br_, pr_, err, code, bail)
+    ple = a.r("p")
+    a(f"setp.eq.u32 {ple}, {lane}, 0;")
+    ev_s, ptw = None, None
+    if trace:
+        ev_s = a.r()
+        a(f"mad.lo.u32 {ev_s}, {ti}, 6, 8;")
+        ptw = a.r("p")
+        a(f"setp.eq.u32 {ptw}, {rowl}, 0;")
     s_ = [a.r("f") for _ in range(BKV)]
     mref, lsum, jj = a.r("f"), a.r("f"), a.r()
     a(f"mov.b32 {mref}, 0fFF800000;")
     a(f"mov.b32 {lsum}, 0f00000000;")
     a(f"mov.u32 {jj}, 0;")
+
+    def sstamp(k):
+        """Softmax timeline stamp ``k`` (0 S ready, 1 S loaded, 2 row max, 3 P stores issued,
+        4 P written) for this tile, from the tile's first thread."""
+        if not trace:
+            return
+        ev = a.r()
+        a(f"add.u32 {ev}, {ev_s}, {k};")
+        stamp(ev, jj, ptw)
+
     l_sj, l_sdone = a.L("sj"), a.L("sdone")
     a.label(l_sj)
     pj = a.r("p")
     a(f"setp.gt.u32 {pj}, {jj}, {last};")
     a(f"@{pj} bra {l_sdone};")
-    par_s = a.r()
-    a(f"and.b32 {par_s}, {jj}, 1;")
+    bsel, sfb, pfb, par_s, scol = a.r(), a.r(), a.r(), a.r(), a.r()
+    a(f"and.b32 {bsel}, {jj}, 1;")
+    a(f"mad.lo.u32 {sfb}, {bsel}, 8, {sfb0};")
+    a(f"mad.lo.u32 {pfb}, {bsel}, 8, {pfb0};")
+    a(f"shr.u32 {par_s}, {jj}, 1;")
+    a(f"and.b32 {par_s}, {par_s}, 1;")
+    a(f"mad.lo.u32 {scol}, {bsel}, {BKV}, {scol0};")
     wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_sdone)
+    sstamp(0)
     a("tcgen05.fence::after_thread_sync;")
     for c in range(BKV // 32):
         src = a.r()
         a(f"add.u32 {src}, {scol}, {32 * c};")
         a(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(s_[32 * c:32 * c + 32])}}}, [{src}];")
     a("tcgen05.wait::ld.sync.aligned;")
-    ple = a.r("p")
-    a(f"setp.eq.u32 {ple}, {lane}, 0;")
+    sstamp(1)
     if causal:
+        # kv = 64*jj + c is masked when kv > query row, i.e. c > grow0 - 64*jj; only the blocks that
+        # reach the diagonal (the tile's last two) have masked columns
         l_nomask = a.L("nomask")
-        pdiag = a.r("p")
-        a(f"setp.ne.u32 {pdiag}, {jj}, {last};")
-        a(f"@{pdiag} bra {l_nomask};")
+        lim, kv0 = a.r(), a.r()
+        a(f"shl.b32 {kv0}, {jj}, 6;")
+        a(f"sub.s32 {lim}, {grow0}, {kv0};")
+        pnm, vnm = a.r("p"), a.r("p")
+        a(f"setp.ge.s32 {pnm}, {lim}, {BKV - 1};")
+        a(f"vote.sync.all.pred {vnm}, {pnm}, -1;")
+        a(f"@{vnm} bra {l_nomask};")
         for c in range(BKV):
             pm = a.r("p")
-            a(f"setp.lt.u32 {pm}, {rowl}, {c};")
+            a(f"setp.lt.s32 {pm}, {lim}, {c};")
             a(f"@{pm} mov.b32 {s_[c]}, 0fFF800000;")
         a.label(l_nomask)
     # row max (tree), in the scaled log2 domain
@@ -443,20 +570,16 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     mblk, mnew = a.r("f"), a.r("f")
     a(f"mul.f32 {mblk}, {lvl[0]}, {cscale};")
     a(f"max.f32 {mnew}, {mref}, {mblk};")
-    l_first, l_after = a.L("first"), a.L("after")
+    sstamp(2)
     # alpha (the O rescale factor) is 1 unless this block raises the running max past the
-    # threshold; it is written on both paths so every later read has a definition
+    # threshold; it is written on every path so every later read has a definition
     alpha = a.r("f")
     a(f"mov.b32 {alpha}, 0f3F800000;")
+    l_first, l_after = a.L("first"), a.L("after")
+    need, anyneed = a.r("p"), a.r("p")
     pfirst = a.r("p")
     a(f"setp.eq.u32 {pfirst}, {jj}, 0;")
     a(f"@{pfirst} bra {l_first};")
-    # later blocks: O_i and P_i are free once the previous PV has completed
-    par_p = a.r()
-    a(f"sub.u32 {par_p}, {jj}, 1;")
-    a(f"and.b32 {par_p}, {par_p}, 1;")
-    wait_bar_warp(a, pfr, par_p, err, ERR_SOFTMAX, l_sdone)
-    need, anyneed = a.r("p"), a.r("p")
     thr = a.r("f")
     a(f"add.f32 {thr}, {mref}, {_f32(RESCALE_THRESHOLD)};")
     a(f"setp.gt.f32 {need}, {mnew}, {thr};")
@@ -474,51 +597,56 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mov.b32 {mref}, {mnew};")
     a(f"setp.ne.u32 {anyneed}, {lane}, {lane};")
     a.label(l_after)
-    # p = 2^(s*c - m), row sum, and P back into S_i's TMEM columns as bf16 pairs (hi, then lo)
+    # p = 2^(s*c - m), row sum, and P back over S's TMEM columns as bf16 pairs (hi, then lo)
     negm = a.r("f")
     a(f"neg.f32 {negm}, {mref};")
     parts = [a.r("f") for _ in range(4)]
     for pp in parts:
         a(f"mov.b32 {pp}, 0f00000000;")
-    for c16 in range(BKV // 32):                        # 32 values -> 16 packed columns per part
-        hi_w, lo_w = [], []
-        for k in range(16):
-            i0, i1 = 32 * c16 + 2 * k, 32 * c16 + 2 * k + 1
-            for idx in (i0, i1):
-                a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
-                a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
-                a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {s_[idx]};")
-            w = a.r()
-            a(f"cvt.rn.bf16x2.f32 {w}, {s_[i1]}, {s_[i0]};")
-            hi_w.append(w)
-            if precise:
-                h0, h1, r0, r1, wl = a.r("f"), a.r("f"), a.r("f"), a.r("f"), a.r()
-                a(f"shl.b32 {h0}, {w}, 16;")
-                a(f"and.b32 {h1}, {w}, -65536;")
-                a(f"sub.f32 {r0}, {s_[i0]}, {h0};")
-                a(f"sub.f32 {r1}, {s_[i1]}, {h1};")
-                a(f"cvt.rn.bf16x2.f32 {wl}, {r1}, {r0};")
-                lo_w.append(wl)
-        dst = a.r()
-        a(f"add.u32 {dst}, {scol}, {16 * c16};")
-        a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dst}], {{{', '.join(hi_w)}}};")
+    hi_w, lo_w = [], []
+    for k in range(BKV // 2):
+        i0, i1 = 2 * k, 2 * k + 1
+        for idx in (i0, i1):
+            a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
+            a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
+            a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {s_[idx]};")
+        w = a.r()
         if precise:
-            dst2 = a.r()
-            a(f"add.u32 {dst2}, {scol}, {64 + 16 * c16};")
-            a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dst2}], {{{', '.join(lo_w)}}};")
+            # hi = the top 16 bits of p (prmt packs two top halves into one word); lo = the top
+            # 16 bits of the exact remainder p - hi
+            h0, h1, wl = a.r("f"), a.r("f"), a.r()
+            a(f"prmt.b32 {w}, {s_[i0]}, {s_[i1]}, 0x7632;")
+            a(f"and.b32 {h0}, {s_[i0]}, -65536;")
+            a(f"and.b32 {h1}, {s_[i1]}, -65536;")
+            a(f"sub.f32 {h0}, {s_[i0]}, {h0};")
+            a(f"sub.f32 {h1}, {s_[i1]}, {h1};")
+            a(f"prmt.b32 {wl}, {h0}, {h1}, 0x7632;")
+            lo_w.append(wl)
+        else:
+            a(f"cvt.rn.bf16x2.f32 {w}, {s_[i1]}, {s_[i0]};")
+        hi_w.append(w)
+    a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{scol}], {{{', '.join(hi_w)}}};")
+    if precise:
+        dst2 = a.r()
+        a(f"add.u32 {dst2}, {scol}, {BKV // 2};")
+        a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{dst2}], {{{', '.join(lo_w)}}};")
+    sstamp(3)
     p01, p23 = a.r("f"), a.r("f")
     a(f"add.f32 {p01}, {parts[0]}, {parts[1]};")
     a(f"add.f32 {p23}, {parts[2]}, {parts[3]};")
     a(f"add.f32 {p01}, {p01}, {p23};")
     a(f"add.f32 {lsum}, {lsum}, {p01};")
-    # the lazy O rescale (the previous PV has completed: waited above)
+    # the lazy O rescale, once the previous PV into O has completed
     l_norescale2 = a.L("norescale2")
     a(f"@!{anyneed} bra {l_norescale2};")
+    prev = a.r()
+    a(f"sub.u32 {prev}, {jj}, 1;")
+    pv_done(prev, l_sdone, ERR_SOFTMAX)
     a("tcgen05.fence::after_thread_sync;")
     for c in range(D // 32):
         src = a.r()
         a(f"add.u32 {src}, {ocol}, {32 * c};")
-        regs = s_[32 * c:32 * c + 32]
+        regs = s_[:32]
         a(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{src}];")
         a("tcgen05.wait::ld.sync.aligned;")
         for r_ in regs:
@@ -528,6 +656,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a("tcgen05.wait::st.sync.aligned;")
     a("tcgen05.fence::before_thread_sync;")
     a("bar.warp.sync -1;")
+    sstamp(4)
     a(f"@{ple} mbarrier.arrive.shared::cta.b64 _, [{pfb}];")
     a(f"add.u32 {jj}, {jj}, 1;")
     a(f"bra {l_sj};")
@@ -537,22 +666,18 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     pok = a.r("p")
     a(f"setp.le.u32 {pok}, {jj}, {last};")                  # left early (time-out): no store
     a(f"@{pok} bra {l_noepi};")
-    par_e = a.r()
-    a(f"and.b32 {par_e}, {last}, 1;")
-    wait_bar_warp(a, pfr, par_e, err, ERR_EPILOGUE, l_noepi)
+    pv_done(last, l_noepi, ERR_EPILOGUE)                    # the last PV, and so every earlier one
     a("tcgen05.fence::after_thread_sync;")
     inv = a.r("f")
     a(f"rcp.rn.f32 {inv}, {lsum};")
     grow, oaddr = a.r(), a.r("rd")
-    a(f"mad.lo.u32 {grow}, {ti}, {BQ}, {row0};")
-    a(f"add.u32 {grow}, {grow}, {rowl};")
-    a(f"mad.lo.u32 {grow}, {bh}, {seq}, {grow};")          # row of O in [batch*heads*S, D]
+    a(f"mad.lo.u32 {grow}, {bh}, {seq}, {grow0};")         # row of O in [batch*heads*S, D]
     a(f"mul.wide.u32 {oaddr}, {grow}, {D * 2};")
     a(f"add.s64 {oaddr}, {oaddr}, {o_ptr};")
     for c in range(D // 32):
         src = a.r()
         a(f"add.u32 {src}, {ocol}, {32 * c};")
-        regs = s_[32 * c:32 * c + 32]
+        regs = s_[:32]
         a(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{src}];")
         a("tcgen05.wait::ld.sync.aligned;")
         words = []
@@ -570,28 +695,48 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a.label(l_end)
     a("barrier.sync 0;")
     a("bar.warp.sync -1;")
+    if trace:
+        pt1 = a.r("p")
+        a(f"setp.eq.u32 {pt1}, {tid}, 0;")
+        stamp(1, TRACE_SLOTS - 1, pt1)
     l_nodealloc = a.L("nodealloc")
     a(f"@!{pw1} bra {l_nodealloc};")
     a("tcgen05.fence::after_thread_sync;")
     a(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {taddr}, {TMEM_COLS};")
     a.label(l_nodealloc)
 
-    dyn = TILES * TILE_BYTES + STAGES * TILE_BYTES + 256 + 1024
-    entry = [f".visible .entry {name}(",
-             "\t.param .u64 p_Q,", "\t.param .u64 p_K,", "\t.param .u64 p_V,", "\t.param .u64 p_O,",
-             "\t.param .align 64 .b8 p_tmQ[128],", "\t.param .align 64 .b8 p_tmK[128],",
-             "\t.param .align 64 .b8 p_tmV[128],", "\t.param .u64 p_err", ")",
-             f".reqntid {THREADS}, 1, 1", ".maxnreg 168", "{"]
+    dyn = TILES * Q_BYTES + STAGES * KV_BYTES + BAR_BYTES + 1024
+    params = ["\t.param .u64 p_Q,", "\t.param .u64 p_K,", "\t.param .u64 p_V,", "\t.param .u64 p_O,",
+              "\t.param .align 64 .b8 p_tmQ[128],", "\t.param .align 64 .b8 p_tmK[128],",
+              "\t.param .align 64 .b8 p_tmV[128],", "\t.param .u64 p_err" + ("," if trace else "")]
+    if trace:
+        params.append("\t.param .u64 p_trace")
+    entry = [f".visible .entry {name}("] + params + [")", f".reqntid {THREADS}, 1, 1", ".maxnreg 168", "{"]
     entry += a.decls() + a.lines + ["\tret;", "}"]
     qn, kn, vn, on = names
     dims = [D, seq, heads, batch]
     strides = [D * 2, seq * D * 2, heads * seq * D * 2]
-    tmaps = [{"name": f"tm{x}", "tensor": nm, "dtype": "bf16", "dims": dims, "strides": strides,
-              "box": [64, 128, 1, 1], "swizzle": "128B"} for x, nm in (("Q", qn), ("K", kn), ("V", vn))]
+    tmaps = [{"name": "tmQ", "tensor": qn, "dtype": "bf16", "dims": dims, "strides": strides,
+              "box": [64, BQ, 1, 1], "swizzle": "128B"}]
+    tmaps += [{"name": f"tm{x}", "tensor": nm, "dtype": "bf16", "dims": dims, "strides": strides,
+               "box": [64, BKV, 1, 1], "swizzle": "128B"} for x, nm in (("K", kn), ("V", vn))]
+    extra = [{"name": "__err", "kind": "errword"}]
+    if trace:
+        extra.append({"name": "__trace", "kind": "buffer"})
     return {
         "name": name, "kind": "tcgen05_attention", "params": [qn, kn, vn, on],
         "raw_entry": entry, "raw_decls": [f".extern .shared .align 1024 .b8 {smem_sym}[];"],
         "grid": [grid, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": dyn,
         "align": {qn: 16, kn: 16, vn: 16, on: 32}, "zero_outputs": [], "tmaps": tmaps,
-        "extra": [{"name": "__err", "kind": "errword"}],
+        "extra": extra,
     }
+
+
+def trace_events(buf, grid: int):
+    """Split a ``trace`` buffer (u64 [grid, 66, 24]) into per-CTA timelines.  For kv block j, events
+    0-7 are the MMA thread's iteration start, K_(j+1) arrived, S(j+1) issued, V_j arrived, P_0(j)
+    ready, PV_0 issued, P_1(j) ready and PV_1 issued; 8-12 (tile 0) and 14-18 (tile 1) are the
+    softmax's S(j) ready, S loaded, row max, P stores issued and P(j) written.  Row 65 holds CTA
+    start, end and the SM id."""
+    import numpy as np
+    return np.asarray(buf, dtype=np.uint64).reshape(grid, TRACE_SLOTS, TRACE_EVENTS)

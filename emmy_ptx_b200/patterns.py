@@ -333,5 +333,7 @@ def try_lower(graph, node, kmeta, prefix, options):
         if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES):
             return None
         return tc_attention.attention_entry(node.op.name, bt, hd, seq, causal, scale,
-                                            names=(Q.name, K.name, V.name, O.name), prefix=prefix)
+                                            names=(Q.name, K.name, V.name, O.name), prefix=prefix,
+                                            precise=bool(options.get("attn_precise", True)),
+                                            trace=bool(options.get("attn_trace", False)))
     return None
