@@ -13,12 +13,14 @@ WAIT_LIMIT = 40000               # bounded polls of try_wait with a 0.1 ms hint:
 WAIT_HINT_NS = 100000
 
 
-def idesc_f16(m: int, n: int, a_mn_major: bool, b_mn_major: bool) -> int:
-    """tcgen05 instruction descriptor, kind::f16, bf16 x bf16 -> f32."""
+def idesc_f16(m: int, n: int, a_mn_major: bool, b_mn_major: bool, half: bool = False) -> int:
+    """tcgen05 instruction descriptor, kind::f16, bf16 x bf16 -> f32 (f16 x f16 -> f32 with ``half``;
+    the two operands always have the same type)."""
+    fmt = 0 if half else 1       # A / B format: 0 f16, 1 bf16
     d = 0
     d |= 1 << 4                  # D format: f32
-    d |= 1 << 7                  # A format: bf16
-    d |= 1 << 10                 # B format: bf16
+    d |= fmt << 7                # A format
+    d |= fmt << 10               # B format
     d |= (1 if a_mn_major else 0) << 15
     d |= (1 if b_mn_major else 0) << 16
     d |= (n >> 3) << 17

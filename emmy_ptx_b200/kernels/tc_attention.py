@@ -43,8 +43,10 @@ Q_BYTES = BQ * D * 2             # 32 KiB: one Q tile
 Q_HALF = Q_BYTES // 2            # one 64-column TMA box of a Q tile
 KV_BYTES = BKV * D * 2           # 16 KiB: one K or V block
 KV_HALF = KV_BYTES // 2          # one 64-column TMA box of a K/V block
-THREADS = 384
+THREADS = 384                    # warps 0-11; with the f16 path, warps 12-15 convert V (512 threads)
+CONV_WARPS = 4
 TMEM_COLS = 512
+F16_MAX_BF16_BITS = 0x477F       # the largest bf16 magnitude (65280) below the f16 overflow threshold
 S_COL0 = TILES * D               # S_i[b] at S_COL0 + 2*BKV*i + BKV*b
 LOG2E = 1.4426950408889634
 RESCALE_THRESHOLD = 8.0          # log2 units: rescale O only when the max grew by more than 2^8
@@ -63,7 +65,11 @@ SFULL = EMPTY + 8 * STAGES
 PFULL = SFULL + 8 * 2 * TILES
 PFREE = PFULL + 8 * 2 * TILES
 SLOT = PFREE + 8 * 2 * TILES
-BAR_BYTES = 256
+VCONV = SLOT + 8                 # per V ring stage (stages 1, 3, 5, 7): block's V converted
+CSYNC = VCONV + 8 * 4            # per V ring stage: the converter warps' overflow votes are in
+FMT = CSYNC + 8 * 4              # per V ring stage: 1 when V and P are f16 for that block
+OVF = FMT + 4 * 4                # per V ring stage: overflow votes, bit = phase parity of the use
+BAR_BYTES = 512
 
 TRACE_SLOTS = 66                 # per-CTA trace rows: kv blocks 0..64, then one row of CTA facts
 TRACE_EVENTS = 24
@@ -76,18 +82,21 @@ def _f32(v: float) -> str:
 
 def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, scale: float,
                     names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True,
-                    trace: bool = False) -> dict:
+                    trace: bool = False, half: bool = True) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`)."""
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     if trace and seq // BKV + 1 >= TRACE_SLOTS:
         raise ValueError("trace supports at most 64 key/value blocks")
+    half = half and precise
+    threads = THREADS + (32 * CONV_WARPS if half else 0)
     nt = seq // (BQ * TILES)
     grid = batch * heads * nt
     a = Asm()
     idesc_qk = idesc_f16(BQ, BKV, False, False)
     idesc_pv = idesc_f16(BQ, D, False, True)
+    idesc_pv16 = idesc_f16(BQ, D, False, True, half=True)
     kdesc_hi = smem_desc_hi(16, 1024)            # K-major SW128 (Q, K): 8-row groups 1 KiB apart
     vdesc_hi = smem_desc_hi(KV_HALF, 1024)       # MN-major SW128 (V): 64-column atoms 8 KiB apart
     cscale = _f32(scale * LOG2E)
@@ -170,6 +179,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"mbarrier.init.shared::cta.b64 [{bars}+{SFULL + 8 * (2 * i + b_)}], 1;")
             a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFULL + 8 * (2 * i + b_)}], 4;")
             a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFREE + 8 * (2 * i + b_)}], 1;")
+    if half:
+        for u in range(4):
+            a(f"mbarrier.init.shared::cta.b64 [{bars}+{VCONV + 8 * u}], {CONV_WARPS};")
+            a(f"mbarrier.init.shared::cta.b64 [{bars}+{CSYNC + 8 * u}], {CONV_WARPS};")
+            a(f"st.shared.u32 [{bars}+{OVF + 4 * u}], 0;")
     a("fence.mbarrier_init.release.cluster;")
     a("fence.proxy.async.shared::cta;")
     a.label(l_init)
@@ -196,10 +210,14 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"@{pt0} st.global.u64 [{sad}], {sm64};")
 
     l_end = a.L("end")
-    l_prod, l_mma, l_mma1, l_soft = a.L("prod"), a.L("mma"), a.L("mma1"), a.L("soft")
+    l_prod, l_mma, l_mma1, l_soft, l_conv = a.L("prod"), a.L("mma"), a.L("mma1"), a.L("soft"), a.L("conv")
     pw0, pw2, pws = a.r("p"), a.r("p"), a.r("p")
     a(f"setp.eq.u32 {pw0}, {warp}, 0;")
     a(f"setp.eq.u32 {pw2}, {warp}, 2;")
+    if half:
+        pwc = a.r("p")
+        a(f"setp.ge.u32 {pwc}, {warp}, 12;")
+        a(f"@{pwc} bra {l_conv};")
     a(f"setp.ge.u32 {pws}, {warp}, 4;")
     a(f"@{pw0} bra {l_prod};")
     a(f"@{pw1} bra {l_mma};")
@@ -304,9 +322,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"mov.u32 {zero2}, 0;")
         wait_bar(a, qb2, zero2, err, ERR_MMA, l_mdone)
         a("tcgen05.fence::after_thread_sync;")
-        iqk, ipv = a.r(), a.r()
+        iqk, ipv, ipv16 = a.r(), a.r(), a.r()
         a(f"mov.u32 {iqk}, {idesc_qk};")
         a(f"mov.u32 {ipv}, {idesc_pv};")
+        a(f"mov.u32 {ipv16}, {idesc_pv16};")
         ptrue, pfalse = a.r("p"), a.r("p")
         a(f"setp.eq.u32 {ptrue}, {lane}, {lane};")
         a(f"setp.ne.u32 {pfalse}, {lane}, {lane};")
@@ -367,22 +386,42 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bars}+{SFULL + 16 * i + 8 * buf_c}];")
 
-        def pv(stage_c, buf_c, u, jreg):
+        def pv(stage_c, buf_c, u, jreg, gpreg):
             """O_i += P_i(j) V_j (V_j in ring stage ``stage_c``) once the softmax has written P_i(j)
-            over S_i[j & 1] (hi part in the buffer's columns 0-31, lo part in 32-63, two bf16 per
-            column).  The P-full barrier of a buffer completes once per use, so block j = 4g + u
-            waits for phase j >> 1, whose parity is (u >> 1) & 1."""
+            over S_i[j & 1].  The P-full barrier of a buffer completes once per use, so block
+            j = 4g + u waits for phase j >> 1, whose parity is (u >> 1) & 1.
+
+            With the f16 path the block's format flag (set by the V converters) picks the MMAs: f16 P
+            (columns 0-31, two f16 per column) times the converted f16 V in one pass, or, when V_j
+            did not fit f16, bf16 P_hi (columns 0-31) and P_lo (32-63) times the untouched bf16 V."""
             vds = [plus(vd[stage_c], 2048 * k) for k in range(BKV // 16)]
             pacc = a.r("p")
             a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
+            p16 = None
+            if half:
+                wait_bar(a, f"{bars}+{VCONV + 8 * u}", gpreg, err, ERR_MMA, l_mdone)
+                fmt = a.r()
+                p16 = a.r("p")
+                a(f"ld.shared.u32 {fmt}, [{bars}+{FMT + 4 * u}];")
+                a(f"setp.ne.u32 {p16}, {fmt}, 0;")
             wait_bar(a, f"{bars}+{PFULL + 16 * i + 8 * buf_c}", str((u >> 1) & 1), err, ERR_MMA, l_mdone)
             stamp(4 + 2 * i, jreg)
             a("tcgen05.fence::after_thread_sync;")
+            l_bf, l_done = a.L("pvbf"), a.L("pvdone")
+            if half:
+                a(f"@!{p16} bra {l_bf};")
+                for k in range(BKV // 16):
+                    acc = pacc if k == 0 else ptrue
+                    a(f"tcgen05.mma.cta_group::1.kind::f16 [{ocol_c}], [{scol_c[buf_c]}+{8 * k}], "
+                      f"{vds[k]}, {ipv16}, {acc};")
+                a(f"bra {l_done};")
+            a.label(l_bf)
             for part in range(2 if precise else 1):
                 for k in range(BKV // 16):
                     acc = pacc if (k == 0 and part == 0) else ptrue
                     a(f"tcgen05.mma.cta_group::1.kind::f16 [{ocol_c}], [{scol_c[buf_c]}+{(BKV // 2) * part + 8 * k}], "
                       f"{vds[k]}, {ipv}, {acc};")
+            a.label(l_done)
             a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bars}+{PFREE + 16 * i + 8 * buf_c}];")
             stamp(5 + 2 * i, jreg)
@@ -442,7 +481,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             pj_ = a.r("p")
             a(f"setp.gt.u32 {pj_}, {j}, {lasti};")
             a(f"@{pj_} bra {l_pv};")
-            pv(vs, u & 1, u, j)
+            pv(vs, u & 1, u, j, gp)
             release(vs, True)
             a(f"bra {l_pvd};")
             a.label(l_pv)
@@ -457,6 +496,94 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 
     issuer(0, l_mma)
     issuer(1, l_mma1)
+
+    if half:
+        # ---------------- V converters (warps 12-15) ------------------------------------------------
+        # each V block is converted in place from bf16 to f16 (same element size, so the swizzled
+        # layout TMA wrote is kept) unless some |v| exceeds the largest bf16 value below the f16
+        # overflow threshold, in which case the block stays bf16 and its P is written as bf16 hi +
+        # lo.  The warps agree through an overflow word and a barrier with bounded waits.
+        a.label(l_conv)
+        ct, coff, cw, pcl0, pw12 = a.r(), a.r(), a.r(), a.r("p"), a.r("p")
+        a(f"sub.u32 {ct}, {tid}, {THREADS};")                 # 0..127
+        a(f"shl.b32 {coff}, {ct}, 4;")                        # this thread's 16-byte slots: coff + 2048 v
+        a(f"shr.u32 {cw}, {ct}, 5;")
+        a(f"setp.eq.u32 {pcl0}, {lane}, 0;")
+        a(f"setp.eq.u32 {pw12}, {ct}, 0;")
+        l_cdone = a.L("cdone")
+        cj, cgp, cgpn = a.r(), a.r(), a.r()
+        a(f"mov.u32 {cj}, 0;")
+        a(f"mov.u32 {cgp}, 0;")
+        cbase = []
+        for u in range(4):
+            cb = a.r()
+            a(f"add.u32 {cb}, {sKV}, {(2 * u + 1) * KV_BYTES};")
+            a(f"add.u32 {cb}, {cb}, {coff};")
+            cbase.append(cb)
+        l_cg = a.L("cg")
+        a.label(l_cg)
+        a(f"xor.b32 {cgpn}, {cgp}, 1;")
+        for u in range(4):
+            pend_ = a.r("p")
+            a(f"setp.ge.u32 {pend_}, {cj}, {nb};")
+            a(f"@{pend_} bra {l_cdone};")
+            wait_bar_warp(a, f"{bars}+{FULL + 8 * (2 * u + 1)}", cgp, err, ERR_SOFTMAX, l_cdone)
+            m = a.r()
+            a(f"mov.u32 {m}, 0;")
+            conv = []
+            for v in range(KV_BYTES // 16 // 128):
+                ws = [a.r() for _ in range(4)]
+                a(f"ld.shared.v4.b32 {{{', '.join(ws)}}}, [{cbase[u]}+{2048 * v}];")
+                cv = []
+                for w in ws:
+                    t_, lo_, hi_, f_ = a.r(), a.r("f"), a.r("f"), a.r()
+                    a(f"and.b32 {t_}, {w}, 0x7FFF7FFF;")
+                    a(f"max.u16x2 {m}, {m}, {t_};")
+                    a(f"shl.b32 {lo_}, {w}, 16;")
+                    a(f"and.b32 {hi_}, {w}, -65536;")
+                    a(f"cvt.rn.f16x2.f32 {f_}, {hi_}, {lo_};")
+                    cv.append(f_)
+                conv.append(cv)
+            mlo, mhi, po1, po2 = a.r(), a.r(), a.r("p"), a.r("p")
+            a(f"and.b32 {mlo}, {m}, 65535;")
+            a(f"shr.u32 {mhi}, {m}, 16;")
+            a(f"setp.gt.u32 {po1}, {mlo}, {F16_MAX_BF16_BITS};")
+            a(f"setp.gt.u32 {po2}, {mhi}, {F16_MAX_BF16_BITS};")
+            a(f"or.pred {po1}, {po1}, {po2};")
+            vany = a.r("p")
+            a(f"vote.sync.any.pred {vany}, {po1}, -1;")
+            vbit, vreg = a.r(), a.r()
+            a(f"shl.b32 {vbit}, 1, {cgp};")
+            a(f"selp.b32 {vreg}, {vbit}, 0, {vany};")
+            a(f"@{pcl0} atom.shared.or.b32 {a.r()}, [{bars}+{OVF + 4 * u}], {vreg};")
+            a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{bars}+{CSYNC + 8 * u}];")
+            wait_bar_warp(a, f"{bars}+{CSYNC + 8 * u}", cgp, err, ERR_SOFTMAX, l_cdone)
+            ov, ovb, pov = a.r(), a.r(), a.r("p")
+            a(f"ld.shared.u32 {ov}, [{bars}+{OVF + 4 * u}];")
+            a(f"and.b32 {ovb}, {ov}, {vbit};")
+            a(f"setp.ne.u32 {pov}, {ovb}, 0;")
+            l_nost = a.L("nost")
+            a(f"@{pov} bra {l_nost};")
+            for v, cv in enumerate(conv):
+                a(f"st.shared.v4.b32 [{cbase[u]}+{2048 * v}], {{{', '.join(cv)}}};")
+            a.label(l_nost)
+            # the tensor core reads this stage through the async proxy
+            a("fence.proxy.async.shared::cta;")
+            a("bar.warp.sync -1;")
+            fmtv, nbit = a.r(), a.r()
+            a(f"selp.u32 {fmtv}, 0, 1, {pov};")
+            a(f"@{pw12} st.shared.u32 [{bars}+{FMT + 4 * u}], {fmtv};")
+            # clear the other parity's vote bit for this stage's next use (block j+4); every warp
+            # has read this block's bit, and none can reach block j+4 before this warp's next arrival
+            a(f"shl.b32 {nbit}, 1, {cgpn};")
+            a(f"not.b32 {nbit}, {nbit};")
+            a(f"@{pw12} atom.shared.and.b32 {a.r()}, [{bars}+{OVF + 4 * u}], {nbit};")
+            a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{bars}+{VCONV + 8 * u}];")
+            a(f"add.u32 {cj}, {cj}, 1;")
+        a(f"mov.u32 {cgp}, {cgpn};")
+        a(f"bra {l_cg};")
+        a.label(l_cdone)
+        a(f"bra {l_end};")
 
     # ---------------- softmax warps ------------------------------------------------------------
     a.label(l_soft)
@@ -603,13 +730,37 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     parts = [a.r("f") for _ in range(4)]
     for pp in parts:
         a(f"mov.b32 {pp}, 0f00000000;")
+    for idx in range(BKV):
+        a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
+        a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
+        a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {s_[idx]};")
+    l_pdone = a.L("pdone")
+    if half:
+        # the V converters decided this block's format: f16 P (rounded to nearest, 2^-12 relative)
+        # when V_j fit f16, else the bf16 hi + lo pair below
+        uu, vcb, vpar, fmt, p16 = a.r(), a.r(), a.r(), a.r(), a.r("p")
+        a(f"and.b32 {uu}, {jj}, 3;")
+        a(f"mad.lo.u32 {vcb}, {uu}, 8, {bars};")
+        a(f"add.u32 {vcb}, {vcb}, {VCONV};")
+        a(f"shr.u32 {vpar}, {jj}, 2;")
+        a(f"and.b32 {vpar}, {vpar}, 1;")
+        wait_bar_warp(a, vcb, vpar, err, ERR_SOFTMAX, l_sdone)
+        a(f"mad.lo.u32 {vcb}, {uu}, 4, {bars};")
+        a(f"ld.shared.u32 {fmt}, [{vcb}+{FMT}];")
+        a(f"setp.ne.u32 {p16}, {fmt}, 0;")
+        l_pbf = a.L("pbf")
+        a(f"@!{p16} bra {l_pbf};")
+        hw = []
+        for k in range(BKV // 2):
+            w = a.r()
+            a(f"cvt.rn.f16x2.f32 {w}, {s_[2 * k + 1]}, {s_[2 * k]};")
+            hw.append(w)
+        a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{scol}], {{{', '.join(hw)}}};")
+        a(f"bra {l_pdone};")
+        a.label(l_pbf)
     hi_w, lo_w = [], []
     for k in range(BKV // 2):
         i0, i1 = 2 * k, 2 * k + 1
-        for idx in (i0, i1):
-            a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
-            a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
-            a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {s_[idx]};")
         w = a.r()
         if precise:
             # hi = the top 16 bits of p (prmt packs two top halves into one word); lo = the top
@@ -630,6 +781,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         dst2 = a.r()
         a(f"add.u32 {dst2}, {scol}, {BKV // 2};")
         a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{dst2}], {{{', '.join(lo_w)}}};")
+    a.label(l_pdone)
     sstamp(3)
     p01, p23 = a.r("f"), a.r("f")
     a(f"add.f32 {p01}, {parts[0]}, {parts[1]};")
@@ -711,7 +863,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
               "\t.param .align 64 .b8 p_tmV[128],", "\t.param .u64 p_err" + ("," if trace else "")]
     if trace:
         params.append("\t.param .u64 p_trace")
-    entry = [f".visible .entry {name}("] + params + [")", f".reqntid {THREADS}, 1, 1", ".maxnreg 168", "{"]
+    entry = [f".visible .entry {name}("] + params + [")", f".reqntid {threads}, 1, 1",
+                                                       f".maxnreg {65536 // threads // 8 * 8}", "{"]
     entry += a.decls() + a.lines + ["\tret;", "}"]
     qn, kn, vn, on = names
     dims = [D, seq, heads, batch]
@@ -726,7 +879,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     return {
         "name": name, "kind": "tcgen05_attention", "params": [qn, kn, vn, on],
         "raw_entry": entry, "raw_decls": [f".extern .shared .align 1024 .b8 {smem_sym}[];"],
-        "grid": [grid, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": dyn,
+        "grid": [grid, 1, 1], "block": [threads, 1, 1], "dyn_smem": dyn,
         "align": {qn: 16, kn: 16, vn: 16, on: 32}, "zero_outputs": [], "tmaps": tmaps,
         "extra": extra,
     }

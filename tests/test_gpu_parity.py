@@ -161,3 +161,23 @@ def test_full_attention_tensor_core_sampled():
         s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
         want = torch.softmax(s_, -1) @ v
         compare(O[b, h], want, "bf16", 1e-4, f"c5 full ({b},{h})", rms_floor=True)
+
+
+@pytest.mark.parametrize("mode", ["mixed", "all_large"])
+def test_attention_value_range_fallback(mode):
+    """V blocks whose values do not fit f16 stay bf16 (P as bf16 hi + lo) while the other blocks use
+    f16: the result still matches the oracle.  ``mixed`` puts 2^20-scaled values in one 64-row kv
+    block, ``all_large`` in every row, and one infinity-free extreme (the largest bf16) appears too."""
+    p = irgen.SMALL["c5tc"]()
+    t_cpu = data.make_inputs(p)
+    V = t_cpu["V"].float()
+    if mode == "mixed":
+        V[:, :, 64:128] *= 2.0 ** 20
+    else:
+        V *= 2.0 ** 20
+        V[0, 0, 5, 3] = 3.3895313892515355e38
+    t_cpu["V"] = V.to(torch.bfloat16)
+    want = oracle_outputs(p, t_cpu)
+    got, ex = _run_ours(p, t_cpu)
+    assert ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"range {mode}", rms_floor=True)
