@@ -47,6 +47,11 @@ THREADS = 384                    # warps 0-11; with the f16 path, warps 12-15 co
 CONV_WARPS = 4
 TMEM_COLS = 512
 F16_MAX_BF16_BITS = 0x477F       # the largest bf16 magnitude (65280) below the f16 overflow threshold
+POLY_EVERY = 0                   # f16 path: every n-th exp2 on the FMA pipe (cubic); 0 = all on the MUFU, which measured fastest
+# 2^f on [-1/2, 1/2] as c0 + c1 f + c2 f^2 + c3 f^3 (f32 bit patterns): a least-squares fit in relative
+# error on 4000 Chebyshev nodes; evaluated by f32 Horner it stays within 7.8e-5 relative, below the
+# f16 rounding of P (tests/test_emitter.py re-derives the bound)
+EXP2_C = ("0f3F7FFB58", "0f3F317A8D", "0f3E786D32", "0f3D61A4AC")
 S_COL0 = TILES * D               # S_i[b] at S_COL0 + 2*BKV*i + BKV*b
 LOG2E = 1.4426950408889634
 RESCALE_THRESHOLD = 8.0          # log2 units: rescale O only when the max grew by more than 2^8
@@ -82,7 +87,7 @@ def _f32(v: float) -> str:
 
 def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, scale: float,
                     names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True,
-                    trace: bool = False, half: bool = True) -> dict:
+                    trace: bool = False, half: bool = True, poly_every: int = POLY_EVERY) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`)."""
     if seq % (BQ * TILES):
@@ -240,10 +245,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     for i in range(TILES):
         r_i = a.r()
         a(f"add.u32 {r_i}, {row0}, {BQ * i};")
-        for half in range(2):
+        for hb in range(2):
             d_ = a.r()
-            a(f"add.u32 {d_}, {sQ}, {Q_BYTES * i + Q_HALF * half};")
-            tma4(d_, tq, 64 * half, r_i, qb)
+            a(f"add.u32 {d_}, {sQ}, {Q_BYTES * i + Q_HALF * hb};")
+            tma4(d_, tq, 64 * hb, r_i, qb)
     n_, stage, phase = a.r(), a.r(), a.r()
     armed = [a.r() for _ in range(STAGES)]
     for r_ in armed:
@@ -627,7 +632,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     ev_s, ptw = None, None
     if trace:
         ev_s = a.r()
-        a(f"mad.lo.u32 {ev_s}, {ti}, 6, 8;")
+        a(f"mad.lo.u32 {ev_s}, {ti}, 8, 8;")
         ptw = a.r("p")
         a(f"setp.eq.u32 {ptw}, {rowl}, 0;")
     s_ = [a.r("f") for _ in range(BKV)]
@@ -637,8 +642,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mov.u32 {jj}, 0;")
 
     def sstamp(k):
-        """Softmax timeline stamp ``k`` (0 S ready, 1 S loaded, 2 row max, 3 P stores issued,
-        4 P written) for this tile, from the tile's first thread."""
+        """Softmax timeline stamp ``k`` (0 S ready, 1 S loaded, 2 row max, 3 format known, 4 exps
+        done, 5 P stores issued, 6 P written) for this tile, from the tile's first thread."""
         if not trace:
             return
         ev = a.r()
@@ -657,6 +662,22 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"shr.u32 {par_s}, {jj}, 1;")
     a(f"and.b32 {par_s}, {par_s}, 1;")
     a(f"mad.lo.u32 {scol}, {bsel}, {BKV}, {scol0};")
+    p16 = None
+    if half:
+        # the V converters' decision for this block: f16 P (rounded to nearest, 2^-12 relative) when
+        # V_j fit f16, else bf16 hi + lo.  Checked before the scores are ready: V_j is loaded
+        # before K_(j+1), so this wait usually overlaps the wait for S.
+        uu, vcb, vpar, fmt = a.r(), a.r(), a.r(), a.r()
+        p16 = a.r("p")
+        a(f"and.b32 {uu}, {jj}, 3;")
+        a(f"mad.lo.u32 {vcb}, {uu}, 8, {bars};")
+        a(f"add.u32 {vcb}, {vcb}, {VCONV};")
+        a(f"shr.u32 {vpar}, {jj}, 2;")
+        a(f"and.b32 {vpar}, {vpar}, 1;")
+        wait_bar_warp(a, vcb, vpar, err, ERR_SOFTMAX, l_sdone)
+        a(f"mad.lo.u32 {vcb}, {uu}, 4, {bars};")
+        a(f"ld.shared.u32 {fmt}, [{vcb}+{FMT}];")
+        a(f"setp.ne.u32 {p16}, {fmt}, 0;")
     wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_sdone)
     sstamp(0)
     a("tcgen05.fence::after_thread_sync;")
@@ -682,18 +703,22 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"setp.lt.s32 {pm}, {lim}, {c};")
             a(f"@{pm} mov.b32 {s_[c]}, 0fFF800000;")
         a.label(l_nomask)
-    # row max (tree), in the scaled log2 domain
+    # row max in the scaled log2 domain: 8 independent chains of three-input maxima (columns k,
+    # k+8, ...), then 8 -> 3 -> 1
     lvl = [a.r("f") for _ in range(8)]
     for k in range(8):
-        a(f"max.f32 {lvl[k]}, {s_[k]}, {s_[k + 8]};")
-        for c in range(k + 16, BKV, 8):
-            a(f"max.f32 {lvl[k]}, {lvl[k]}, {s_[c]};")
-    while len(lvl) > 1:
-        nxt = []
-        for k in range(0, len(lvl), 2):
-            a(f"max.f32 {lvl[k]}, {lvl[k]}, {lvl[k + 1]};")
-            nxt.append(lvl[k])
-        lvl = nxt
+        col = list(range(k, BKV, 8))
+        a(f"max.f32 {lvl[k]}, {s_[col[0]]}, {s_[col[1]]}, {s_[col[2]]};")
+        rest = col[3:]
+        while len(rest) >= 2:
+            a(f"max.f32 {lvl[k]}, {lvl[k]}, {s_[rest[0]]}, {s_[rest[1]]};")
+            rest = rest[2:]
+        if rest:
+            a(f"max.f32 {lvl[k]}, {lvl[k]}, {s_[rest[0]]};")
+    a(f"max.f32 {lvl[0]}, {lvl[0]}, {lvl[1]}, {lvl[2]};")
+    a(f"max.f32 {lvl[3]}, {lvl[3]}, {lvl[4]}, {lvl[5]};")
+    a(f"max.f32 {lvl[6]}, {lvl[6]}, {lvl[7]};")
+    a(f"max.f32 {lvl[0]}, {lvl[0]}, {lvl[3]}, {lvl[6]};")
     mblk, mnew = a.r("f"), a.r("f")
     a(f"mul.f32 {mblk}, {lvl[0]}, {cscale};")
     a(f"max.f32 {mnew}, {mref}, {mblk};")
@@ -730,34 +755,56 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     parts = [a.r("f") for _ in range(4)]
     for pp in parts:
         a(f"mov.b32 {pp}, 0f00000000;")
-    for idx in range(BKV):
-        a(f"fma.rn.f32 {s_[idx]}, {s_[idx]}, {cscale}, {negm};")
-        a(f"ex2.approx.ftz.f32 {s_[idx]}, {s_[idx]};")
-        a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {s_[idx]};")
+    def exp_block(poly_every, cols=range(BKV)):
+        """p = 2^(s*c - m) for the row's BKV scores, summed into ``parts``.  With ``poly_every`` = n,
+        every n-th value is taken on the FMA pipe instead of the MUFU (the softmax's bottleneck):
+        x is clamped at -120, split as n + f with f in [-1/2, 1/2] by the 1.5*2^23 rounding trick,
+        2^f comes from a cubic (``EXP2_C``), and n is added to the exponent field.  Only the f16 path
+        uses it: there P rounds 2^-120 to zero, as the MUFU's 2^-inf is zero."""
+        t_, j_, f_, r_, ti_, ri_ = (a.r("f"), a.r("f"), a.r("f"), a.r("f"), a.r(), a.r())
+        for idx in cols:
+            x = s_[idx]
+            a(f"fma.rn.f32 {x}, {x}, {cscale}, {negm};")
+            if poly_every and idx % poly_every == poly_every - 1:
+                a(f"max.f32 {x}, {x}, 0fC2F00000;")
+                a(f"add.f32 {t_}, {x}, 0f4B400000;")
+                a(f"sub.f32 {j_}, {t_}, 0f4B400000;")
+                a(f"sub.f32 {f_}, {x}, {j_};")
+                a(f"fma.rn.f32 {r_}, {f_}, {EXP2_C[3]}, {EXP2_C[2]};")
+                a(f"fma.rn.f32 {r_}, {r_}, {f_}, {EXP2_C[1]};")
+                a(f"fma.rn.f32 {r_}, {r_}, {f_}, {EXP2_C[0]};")
+                a(f"mov.b32 {ti_}, {t_};")
+                a(f"shl.b32 {ti_}, {ti_}, 23;")
+                a(f"mov.b32 {ri_}, {r_};")
+                a(f"add.s32 {ri_}, {ri_}, {ti_};")
+                a(f"mov.b32 {x}, {ri_};")
+            else:
+                a(f"ex2.approx.ftz.f32 {x}, {x};")
+            a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {x};")
+
     l_pdone = a.L("pdone")
     if half:
-        # the V converters decided this block's format: f16 P (rounded to nearest, 2^-12 relative)
-        # when V_j fit f16, else the bf16 hi + lo pair below
-        uu, vcb, vpar, fmt, p16 = a.r(), a.r(), a.r(), a.r(), a.r("p")
-        a(f"and.b32 {uu}, {jj}, 3;")
-        a(f"mad.lo.u32 {vcb}, {uu}, 8, {bars};")
-        a(f"add.u32 {vcb}, {vcb}, {VCONV};")
-        a(f"shr.u32 {vpar}, {jj}, 2;")
-        a(f"and.b32 {vpar}, {vpar}, 1;")
-        wait_bar_warp(a, vcb, vpar, err, ERR_SOFTMAX, l_sdone)
-        a(f"mad.lo.u32 {vcb}, {uu}, 4, {bars};")
-        a(f"ld.shared.u32 {fmt}, [{vcb}+{FMT}];")
-        a(f"setp.ne.u32 {p16}, {fmt}, 0;")
+        # the format the V converters chose for this block (read at the top of the iteration)
+        sstamp(3)
         l_pbf = a.L("pbf")
         a(f"@!{p16} bra {l_pbf};")
-        hw = []
-        for k in range(BKV // 2):
-            w = a.r()
-            a(f"cvt.rn.f16x2.f32 {w}, {s_[2 * k + 1]}, {s_[2 * k]};")
-            hw.append(w)
-        a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{scol}], {{{', '.join(hw)}}};")
+        half_n = BKV // 2
+        for h in range(2):
+            # each half of the row is packed and stored as soon as its exps are done
+            exp_block(poly_every, range(half_n * h, half_n * (h + 1)))
+            hw = []
+            for k in range(half_n * h // 2, half_n * (h + 1) // 2):
+                w = a.r()
+                a(f"cvt.rn.f16x2.f32 {w}, {s_[2 * k + 1]}, {s_[2 * k]};")
+                hw.append(w)
+            dsth = a.r()
+            a(f"add.u32 {dsth}, {scol}, {len(hw) * h};")
+            a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dsth}], {{{', '.join(hw)}}};")
+        sstamp(4)
+        sstamp(5)
         a(f"bra {l_pdone};")
         a.label(l_pbf)
+    exp_block(0)
     hi_w, lo_w = [], []
     for k in range(BKV // 2):
         i0, i1 = 2 * k, 2 * k + 1
@@ -781,8 +828,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         dst2 = a.r()
         a(f"add.u32 {dst2}, {scol}, {BKV // 2};")
         a(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{dst2}], {{{', '.join(lo_w)}}};")
+    sstamp(5)
     a.label(l_pdone)
-    sstamp(3)
     p01, p23 = a.r("f"), a.r("f")
     a(f"add.f32 {p01}, {parts[0]}, {parts[1]};")
     a(f"add.f32 {p23}, {parts[2]}, {parts[3]};")
@@ -808,7 +855,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a("tcgen05.wait::st.sync.aligned;")
     a("tcgen05.fence::before_thread_sync;")
     a("bar.warp.sync -1;")
-    sstamp(4)
+    sstamp(6)
     a(f"@{ple} mbarrier.arrive.shared::cta.b64 _, [{pfb}];")
     a(f"add.u32 {jj}, {jj}, 1;")
     a(f"bra {l_sj};")
@@ -887,9 +934,9 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 
 def trace_events(buf, grid: int):
     """Split a ``trace`` buffer (u64 [grid, 66, 24]) into per-CTA timelines.  For kv block j, events
-    0-7 are the MMA thread's iteration start, K_(j+1) arrived, S(j+1) issued, V_j arrived, P_0(j)
-    ready, PV_0 issued, P_1(j) ready and PV_1 issued; 8-12 (tile 0) and 14-18 (tile 1) are the
-    softmax's S(j) ready, S loaded, row max, P stores issued and P(j) written.  Row 65 holds CTA
-    start, end and the SM id."""
+    0-7 are tile 0's issuer's iteration start, K_(j+1) arrived, S(j+1) issued and V_j arrived,
+    then P_0(j) ready, PV_0 issued, P_1(j) ready and PV_1 issued (each tile's issuer); 8-14 (tile 0)
+    and 16-22 (tile 1) are the softmax's S(j) ready, S loaded, row max, format known, exps done,
+    P stores issued and P(j) written.  Row 65 holds CTA start, end and the SM id."""
     import numpy as np
     return np.asarray(buf, dtype=np.uint64).reshape(grid, TRACE_SLOTS, TRACE_EVENTS)

@@ -335,5 +335,7 @@ def try_lower(graph, node, kmeta, prefix, options):
         return tc_attention.attention_entry(node.op.name, bt, hd, seq, causal, scale,
                                             names=(Q.name, K.name, V.name, O.name), prefix=prefix,
                                             precise=bool(options.get("attn_precise", True)),
-                                            trace=bool(options.get("attn_trace", False)))
+                                            trace=bool(options.get("attn_trace", False)),
+                                            half=bool(options.get("attn_half", True)),
+                                            poly_every=int(options.get("attn_poly", tc_attention.POLY_EVERY)))
     return None

@@ -167,3 +167,48 @@ def test_programmatic_dependent_launch_is_opt_in_and_waits_before_memory():
     body = mod.ptx.split("griddepcontrol.wait;", 1)
     assert len(body) == 2 and "ld.global" not in body[0] and "st.global" not in body[0]
     assert "griddepcontrol.launch_dependents;" in body[1]
+
+
+def test_attention_cubic_exp2_meets_its_error_bound():
+    """The FMA-pipe 2^x of the attention softmax (range reduction by the 1.5*2^23 rounding trick, a
+    cubic on [-1/2, 1/2], exponent added as an integer), evaluated with f32 / i32 arithmetic."""
+    import numpy as np
+    from emmy_ptx_b200.kernels import tc_attention as T
+    c = [np.frombuffer(bytes.fromhex(h[2:])[::-1], dtype=np.float32)[0] for h in T.EXP2_C]
+    f = np.linspace(-0.5, 0.5, 200001).astype(np.float32)
+    r = c[3] * f + c[2]
+    r = (r * f + c[1]).astype(np.float32)
+    r = (r * f + c[0]).astype(np.float32)
+    assert np.max(np.abs(r.astype(np.float64) / 2.0 ** f.astype(np.float64) - 1)) < 7.8e-5
+    x = np.linspace(-119.9, 8.0, 400001).astype(np.float32)
+    magic = np.float32(12582912.0)
+    t = (x + magic).astype(np.float32)
+    j = (t - magic).astype(np.float32)
+    fr = (x - j).astype(np.float32)
+    r = (c[3] * fr + c[2]).astype(np.float32)
+    r = (r * fr + c[1]).astype(np.float32)
+    r = (r * fr + c[0]).astype(np.float32)
+    bits = r.view(np.int32) + (t.view(np.int32) << 23)
+    p = bits.view(np.float32).astype(np.float64)
+    assert np.max(np.abs(p / 2.0 ** x.astype(np.float64) - 1)) < 8e-5
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("precise,half", [(True, True), (True, False), (False, False)])
+def test_attention_variants_only_use_initialised_barriers(causal, precise, half):
+    """Every mbarrier the attention kernel waits on or arrives at is one it initialises, and the
+    launch geometry matches the warp roles of the variant (a variant that waited on a barrier nobody
+    arrives at would stall until its bounded waits ran out)."""
+    import math
+    import re
+    from emmy_ptx_b200.codegen.ptxcheck import undefined_uses
+    from emmy_ptx_b200.kernels import tc_attention as T
+    e = T.attention_entry("k", 2, 4, 1024, causal, 1 / math.sqrt(128), precise=precise, half=half)
+    body = "\n".join(e["raw_entry"])
+    base = re.search(r"add\.u32 (%r\d+), %r\d+, " + str(T.TILES * T.Q_BYTES + T.STAGES * T.KV_BYTES) + ";", body).group(1)
+    inited = {int(m) for m in re.findall(r"mbarrier\.init\.shared::cta\.b64 \[" + re.escape(base) + r"\+(\d+)\]", body)}
+    used = {int(m) for m in re.findall(r"mbarrier\.(?:try_wait\.parity|arrive)[^\[]*\[" + re.escape(base) + r"\+(\d+)\]", body)}
+    used |= {int(m) for m in re.findall(r"tcgen05\.commit[^\[]*\[" + re.escape(base) + r"\+(\d+)\]", body)}
+    assert used and used <= inited, sorted(used - inited)
+    assert e["block"][0] == (512 if (half and precise) else 384)
+    assert undefined_uses(".version 8.8\n.target sm_100a\n.address_size 64\n" + body) == []
