@@ -82,7 +82,7 @@ def test_attention_ir_is_recognised():
         assert abs(scale - p.params["scale"]) < 1e-7
     full = irgen.FULL["c5"]()
     rec = compile_graph(Graph.from_dict(full.graph), full.meta()).kernels[0]
-    assert rec["kind"] == "tcgen05_attention" and rec["block"] == [384, 1, 1] and rec["grid"] == [4096, 1, 1]
+    assert rec["kind"] == "tcgen05_attention" and rec["block"] == [512, 1, 1] and rec["grid"] == [4096, 1, 1]
 
 
 def test_attention_with_a_different_mask_is_refused():
