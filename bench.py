@@ -53,7 +53,7 @@ def _small_for_profile():
         "c2i": lambda: irgen.sum_ir(1 << 26, "i32"),
         "c3": lambda: irgen.fused_ir(4096, 8192),
         "c4": lambda: irgen.bmm_ir(2, 4096, 4096, 4096),
-        "c5": lambda: irgen.attention_ir(1, 8, 4096, 128),
+        "c5": lambda: irgen.attention_ir(2, 16, 4096, 128),
     }
 
 
@@ -490,12 +490,13 @@ def main() -> int:
         nb = int(units // 2) // 4
         pairs = [(torch.ones(nb, dtype=torch.float32, device="cuda"), torch.empty(nb, dtype=torch.float32, device="cuda"))
                  for _ in range(rotate)]
+        # an elementwise kernel on the SMs (torch's copy_ of same-dtype tensors may go to a copy engine)
         for a_, b_ in pairs:
-            b_.copy_(a_)
+            torch.mul(a_, 1.0, out=b_)
         g_copy = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_copy):
             for i in range(reps):
-                pairs[i % rotate][1].copy_(pairs[i % rotate][0])
+                torch.mul(pairs[i % rotate][0], 1.0, out=pairs[i % rotate][1])
         g_copy.replay()
         torch.cuda.synchronize()
         c0 = torch.cuda.Event(enable_timing=True)
@@ -508,7 +509,7 @@ def main() -> int:
         del g_copy, pairs
         torch.cuda.synchronize()
         copy_ref = {"achieved": units / (copy_ms / 1000.0) / scale, "ms_per_launch": copy_ms,
-                    "how": "torch copy_ of the same bytes (half read, half written), same rotation, graph replay"}
+                    "how": "torch elementwise y = x * 1 over the same bytes (half read, half written), same rotation, graph replay"}
 
     achieved = units / (kern_ms / 1000.0) / scale
     if copy_ref:

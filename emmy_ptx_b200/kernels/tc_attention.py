@@ -516,77 +516,80 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"setp.eq.u32 {pcl0}, {lane}, 0;")
         a(f"setp.eq.u32 {pw12}, {ct}, 0;")
         l_cdone = a.L("cdone")
-        cj, cgp, cgpn = a.r(), a.r(), a.r()
+        cj = a.r()
         a(f"mov.u32 {cj}, 0;")
-        a(f"mov.u32 {cgp}, 0;")
-        cbase = []
-        for u in range(4):
-            cb = a.r()
-            a(f"add.u32 {cb}, {sKV}, {(2 * u + 1) * KV_BYTES};")
-            a(f"add.u32 {cb}, {cb}, {coff};")
-            cbase.append(cb)
-        l_cg = a.L("cg")
-        a.label(l_cg)
-        a(f"xor.b32 {cgpn}, {cgp}, 1;")
-        for u in range(4):
-            pend_ = a.r("p")
-            a(f"setp.ge.u32 {pend_}, {cj}, {nb};")
-            a(f"@{pend_} bra {l_cdone};")
-            wait_bar_warp(a, f"{bars}+{FULL + 8 * (2 * u + 1)}", cgp, err, ERR_SOFTMAX, l_cdone)
-            m = a.r()
-            a(f"mov.u32 {m}, 0;")
-            conv = []
-            for v in range(KV_BYTES // 16 // 128):
-                ws = [a.r() for _ in range(4)]
-                a(f"ld.shared.v4.b32 {{{', '.join(ws)}}}, [{cbase[u]}+{2048 * v}];")
-                cv = []
-                for w in ws:
-                    t_, lo_, hi_, f_ = a.r(), a.r("f"), a.r("f"), a.r()
-                    a(f"and.b32 {t_}, {w}, 0x7FFF7FFF;")
-                    a(f"max.u16x2 {m}, {m}, {t_};")
-                    a(f"shl.b32 {lo_}, {w}, 16;")
-                    a(f"and.b32 {hi_}, {w}, -65536;")
-                    a(f"cvt.rn.f16x2.f32 {f_}, {hi_}, {lo_};")
-                    cv.append(f_)
-                conv.append(cv)
-            mlo, mhi, po1, po2 = a.r(), a.r(), a.r("p"), a.r("p")
-            a(f"and.b32 {mlo}, {m}, 65535;")
-            a(f"shr.u32 {mhi}, {m}, 16;")
-            a(f"setp.gt.u32 {po1}, {mlo}, {F16_MAX_BF16_BITS};")
-            a(f"setp.gt.u32 {po2}, {mhi}, {F16_MAX_BF16_BITS};")
-            a(f"or.pred {po1}, {po1}, {po2};")
-            vany = a.r("p")
-            a(f"vote.sync.any.pred {vany}, {po1}, -1;")
-            vbit, vreg = a.r(), a.r()
-            a(f"shl.b32 {vbit}, 1, {cgp};")
-            a(f"selp.b32 {vreg}, {vbit}, 0, {vany};")
-            a(f"@{pcl0} atom.shared.or.b32 {a.r()}, [{bars}+{OVF + 4 * u}], {vreg};")
-            a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{bars}+{CSYNC + 8 * u}];")
-            wait_bar_warp(a, f"{bars}+{CSYNC + 8 * u}", cgp, err, ERR_SOFTMAX, l_cdone)
-            ov, ovb, pov = a.r(), a.r(), a.r("p")
-            a(f"ld.shared.u32 {ov}, [{bars}+{OVF + 4 * u}];")
-            a(f"and.b32 {ovb}, {ov}, {vbit};")
-            a(f"setp.ne.u32 {pov}, {ovb}, 0;")
-            l_nost = a.L("nost")
-            a(f"@{pov} bra {l_nost};")
-            for v, cv in enumerate(conv):
-                a(f"st.shared.v4.b32 [{cbase[u]}+{2048 * v}], {{{', '.join(cv)}}};")
-            a.label(l_nost)
-            # the tensor core reads this stage through the async proxy
-            a("fence.proxy.async.shared::cta;")
-            a("bar.warp.sync -1;")
-            fmtv, nbit = a.r(), a.r()
-            a(f"selp.u32 {fmtv}, 0, 1, {pov};")
-            a(f"@{pw12} st.shared.u32 [{bars}+{FMT + 4 * u}], {fmtv};")
-            # clear the other parity's vote bit for this stage's next use (block j+4); every warp
-            # has read this block's bit, and none can reach block j+4 before this warp's next arrival
-            a(f"shl.b32 {nbit}, 1, {cgpn};")
-            a(f"not.b32 {nbit}, {nbit};")
-            a(f"@{pw12} atom.shared.and.b32 {a.r()}, [{bars}+{OVF + 4 * u}], {nbit};")
-            a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{bars}+{VCONV + 8 * u}];")
-            a(f"add.u32 {cj}, {cj}, 1;")
-        a(f"mov.u32 {cgp}, {cgpn};")
-        a(f"bra {l_cg};")
+        l_cb = a.L("cb")
+        a.label(l_cb)
+        pend_ = a.r("p")
+        a(f"setp.ge.u32 {pend_}, {cj}, {nb};")
+        a(f"@{pend_} bra {l_cdone};")
+        # block j: V_j is ring item 2j+1, stage 2u+1 with u = j & 3, phase parity (j >> 2) & 1
+        cu, cst, cgp, cfb, cbase, cs8, cs4 = a.r(), a.r(), a.r(), a.r(), a.r(), a.r(), a.r()
+        a(f"and.b32 {cu}, {cj}, 3;")
+        a(f"mad.lo.u32 {cst}, {cu}, 2, 1;")
+        a(f"shr.u32 {cgp}, {cj}, 2;")
+        a(f"and.b32 {cgp}, {cgp}, 1;")
+        a(f"mad.lo.u32 {cfb}, {cst}, 8, {bars};")
+        a(f"mad.lo.u32 {cbase}, {cst}, {KV_BYTES}, {sKV};")
+        a(f"add.u32 {cbase}, {cbase}, {coff};")
+        a(f"mad.lo.u32 {cs8}, {cu}, 8, {bars};")            # per-stage barriers (CSYNC, VCONV)
+        a(f"mad.lo.u32 {cs4}, {cu}, 4, {bars};")            # per-stage words (OVF, FMT)
+        wait_bar_warp(a, f"{cfb}+{FULL}", cgp, err, ERR_SOFTMAX, l_cdone)
+        m = a.r()
+        a(f"mov.u32 {m}, 0;")
+        conv = []
+        for v in range(KV_BYTES // 16 // 128):
+            ws = [a.r() for _ in range(4)]
+            a(f"ld.shared.v4.b32 {{{', '.join(ws)}}}, [{cbase}+{2048 * v}];")
+            cv = []
+            for w in ws:
+                t_, lo_, hi_, f_ = a.r(), a.r("f"), a.r("f"), a.r()
+                a(f"and.b32 {t_}, {w}, 0x7FFF7FFF;")
+                a(f"max.u16x2 {m}, {m}, {t_};")
+                a(f"shl.b32 {lo_}, {w}, 16;")
+                a(f"and.b32 {hi_}, {w}, -65536;")
+                a(f"cvt.rn.f16x2.f32 {f_}, {hi_}, {lo_};")
+                cv.append(f_)
+            conv.append(cv)
+        mlo, mhi, po1, po2 = a.r(), a.r(), a.r("p"), a.r("p")
+        a(f"and.b32 {mlo}, {m}, 65535;")
+        a(f"shr.u32 {mhi}, {m}, 16;")
+        a(f"setp.gt.u32 {po1}, {mlo}, {F16_MAX_BF16_BITS};")
+        a(f"setp.gt.u32 {po2}, {mhi}, {F16_MAX_BF16_BITS};")
+        a(f"or.pred {po1}, {po1}, {po2};")
+        vany = a.r("p")
+        a(f"vote.sync.any.pred {vany}, {po1}, -1;")
+        vbit, vreg = a.r(), a.r()
+        a(f"shl.b32 {vbit}, 1, {cgp};")
+        a(f"selp.b32 {vreg}, {vbit}, 0, {vany};")
+        a(f"@{pcl0} atom.shared.or.b32 {a.r()}, [{cs4}+{OVF}], {vreg};")
+        a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{cs8}+{CSYNC}];")
+        wait_bar_warp(a, f"{cs8}+{CSYNC}", cgp, err, ERR_SOFTMAX, l_cdone)
+        ov, ovb, pov = a.r(), a.r(), a.r("p")
+        a(f"ld.shared.u32 {ov}, [{cs4}+{OVF}];")
+        a(f"and.b32 {ovb}, {ov}, {vbit};")
+        a(f"setp.ne.u32 {pov}, {ovb}, 0;")
+        l_nost = a.L("nost")
+        a(f"@{pov} bra {l_nost};")
+        for v, cv in enumerate(conv):
+            a(f"st.shared.v4.b32 [{cbase}+{2048 * v}], {{{', '.join(cv)}}};")
+        a.label(l_nost)
+        # the tensor core reads this stage through the async proxy
+        a("fence.proxy.async.shared::cta;")
+        a("bar.warp.sync -1;")
+        fmtv, nbit = a.r(), a.r()
+        a(f"selp.u32 {fmtv}, 0, 1, {pov};")
+        a(f"@{pw12} st.shared.u32 [{cs4}+{FMT}], {fmtv};")
+        # clear the other parity's vote bit for this stage's next use (block j+4); every warp has
+        # read this block's bit, and none can reach block j+4 before this warp's next arrival
+        ogp = a.r()
+        a(f"xor.b32 {ogp}, {cgp}, 1;")
+        a(f"shl.b32 {nbit}, 1, {ogp};")
+        a(f"not.b32 {nbit}, {nbit};")
+        a(f"@{pw12} atom.shared.and.b32 {a.r()}, [{cs4}+{OVF}], {nbit};")
+        a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{cs8}+{VCONV}];")
+        a(f"add.u32 {cj}, {cj}, 1;")
+        a(f"bra {l_cb};")
         a.label(l_cdone)
         a(f"bra {l_end};")
 
