@@ -73,6 +73,8 @@ TRAFFIC = {
     "c2i": (268.443904e6 + 4.902912e6) * 4,      # same kernel shape, i32 elements
     "c3": (201.394176e6 + 44.741632e6) * 2,      # 4096 -> 8192 rows
     "c4": (192.727040e6 + 105.907456e6) * 8,     # 2 -> 16 batches
+    "c1": 16.793088e6 + 0.0,                     # captured at full size (y stays in L2 at kernel end)
+    "c5": (143.738112e6 + 14.620416e6) * 8,      # 32 -> 256 (batch, head) pairs
 }
 
 
