@@ -19,8 +19,8 @@ MARK = "// emmy-b200-kernel "
 def shared_decls(built: list[dict]) -> list[str]:
     out = []
     for b in built:
-        if b.get("raw_decls"):
-            out.extend(b["raw_decls"])
+        if b.get("raw_entry"):
+            out.extend(b.get("raw_decls") or [])
             continue
         if b["dyn"]:
             out.append(f".extern .shared .align 1024 .b8 {b['pool_name']}[];")
@@ -46,7 +46,7 @@ def launch_record(b: dict) -> dict:
         "zero_outputs": b.get("zero_outputs", []),
         "kind": b.get("kind", "generic"),
     }
-    for k in ("tmaps", "cluster", "extra", "pdl"):
+    for k in ("tmaps", "cluster", "extra", "pdl", "scratch"):
         if b.get(k):
             rec[k] = b[k]
     return rec

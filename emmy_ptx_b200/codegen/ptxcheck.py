@@ -250,7 +250,8 @@ def undefined_uses(ptx: str) -> list[tuple[str, int, str, str]]:
                 continue
             if x.guard in regs:
                 x.uses.add(x.guard)
-            first_is_dest = bool(x.ops) and not x.op.startswith(_NO_DEST) and not x.ops[0].startswith("[")
+            no_dest = x.op.startswith(_NO_DEST) and not x.op.startswith("bar.red")   # bar.red writes a result
+            first_is_dest = bool(x.ops) and not no_dest and not x.ops[0].startswith("[")
             for j, o in enumerate(x.ops):
                 toks = {t for t in _TOKEN.findall(o) if t in regs}
                 if j == 0 and first_is_dest:

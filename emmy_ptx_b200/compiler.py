@@ -56,7 +56,8 @@ def compile_graph(graph: Graph, meta: dict | None = None, options: dict | None =
             b = patterns.try_lower(graph, node, km, prefix, options)
         if b is None:
             b = KernelEmitter(graph, node, km, prefix, options).build()
-        built.append(b)
+        # a lowering may emit several entries for one KernelOp (a pre-pass before the main kernel)
+        built.extend(b if isinstance(b, list) else [b])
     text = modwriter.module_text(built)
     return CompiledModule(text, modwriter.parse_records(text))
 

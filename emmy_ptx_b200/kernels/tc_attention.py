@@ -20,12 +20,16 @@ Accum loop nest of the attention IR (config 5).  One CTA owns 256 query rows of 
   long as P and the row sum use the same one), after the previous PV has completed;
 * blocks above the diagonal are never computed; CTAs start with the longest rows.
 
-The tensor core multiplies bf16 by bf16, so P is written as two bf16 parts, P = P_hi + P_lo: P_hi is
-p truncated to bf16 and P_lo the exact remainder p - P_hi truncated to bf16, both taken with integer
-masks and byte permutes (the conversion unit stays free for ``ex2``), and O_i += P_hi V + P_lo V.  The
-sum keeps p to within 2^-14 relative, so the result matches an f32-P computation to within the
-output's bf16 rounding.  ``precise=False`` drops P_lo (one PV pass, P rounded to nearest bf16, 2^-9
-relative error per term).
+The tensor core multiplies operands of one type.  By default (``half``) the value pre-pass
+(:mod:`.vconv`, a separate launch just before this kernel) writes an f16 copy of V and one flag per
+64-row block; the producer loads a block's V from that copy when its flag is clear, the softmax writes P
+in f16 (rounded to nearest, 2^-12 relative) and one PV pass runs f16 x f16.  A flagged block (some |v|
+above 65,280, so it does not fit f16) is loaded from V itself and P is written as two bf16 parts,
+P = P_hi + P_lo (p truncated to bf16, and the exact remainder truncated to bf16, taken with integer
+masks and byte permutes), with two PV passes: p to within 2^-14.  The MMA accumulates both kinds into
+the same f32 O, so the choice is per block.  Either way the result matches an f32-P computation to
+within the output's bf16 rounding.  ``half=False`` uses the bf16 pair for every block;
+``precise=False`` writes one bf16 P (rounded to nearest, 2^-9 relative error per term).
 
 Every mbarrier wait is bounded (see :mod:`.ptxasm`); a time-out writes a code to the status word and
 leaves the loop, the producer waits (bounded) for its own loads, and TMEM is always freed.
@@ -43,8 +47,7 @@ Q_BYTES = BQ * D * 2             # 32 KiB: one Q tile
 Q_HALF = Q_BYTES // 2            # one 64-column TMA box of a Q tile
 KV_BYTES = BKV * D * 2           # 16 KiB: one K or V block
 KV_HALF = KV_BYTES // 2          # one 64-column TMA box of a K/V block
-THREADS = 384                    # warps 0-11; with the f16 path, warps 12-15 convert V (512 threads)
-CONV_WARPS = 4
+THREADS = 384
 TMEM_COLS = 512
 F16_MAX_BF16_BITS = 0x477F       # the largest bf16 magnitude (65280) below the f16 overflow threshold
 POLY_EVERY = 0                   # f16 path: every n-th exp2 on the FMA pipe (cubic); 0 = all on the MUFU, which measured fastest
@@ -70,10 +73,7 @@ SFULL = EMPTY + 8 * STAGES
 PFULL = SFULL + 8 * 2 * TILES
 PFREE = PFULL + 8 * 2 * TILES
 SLOT = PFREE + 8 * 2 * TILES
-VCONV = SLOT + 8                 # per V ring stage (stages 1, 3, 5, 7): block's V converted
-CSYNC = VCONV + 8 * 4            # per V ring stage: the converter warps' overflow votes are in
-FMT = CSYNC + 8 * 4              # per V ring stage: 1 when V and P are f16 for that block
-OVF = FMT + 4 * 4                # per V ring stage: overflow votes, bit = phase parity of the use
+VFLAGS = 256                     # per kv block of this CTA: 1 when V did not fit f16 (64 words)
 BAR_BYTES = 512
 
 TRACE_SLOTS = 66                 # per-CTA trace rows: kv blocks 0..64, then one row of CTA facts
@@ -92,10 +92,13 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`)."""
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
+    if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
+        raise ValueError("the f16 path keeps one flag per kv block in shared memory: S <= 4096")
     if trace and seq // BKV + 1 >= TRACE_SLOTS:
         raise ValueError("trace supports at most 64 key/value blocks")
     half = half and precise
-    threads = THREADS + (32 * CONV_WARPS if half else 0)
+    threads = THREADS
+    nblk = seq // BKV
     nt = seq // (BQ * TILES)
     grid = batch * heads * nt
     a = Asm()
@@ -142,7 +145,12 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"{'@' + guard + ' ' if guard else ''}st.global.u64 [{ad}], {ck};")
 
     tq, tk, tv = a.r("rd"), a.r("rd"), a.r("rd")
-    for reg, pname in ((tq, "p_tmQ"), (tk, "p_tmK"), (tv, "p_tmV")):
+    tmaps_used = [(tq, "p_tmQ"), (tk, "p_tmK"), (tv, "p_tmV")]
+    tv16 = None
+    if half:
+        tv16 = a.r("rd")
+        tmaps_used.append((tv16, "p_tmV16"))
+    for reg, pname in tmaps_used:
         a(f"mov.u64 {reg}, {pname};")
         a(f"cvta.param.u64 {reg}, {reg};")
 
@@ -184,11 +192,6 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"mbarrier.init.shared::cta.b64 [{bars}+{SFULL + 8 * (2 * i + b_)}], 1;")
             a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFULL + 8 * (2 * i + b_)}], 4;")
             a(f"mbarrier.init.shared::cta.b64 [{bars}+{PFREE + 8 * (2 * i + b_)}], 1;")
-    if half:
-        for u in range(4):
-            a(f"mbarrier.init.shared::cta.b64 [{bars}+{VCONV + 8 * u}], {CONV_WARPS};")
-            a(f"mbarrier.init.shared::cta.b64 [{bars}+{CSYNC + 8 * u}], {CONV_WARPS};")
-            a(f"st.shared.u32 [{bars}+{OVF + 4 * u}], 0;")
     a("fence.mbarrier_init.release.cluster;")
     a("fence.proxy.async.shared::cta;")
     a.label(l_init)
@@ -215,14 +218,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"@{pt0} st.global.u64 [{sad}], {sm64};")
 
     l_end = a.L("end")
-    l_prod, l_mma, l_mma1, l_soft, l_conv = a.L("prod"), a.L("mma"), a.L("mma1"), a.L("soft"), a.L("conv")
+    l_prod, l_mma, l_mma1, l_soft = a.L("prod"), a.L("mma"), a.L("mma1"), a.L("soft")
     pw0, pw2, pws = a.r("p"), a.r("p"), a.r("p")
     a(f"setp.eq.u32 {pw0}, {warp}, 0;")
     a(f"setp.eq.u32 {pw2}, {warp}, 2;")
-    if half:
-        pwc = a.r("p")
-        a(f"setp.ge.u32 {pwc}, {warp}, 12;")
-        a(f"@{pwc} bra {l_conv};")
     a(f"setp.ge.u32 {pws}, {warp}, 4;")
     a(f"@{pw0} bra {l_prod};")
     a(f"@{pw1} bra {l_mma};")
@@ -236,6 +235,25 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 
     # ---------------- producer ------------------------------------------------------------
     a.label(l_prod)
+    if half:
+        # the value pre-pass's per-block flags of this (batch, head) into shared memory (lane l
+        # loads blocks l and l + 32); they are published with the Q barrier's arrival below
+        vfp, vbase = a.r("rd"), a.r()
+        a(f"ld.param.u64 {vfp}, [p_vflag];")
+        a(f"cvta.to.global.u64 {vfp}, {vfp};")
+        a(f"mul.lo.u32 {vbase}, {bh}, {nblk};")
+        for k in range(2):
+            bk, pk, fk, ga, sa = a.r(), a.r("p"), a.r(), a.r("rd"), a.r()
+            a(f"add.u32 {bk}, {lane}, {32 * k};")
+            a(f"setp.lt.u32 {pk}, {bk}, {nb};")
+            a(f"add.u32 {fk}, {vbase}, {bk};")
+            a(f"mul.wide.u32 {ga}, {fk}, 4;")
+            a(f"add.s64 {ga}, {ga}, {vfp};")
+            a(f"@{pk} ld.global.nc.u32 {fk}, [{ga}];")
+            a(f"mad.lo.u32 {sa}, {bk}, 4, {bars};")
+            a(f"@{pk} st.shared.u32 [{sa}+{VFLAGS}], {fk};")
+        a("fence.acq_rel.cta;")
+        a("bar.warp.sync -1;")
     pl0 = a.r("p")
     a(f"setp.ne.u32 {pl0}, {lane}, 0;")
     a(f"@{pl0} bra {l_end};")
@@ -282,7 +300,18 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     andn = a.r()
     a(f"and.b32 {andn}, {n_}, 1;")
     a(f"setp.ne.u32 {isv}, {andn}, 0;")
-    a(f"selp.b64 {tsel}, {tv}, {tk}, {isv};")
+    if half:
+        # a V block that fit f16 comes from the pre-pass's f16 copy, a flagged one from V itself
+        vfl, vfa2, pvf = a.r(), a.r(), a.r("p")
+        a(f"shr.u32 {vfa2}, {n_}, 1;")
+        a(f"mad.lo.u32 {vfa2}, {vfa2}, 4, {bars};")
+        a(f"ld.shared.u32 {vfl}, [{vfa2}+{VFLAGS}];")
+        a(f"setp.eq.u32 {pvf}, {vfl}, 0;")
+        tvs = a.r("rd")
+        a(f"selp.b64 {tvs}, {tv16}, {tv}, {pvf};")
+        a(f"selp.b64 {tsel}, {tvs}, {tk}, {isv};")
+    else:
+        a(f"selp.b64 {tsel}, {tv}, {tk}, {isv};")
     tma4(dst, tsel, 0, kvrow, fb)
     dst2 = a.r()
     a(f"add.u32 {dst2}, {dst}, {KV_HALF};")
@@ -396,19 +425,19 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             over S_i[j & 1].  The P-full barrier of a buffer completes once per use, so block
             j = 4g + u waits for phase j >> 1, whose parity is (u >> 1) & 1.
 
-            With the f16 path the block's format flag (set by the V converters) picks the MMAs: f16 P
-            (columns 0-31, two f16 per column) times the converted f16 V in one pass, or, when V_j
-            did not fit f16, bf16 P_hi (columns 0-31) and P_lo (32-63) times the untouched bf16 V."""
+            With the f16 path the block's flag (from the value pre-pass) picks the MMAs: f16 P (columns
+            0-31, two f16 per column) times the f16 copy of V in one pass, or, when V_j did not fit
+            f16, bf16 P_hi (columns 0-31) and P_lo (32-63) times V itself."""
             vds = [plus(vd[stage_c], 2048 * k) for k in range(BKV // 16)]
             pacc = a.r("p")
             a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
             p16 = None
             if half:
-                wait_bar(a, f"{bars}+{VCONV + 8 * u}", gpreg, err, ERR_MMA, l_mdone)
-                fmt = a.r()
+                fa_, fmt = a.r(), a.r()
                 p16 = a.r("p")
-                a(f"ld.shared.u32 {fmt}, [{bars}+{FMT + 4 * u}];")
-                a(f"setp.ne.u32 {p16}, {fmt}, 0;")
+                a(f"mad.lo.u32 {fa_}, {jreg}, 4, {bars};")
+                a(f"ld.shared.u32 {fmt}, [{fa_}+{VFLAGS}];")
+                a(f"setp.eq.u32 {p16}, {fmt}, 0;")
             wait_bar(a, f"{bars}+{PFULL + 16 * i + 8 * buf_c}", str((u >> 1) & 1), err, ERR_MMA, l_mdone)
             stamp(4 + 2 * i, jreg)
             a("tcgen05.fence::after_thread_sync;")
@@ -502,97 +531,6 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     issuer(0, l_mma)
     issuer(1, l_mma1)
 
-    if half:
-        # ---------------- V converters (warps 12-15) ------------------------------------------------
-        # each V block is converted in place from bf16 to f16 (same element size, so the swizzled
-        # layout TMA wrote is kept) unless some |v| exceeds the largest bf16 value below the f16
-        # overflow threshold, in which case the block stays bf16 and its P is written as bf16 hi +
-        # lo.  The warps agree through an overflow word and a barrier with bounded waits.
-        a.label(l_conv)
-        ct, coff, cw, pcl0, pw12 = a.r(), a.r(), a.r(), a.r("p"), a.r("p")
-        a(f"sub.u32 {ct}, {tid}, {THREADS};")                 # 0..127
-        a(f"shl.b32 {coff}, {ct}, 4;")                        # this thread's 16-byte slots: coff + 2048 v
-        a(f"shr.u32 {cw}, {ct}, 5;")
-        a(f"setp.eq.u32 {pcl0}, {lane}, 0;")
-        a(f"setp.eq.u32 {pw12}, {ct}, 0;")
-        l_cdone = a.L("cdone")
-        cj = a.r()
-        a(f"mov.u32 {cj}, 0;")
-        l_cb = a.L("cb")
-        a.label(l_cb)
-        pend_ = a.r("p")
-        a(f"setp.ge.u32 {pend_}, {cj}, {nb};")
-        a(f"@{pend_} bra {l_cdone};")
-        # block j: V_j is ring item 2j+1, stage 2u+1 with u = j & 3, phase parity (j >> 2) & 1
-        cu, cst, cgp, cfb, cbase, cs8, cs4 = a.r(), a.r(), a.r(), a.r(), a.r(), a.r(), a.r()
-        a(f"and.b32 {cu}, {cj}, 3;")
-        a(f"mad.lo.u32 {cst}, {cu}, 2, 1;")
-        a(f"shr.u32 {cgp}, {cj}, 2;")
-        a(f"and.b32 {cgp}, {cgp}, 1;")
-        a(f"mad.lo.u32 {cfb}, {cst}, 8, {bars};")
-        a(f"mad.lo.u32 {cbase}, {cst}, {KV_BYTES}, {sKV};")
-        a(f"add.u32 {cbase}, {cbase}, {coff};")
-        a(f"mad.lo.u32 {cs8}, {cu}, 8, {bars};")            # per-stage barriers (CSYNC, VCONV)
-        a(f"mad.lo.u32 {cs4}, {cu}, 4, {bars};")            # per-stage words (OVF, FMT)
-        wait_bar_warp(a, f"{cfb}+{FULL}", cgp, err, ERR_SOFTMAX, l_cdone)
-        m = a.r()
-        a(f"mov.u32 {m}, 0;")
-        conv = []
-        for v in range(KV_BYTES // 16 // 128):
-            ws = [a.r() for _ in range(4)]
-            a(f"ld.shared.v4.b32 {{{', '.join(ws)}}}, [{cbase}+{2048 * v}];")
-            cv = []
-            for w in ws:
-                t_, lo_, hi_, f_ = a.r(), a.r("f"), a.r("f"), a.r()
-                a(f"and.b32 {t_}, {w}, 0x7FFF7FFF;")
-                a(f"max.u16x2 {m}, {m}, {t_};")
-                a(f"shl.b32 {lo_}, {w}, 16;")
-                a(f"and.b32 {hi_}, {w}, -65536;")
-                a(f"cvt.rn.f16x2.f32 {f_}, {hi_}, {lo_};")
-                cv.append(f_)
-            conv.append(cv)
-        mlo, mhi, po1, po2 = a.r(), a.r(), a.r("p"), a.r("p")
-        a(f"and.b32 {mlo}, {m}, 65535;")
-        a(f"shr.u32 {mhi}, {m}, 16;")
-        a(f"setp.gt.u32 {po1}, {mlo}, {F16_MAX_BF16_BITS};")
-        a(f"setp.gt.u32 {po2}, {mhi}, {F16_MAX_BF16_BITS};")
-        a(f"or.pred {po1}, {po1}, {po2};")
-        vany = a.r("p")
-        a(f"vote.sync.any.pred {vany}, {po1}, -1;")
-        vbit, vreg = a.r(), a.r()
-        a(f"shl.b32 {vbit}, 1, {cgp};")
-        a(f"selp.b32 {vreg}, {vbit}, 0, {vany};")
-        a(f"@{pcl0} atom.shared.or.b32 {a.r()}, [{cs4}+{OVF}], {vreg};")
-        a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{cs8}+{CSYNC}];")
-        wait_bar_warp(a, f"{cs8}+{CSYNC}", cgp, err, ERR_SOFTMAX, l_cdone)
-        ov, ovb, pov = a.r(), a.r(), a.r("p")
-        a(f"ld.shared.u32 {ov}, [{cs4}+{OVF}];")
-        a(f"and.b32 {ovb}, {ov}, {vbit};")
-        a(f"setp.ne.u32 {pov}, {ovb}, 0;")
-        l_nost = a.L("nost")
-        a(f"@{pov} bra {l_nost};")
-        for v, cv in enumerate(conv):
-            a(f"st.shared.v4.b32 [{cbase}+{2048 * v}], {{{', '.join(cv)}}};")
-        a.label(l_nost)
-        # the tensor core reads this stage through the async proxy
-        a("fence.proxy.async.shared::cta;")
-        a("bar.warp.sync -1;")
-        fmtv, nbit = a.r(), a.r()
-        a(f"selp.u32 {fmtv}, 0, 1, {pov};")
-        a(f"@{pw12} st.shared.u32 [{cs4}+{FMT}], {fmtv};")
-        # clear the other parity's vote bit for this stage's next use (block j+4); every warp has
-        # read this block's bit, and none can reach block j+4 before this warp's next arrival
-        ogp = a.r()
-        a(f"xor.b32 {ogp}, {cgp}, 1;")
-        a(f"shl.b32 {nbit}, 1, {ogp};")
-        a(f"not.b32 {nbit}, {nbit};")
-        a(f"@{pw12} atom.shared.and.b32 {a.r()}, [{cs4}+{OVF}], {nbit};")
-        a(f"@{pcl0} mbarrier.arrive.shared::cta.b64 _, [{cs8}+{VCONV}];")
-        a(f"add.u32 {cj}, {cj}, 1;")
-        a(f"bra {l_cb};")
-        a.label(l_cdone)
-        a(f"bra {l_end};")
-
     # ---------------- softmax warps ------------------------------------------------------------
     a.label(l_soft)
     ti, q, rowl = a.r(), a.r(), a.r()
@@ -638,6 +576,12 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"mad.lo.u32 {ev_s}, {ti}, 8, 8;")
         ptw = a.r("p")
         a(f"setp.eq.u32 {ptw}, {rowl}, 0;")
+    if half:
+        # the producer published the per-block flags with its Q-barrier arrival
+        qbs, zqs = a.r(), a.r()
+        a(f"add.u32 {qbs}, {bars}, {QFULL};")
+        a(f"mov.u32 {zqs}, 0;")
+        wait_bar_warp(a, qbs, zqs, err, ERR_SOFTMAX, l_end)
     s_ = [a.r("f") for _ in range(BKV)]
     mref, lsum, jj = a.r("f"), a.r("f"), a.r()
     a(f"mov.b32 {mref}, 0fFF800000;")
@@ -665,23 +609,16 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"shr.u32 {par_s}, {jj}, 1;")
     a(f"and.b32 {par_s}, {par_s}, 1;")
     a(f"mad.lo.u32 {scol}, {bsel}, {BKV}, {scol0};")
+    wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_sdone)
     p16 = None
     if half:
-        # the V converters' decision for this block: f16 P (rounded to nearest, 2^-12 relative) when
-        # V_j fit f16, else bf16 hi + lo.  Checked before the scores are ready: V_j is loaded
-        # before K_(j+1), so this wait usually overlaps the wait for S.
-        uu, vcb, vpar, fmt = a.r(), a.r(), a.r(), a.r()
+        # the value pre-pass's flag for this block: f16 P (rounded to nearest, 2^-12 relative) when
+        # V_j fit f16, else bf16 hi + lo
+        vfa, fmt = a.r(), a.r()
         p16 = a.r("p")
-        a(f"and.b32 {uu}, {jj}, 3;")
-        a(f"mad.lo.u32 {vcb}, {uu}, 8, {bars};")
-        a(f"add.u32 {vcb}, {vcb}, {VCONV};")
-        a(f"shr.u32 {vpar}, {jj}, 2;")
-        a(f"and.b32 {vpar}, {vpar}, 1;")
-        wait_bar_warp(a, vcb, vpar, err, ERR_SOFTMAX, l_sdone)
-        a(f"mad.lo.u32 {vcb}, {uu}, 4, {bars};")
-        a(f"ld.shared.u32 {fmt}, [{vcb}+{FMT}];")
-        a(f"setp.ne.u32 {p16}, {fmt}, 0;")
-    wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_sdone)
+        a(f"mad.lo.u32 {vfa}, {jj}, 4, {bars};")
+        a(f"ld.shared.u32 {fmt}, [{vfa}+{VFLAGS}];")
+        a(f"setp.eq.u32 {p16}, {fmt}, 0;")
     sstamp(0)
     a("tcgen05.fence::after_thread_sync;")
     for c in range(BKV // 32):
@@ -764,6 +701,30 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         x is clamped at -120, split as n + f with f in [-1/2, 1/2] by the 1.5*2^23 rounding trick,
         2^f comes from a cubic (``EXP2_C``), and n is added to the exponent field.  Only the f16 path
         uses it: there P rounds 2^-120 to zero, as the MUFU's 2^-inf is zero."""
+        cols = list(cols)
+        if not poly_every:
+            # two scores per instruction on the FMA pipe (f32x2 fma and add); the MUFU takes one each
+            cf, cp2, np2 = a.r("f"), a.r("rd"), a.r("rd")
+            a(f"mov.b32 {cf}, {cscale};")
+            a(f"mov.b64 {cp2}, {{{cf}, {cf}}};")
+            a(f"mov.b64 {np2}, {{{negm}, {negm}}};")
+            acc = [a.r("rd"), a.r("rd")]
+            a(f"mov.b64 {acc[0]}, {{{parts[0]}, {parts[1]}}};")
+            a(f"mov.b64 {acc[1]}, {{{parts[2]}, {parts[3]}}};")
+            for k, idx in enumerate(cols[::2]):
+                x0, x1 = s_[idx], s_[idx + 1]
+                xp = a.r("rd")
+                a(f"mov.b64 {xp}, {{{x0}, {x1}}};")
+                a(f"fma.rn.f32x2 {xp}, {xp}, {cp2}, {np2};")
+                a(f"mov.b64 {{{x0}, {x1}}}, {xp};")
+                a(f"ex2.approx.ftz.f32 {x0}, {x0};")
+                a(f"ex2.approx.ftz.f32 {x1}, {x1};")
+                ep = a.r("rd")
+                a(f"mov.b64 {ep}, {{{x0}, {x1}}};")
+                a(f"add.rn.f32x2 {acc[k & 1]}, {acc[k & 1]}, {ep};")
+            a(f"mov.b64 {{{parts[0]}, {parts[1]}}}, {acc[0]};")
+            a(f"mov.b64 {{{parts[2]}, {parts[3]}}}, {acc[1]};")
+            return
         t_, j_, f_, r_, ti_, ri_ = (a.r("f"), a.r("f"), a.r("f"), a.r("f"), a.r(), a.r())
         for idx in cols:
             x = s_[idx]
@@ -787,7 +748,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 
     l_pdone = a.L("pdone")
     if half:
-        # the format the V converters chose for this block (read at the top of the iteration)
+        # the format the value pre-pass chose for this block (read once S was ready)
         sstamp(3)
         l_pbf = a.L("pbf")
         a(f"@!{p16} bra {l_pbf};")
@@ -908,9 +869,14 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a.label(l_nodealloc)
 
     dyn = TILES * Q_BYTES + STAGES * KV_BYTES + BAR_BYTES + 1024
-    params = ["\t.param .u64 p_Q,", "\t.param .u64 p_K,", "\t.param .u64 p_V,", "\t.param .u64 p_O,",
-              "\t.param .align 64 .b8 p_tmQ[128],", "\t.param .align 64 .b8 p_tmK[128],",
-              "\t.param .align 64 .b8 p_tmV[128],", "\t.param .u64 p_err" + ("," if trace else "")]
+    params = ["\t.param .u64 p_Q,", "\t.param .u64 p_K,", "\t.param .u64 p_V,", "\t.param .u64 p_O,"]
+    if half:
+        params += ["\t.param .u64 p_V16,", "\t.param .u64 p_vflag,"]
+    params += ["\t.param .align 64 .b8 p_tmQ[128],", "\t.param .align 64 .b8 p_tmK[128],",
+               "\t.param .align 64 .b8 p_tmV[128],"]
+    if half:
+        params.append("\t.param .align 64 .b8 p_tmV16[128],")
+    params.append("\t.param .u64 p_err" + ("," if trace else ""))
     if trace:
         params.append("\t.param .u64 p_trace")
     entry = [f".visible .entry {name}("] + params + [")", f".reqntid {threads}, 1, 1",
@@ -923,14 +889,21 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
               "box": [64, BQ, 1, 1], "swizzle": "128B"}]
     tmaps += [{"name": f"tm{x}", "tensor": nm, "dtype": "bf16", "dims": dims, "strides": strides,
                "box": [64, BKV, 1, 1], "swizzle": "128B"} for x, nm in (("K", kn), ("V", vn))]
+    uparams = [qn, kn, vn, on]
+    if half:
+        v16n, vfn = f"{prefix}{name}__v16", f"{prefix}{name}__vflag"
+        uparams += [v16n, vfn]
+        tmaps.append({"name": "tmV16", "tensor": v16n, "dtype": "f16", "dims": dims, "strides": strides,
+                      "box": [64, BKV, 1, 1], "swizzle": "128B"})
     extra = [{"name": "__err", "kind": "errword"}]
     if trace:
         extra.append({"name": "__trace", "kind": "buffer"})
     return {
-        "name": name, "kind": "tcgen05_attention", "params": [qn, kn, vn, on],
+        "name": name, "kind": "tcgen05_attention", "params": uparams,
         "raw_entry": entry, "raw_decls": [f".extern .shared .align 1024 .b8 {smem_sym}[];"],
         "grid": [grid, 1, 1], "block": [threads, 1, 1], "dyn_smem": dyn,
-        "align": {qn: 16, kn: 16, vn: 16, on: 32}, "zero_outputs": [], "tmaps": tmaps,
+        "align": {qn: 16, kn: 16, vn: 16, on: 32, **({uparams[4]: 16, uparams[5]: 4} if half else {})},
+        "zero_outputs": [], "tmaps": tmaps,
         "extra": extra,
     }
 

@@ -1,0 +1,85 @@
+"""The attention kernel's value pre-pass: V bf16 -> f16 once per launch, with a per-block range flag.
+
+The tensor core multiplies operands of one type, so the f16 P of the attention kernel needs V in f16.
+Every 64-row key/value block of V [batch, heads, S, 128] is converted here (one CTA per block, 16-byte
+loads and stores, 256 threads) into a scratch tensor of the same shape, and the block's flag records
+whether it fits: 0 when every |v| is at most 65,280 (the largest bf16 value below the f16 overflow
+threshold), 1 otherwise.  The attention kernel then loads each block from the f16 copy or, for a
+flagged block, from V itself with P as two bf16 parts.  Each CTA writes its own flag, so nothing needs
+zeroing first.
+"""
+from __future__ import annotations
+
+from .ptxasm import Asm
+
+THREADS = 256
+BLOCK_ROWS = 64
+D = 128
+BLOCK_BYTES = BLOCK_ROWS * D * 2          # 16 KiB of bf16 in, the same of f16 out
+F16_MAX_BF16_BITS = 0x477F
+
+
+def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16", "__vflag")) -> dict:
+    if seq % BLOCK_ROWS:
+        raise ValueError("the value pre-pass needs S % 64 == 0")
+    blocks = batch * heads * (seq // BLOCK_ROWS)
+    vec = BLOCK_BYTES // 16 // THREADS      # 16-byte vectors per thread
+    a = Asm()
+    tid, blk = a.r(), a.r()
+    a(f"mov.u32 {tid}, %tid.x;")
+    a(f"mov.u32 {blk}, %ctaid.x;")
+    pv, p16, pf = a.r("rd"), a.r("rd"), a.r("rd")
+    for reg, pname in ((pv, "p_V"), (p16, "p_V16"), (pf, "p_flag")):
+        a(f"ld.param.u64 {reg}, [{pname}];")
+        a(f"cvta.to.global.u64 {reg}, {reg};")
+    off = a.r("rd")
+    a(f"mul.wide.u32 {off}, {blk}, {BLOCK_BYTES};")
+    t16 = a.r("rd")
+    a(f"mul.wide.u32 {t16}, {tid}, 16;")
+    a(f"add.s64 {off}, {off}, {t16};")
+    src, dst = a.r("rd"), a.r("rd")
+    a(f"add.s64 {src}, {pv}, {off};")
+    a(f"add.s64 {dst}, {p16}, {off};")
+    m = a.r()
+    a(f"mov.u32 {m}, 0;")
+    ws_all = []
+    for v in range(vec):
+        ws = [a.r() for _ in range(4)]
+        a(f"ld.global.nc.v4.b32 {{{', '.join(ws)}}}, [{src}+{v * THREADS * 16}];")
+        ws_all.append(ws)
+    for v, ws in enumerate(ws_all):
+        out = []
+        for w in ws:
+            t_, lo_, hi_, f_ = a.r(), a.r("f"), a.r("f"), a.r()
+            a(f"and.b32 {t_}, {w}, 0x7FFF7FFF;")
+            a(f"max.u16x2 {m}, {m}, {t_};")
+            a(f"shl.b32 {lo_}, {w}, 16;")
+            a(f"and.b32 {hi_}, {w}, -65536;")
+            a(f"cvt.rn.f16x2.f32 {f_}, {hi_}, {lo_};")
+            out.append(f_)
+        a(f"st.global.v4.b32 [{dst}+{v * THREADS * 16}], {{{', '.join(out)}}};")
+    mlo, mhi, p1, p2, ovf = a.r(), a.r(), a.r("p"), a.r("p"), a.r("p")
+    a(f"and.b32 {mlo}, {m}, 65535;")
+    a(f"shr.u32 {mhi}, {m}, 16;")
+    a(f"setp.gt.u32 {p1}, {mlo}, {F16_MAX_BF16_BITS};")
+    a(f"setp.gt.u32 {p2}, {mhi}, {F16_MAX_BF16_BITS};")
+    a(f"or.pred {p1}, {p1}, {p2};")
+    # the whole block's verdict (every thread of the CTA takes part; no wait on anything outside it)
+    a(f"bar.red.or.pred {ovf}, 0, {p1};")
+    p0 = a.r("p")
+    a(f"setp.eq.u32 {p0}, {tid}, 0;")
+    fv, fa = a.r(), a.r("rd")
+    a(f"selp.u32 {fv}, 1, 0, {ovf};")
+    a(f"mul.wide.u32 {fa}, {blk}, 4;")
+    a(f"add.s64 {fa}, {fa}, {pf};")
+    a(f"@{p0} st.global.u32 [{fa}], {fv};")
+    entry = [f".visible .entry {name}(", "\t.param .u64 p_V,", "\t.param .u64 p_V16,", "\t.param .u64 p_flag", ")",
+             f".reqntid {THREADS}, 1, 1", "{"] + a.decls() + a.lines + ["\tret;", "}"]
+    vn, v16n, fn = names
+    return {
+        "name": name, "kind": "value_prepass", "params": [vn, v16n, fn], "raw_entry": entry,
+        "grid": [blocks, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": 0,
+        "align": {vn: 16, v16n: 16, fn: 4}, "zero_outputs": [],
+        "scratch": [{"name": v16n, "dtype": "f16", "shape": [batch, heads, seq, D]},
+                    {"name": fn, "dtype": "i32", "shape": [blocks]}],
+    }

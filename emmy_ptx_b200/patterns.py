@@ -332,10 +332,16 @@ def try_lower(graph, node, kmeta, prefix, options):
         from .kernels import tc_attention
         if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES):
             return None
-        return tc_attention.attention_entry(node.op.name, bt, hd, seq, causal, scale,
+        precise = bool(options.get("attn_precise", True))
+        half = bool(options.get("attn_half", True)) and precise
+        attn = tc_attention.attention_entry(node.op.name, bt, hd, seq, causal, scale,
                                             names=(Q.name, K.name, V.name, O.name), prefix=prefix,
-                                            precise=bool(options.get("attn_precise", True)),
-                                            trace=bool(options.get("attn_trace", False)),
-                                            half=bool(options.get("attn_half", True)),
+                                            precise=precise, trace=bool(options.get("attn_trace", False)),
+                                            half=half,
                                             poly_every=int(options.get("attn_poly", tc_attention.POLY_EVERY)))
+        if not half:
+            return attn
+        from .kernels import vconv
+        pre = vconv.vconv_entry(f"{node.op.name}_vconv", bt, hd, seq, names=(V.name,) + tuple(attn["params"][4:6]))
+        return [pre, attn]
     return None

@@ -12,6 +12,7 @@ import ctypes
 
 from .compiler import CompiledModule, compile_ir
 from .launcher import Device
+from .data import torch_dtype
 
 _TMAP_DTYPE = {"u8": 0, "f16": 6, "f32": 7, "bf16": 9}   # CUtensorMapDataType (cuda.h)
 _SWIZZLE = {"none": 0, "32B": 1, "64B": 2, "128B": 3}
@@ -43,6 +44,14 @@ class Executable:
                 self.dev.set_max_dyn_smem(fn, rec["dyn_smem"])
             self.funcs.append(fn)
         self._tmap_cache: dict = {}
+        # device scratch some lowerings need between their entries (e.g. the attention's f16 copy of V),
+        # allocated once per Executable and passed to the entries by name
+        self.scratch: dict = {}
+        for rec in compiled.kernels:
+            for spec in rec.get("scratch", []):
+                if spec["name"] not in self.scratch:
+                    self.scratch[spec["name"]] = torch.empty(tuple(spec["shape"]), dtype=torch_dtype(spec["dtype"]),
+                                                             device=f"cuda:{self.index}")
         self.err = None
         if any(spec.get("kind") == "errword" for rec in compiled.kernels for spec in rec.get("extra", [])):
             self.err = torch.zeros(4, dtype=torch.int32, device=f"cuda:{self.index}")
@@ -90,6 +99,8 @@ class Executable:
 
     def launch(self, i: int, tensors: dict, stream: int, grid=None, zero: bool = True) -> None:
         """Launch entry ``i`` with its parameters taken from ``tensors`` by name."""
+        if self.scratch:
+            tensors = {**self.scratch, **tensors}
         rec = self.records[i]
         fn = self.funcs[i]
         if zero:

@@ -210,5 +210,5 @@ def test_attention_variants_only_use_initialised_barriers(causal, precise, half)
     used = {int(m) for m in re.findall(r"mbarrier\.(?:try_wait\.parity|arrive)[^\[]*\[" + re.escape(base) + r"\+(\d+)\]", body)}
     used |= {int(m) for m in re.findall(r"tcgen05\.commit[^\[]*\[" + re.escape(base) + r"\+(\d+)\]", body)}
     assert used and used <= inited, sorted(used - inited)
-    assert e["block"][0] == (512 if (half and precise) else 384)
+    assert e["block"][0] == 384
     assert undefined_uses(".version 8.8\n.target sm_100a\n.address_size 64\n" + body) == []

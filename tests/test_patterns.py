@@ -81,8 +81,10 @@ def test_attention_ir_is_recognised():
         assert (bt, hd, seq, dim, c) == (p.params["batch"], p.params["heads"], p.params["seq"], p.params["dim"], causal)
         assert abs(scale - p.params["scale"]) < 1e-7
     full = irgen.FULL["c5"]()
-    rec = compile_graph(Graph.from_dict(full.graph), full.meta()).kernels[0]
-    assert rec["kind"] == "tcgen05_attention" and rec["block"] == [512, 1, 1] and rec["grid"] == [4096, 1, 1]
+    recs = compile_graph(Graph.from_dict(full.graph), full.meta()).kernels
+    assert [r["kind"] for r in recs] == ["value_prepass", "tcgen05_attention"]
+    rec = recs[1]
+    assert rec["kind"] == "tcgen05_attention" and rec["block"] == [384, 1, 1] and rec["grid"] == [4096, 1, 1]
 
 
 def test_attention_with_a_different_mask_is_refused():
