@@ -1323,11 +1323,18 @@ class KernelEmitter:
         self.prepare()
         self.prologue()
         self.stmts(self.op.body)
+        body, decls = self.b.lines(), self.b.reg_decls()
+        if self.opts.get("regalloc", os.environ.get("EMMY_B200_REGALLOC", "1") != "0"):
+            from .regalloc import allocate
+            from .ptx import REG_CLASSES
+            body, counts = allocate(body)
+            by_prefix = {pre[1:]: ty for pre, ty in REG_CLASSES.values()}
+            decls = [f"\t.reg {by_prefix[c]} %{c}<{k + 1}>;" for c, k in sorted(counts.items())]
         return {
             "name": self.name,
             "params": list(self.params),
-            "body": self.b.lines(),
-            "decls": self.b.reg_decls(),
+            "body": body,
+            "decls": decls,
             "smem": [(self.sym_name(n), self.smem_off[n], self.smem[n]) for n in self.smem],
             "smem_total": self.smem_total,
             "dyn": self.dyn,
