@@ -87,9 +87,11 @@ def _f32(v: float) -> str:
 
 def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, scale: float,
                     names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True,
-                    trace: bool = False, half: bool = True, poly_every: int = POLY_EVERY) -> dict:
+                    trace: bool = False, half: bool = True, poly_every: int = POLY_EVERY,
+                    pingpong: bool = True) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
-    grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`)."""
+    grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
+    ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps."""
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
@@ -576,28 +578,76 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"mad.lo.u32 {ev_s}, {ti}, 8, 8;")
         ptw = a.r("p")
         a(f"setp.eq.u32 {ptw}, {rowl}, 0;")
+    jj, failed = a.r(), a.r()
+    a(f"mov.u32 {jj}, 0;")
+    a(f"mov.u32 {failed}, 0;")
+    l_sdone = a.L("sdone")
+    l_drain, l_drain_post = (a.L("drain"), a.L("drainpost")) if pingpong else (l_sdone, l_sdone)
+    if pingpong:
+        # The two tiles' softmax warpgroups take turns on the MUFU: tile 0's exps of block j, then
+        # tile 1's, then tile 0's of block j+1, ...  Each hands the turn over with a named barrier
+        # (tile 0 waits on barrier 1 and passes on barrier 2, tile 1 the reverse; 256 threads: one
+        # warpgroup syncs, the other arrives), so while one tile's exps run the other loads its
+        # scores, takes the row max and writes P.  Tile 1 has two blocks more than tile 0 on the
+        # causal diagonal and runs those alone.  Every softmax thread executes the same sequence of
+        # barrier operations whatever happens: a time-out leaves the work but not the hand-overs
+        # (the drain below), so neither warpgroup can be left waiting on the other.
+        last0, bown, both_, arr_lim = a.r(), a.r(), a.r(), a.r()
+        if causal:
+            a(f"shl.b32 {last0}, {t}, 2;")
+            a(f"add.u32 {last0}, {last0}, 1;")             # tile 0's last kv block
+        else:
+            a(f"sub.u32 {last0}, {nb}, 1;")
+        a(f"add.u32 {bown}, {ti}, 1;")
+        a(f"xor.b32 {both_}, {bown}, 3;")
+        a(f"sub.u32 {arr_lim}, {last0}, {ti};")
+        a(f"add.u32 {arr_lim}, {arr_lim}, 1;")             # pass the turn while jj < arr_lim
+        pt1_, l_noinit = a.r("p"), a.L("noturn0")
+        a(f"setp.eq.u32 {pt1_}, {ti}, 1;")
+        a(f"@!{pt1_} bra {l_noinit};")
+        a("bar.arrive 1, 256;")                              # tile 0 goes first
+        a.label(l_noinit)
+
+    def turn_wait():
+        if not pingpong:
+            return
+        pw_, l_ = a.r("p"), a.L("noturnw")
+        a(f"setp.gt.u32 {pw_}, {jj}, {last0};")
+        a(f"@{pw_} bra {l_};")
+        a(f"bar.sync {bown}, 256;")
+        a.label(l_)
+
+    def turn_pass():
+        if not pingpong:
+            return
+        pp_, l_ = a.r("p"), a.L("noturnp")
+        a(f"setp.ge.u32 {pp_}, {jj}, {arr_lim};")
+        a(f"@{pp_} bra {l_};")
+        a(f"bar.arrive {both_}, 256;")
+        a.label(l_)
+
+    s_ = [a.r("f") for _ in range(BKV)]
+    mref, lsum = a.r("f"), a.r("f")
+    a(f"mov.b32 {mref}, 0fFF800000;")
+    a(f"mov.b32 {lsum}, 0f00000000;")
     if half:
         # the producer published the per-block flags with its Q-barrier arrival
         qbs, zqs = a.r(), a.r()
         a(f"add.u32 {qbs}, {bars}, {QFULL};")
         a(f"mov.u32 {zqs}, 0;")
-        wait_bar_warp(a, qbs, zqs, err, ERR_SOFTMAX, l_end)
-    s_ = [a.r("f") for _ in range(BKV)]
-    mref, lsum, jj = a.r("f"), a.r("f"), a.r()
-    a(f"mov.b32 {mref}, 0fFF800000;")
-    a(f"mov.b32 {lsum}, 0f00000000;")
-    a(f"mov.u32 {jj}, 0;")
+        wait_bar_warp(a, qbs, zqs, err, ERR_SOFTMAX, l_drain if pingpong else l_end)
 
     def sstamp(k):
-        """Softmax timeline stamp ``k`` (0 S ready, 1 S loaded, 2 row max, 3 format known, 4 exps
-        done, 5 P stores issued, 6 P written) for this tile, from the tile's first thread."""
+        """Softmax timeline stamp ``k`` (0 S ready, 1 S loaded, 2 row max, 3 format known, 7 MUFU turn
+        taken, 4 exps done, 5 P stores issued, 6 P written) for this tile, from the tile's first
+        thread."""
         if not trace:
             return
         ev = a.r()
         a(f"add.u32 {ev}, {ev_s}, {k};")
         stamp(ev, jj, ptw)
 
-    l_sj, l_sdone = a.L("sj"), a.L("sdone")
+    l_sj = a.L("sj")
     a.label(l_sj)
     pj = a.r("p")
     a(f"setp.gt.u32 {pj}, {jj}, {last};")
@@ -609,7 +659,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"shr.u32 {par_s}, {jj}, 1;")
     a(f"and.b32 {par_s}, {par_s}, 1;")
     a(f"mad.lo.u32 {scol}, {bsel}, {BKV}, {scol0};")
-    wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_sdone)
+    wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_drain)
     p16 = None
     if half:
         # the value pre-pass's flag for this block: f16 P (rounded to nearest, 2^-12 relative) when
@@ -750,12 +800,18 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     if half:
         # the format the value pre-pass chose for this block (read once S was ready)
         sstamp(3)
+    turn_wait()
+    sstamp(7)
+    if half:
         l_pbf = a.L("pbf")
         a(f"@!{p16} bra {l_pbf};")
         half_n = BKV // 2
         for h in range(2):
             # each half of the row is packed and stored as soon as its exps are done
             exp_block(poly_every, range(half_n * h, half_n * (h + 1)))
+            if h == 1:
+                sstamp(4)
+                turn_pass()
             hw = []
             for k in range(half_n * h // 2, half_n * (h + 1) // 2):
                 w = a.r()
@@ -764,11 +820,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             dsth = a.r()
             a(f"add.u32 {dsth}, {scol}, {len(hw) * h};")
             a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dsth}], {{{', '.join(hw)}}};")
-        sstamp(4)
         sstamp(5)
         a(f"bra {l_pdone};")
         a.label(l_pbf)
     exp_block(0)
+    turn_pass()
     hi_w, lo_w = [], []
     for k in range(BKV // 2):
         i0, i1 = 2 * k, 2 * k + 1
@@ -804,7 +860,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"@!{anyneed} bra {l_norescale2};")
     prev = a.r()
     a(f"sub.u32 {prev}, {jj}, 1;")
-    pv_done(prev, l_sdone, ERR_SOFTMAX)
+    pv_done(prev, l_drain_post, ERR_SOFTMAX)
     a("tcgen05.fence::after_thread_sync;")
     for c in range(D // 32):
         src = a.r()
@@ -823,11 +879,29 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"@{ple} mbarrier.arrive.shared::cta.b64 _, [{pfb}];")
     a(f"add.u32 {jj}, {jj}, 1;")
     a(f"bra {l_sj};")
+    if pingpong:
+        # after a time-out: the remaining blocks' turn hand-overs without their work (from block jj,
+        # or from jj + 1 when block jj's were already made)
+        l_dl = a.L("dloop")
+        a.label(l_drain_post)
+        a(f"add.u32 {jj}, {jj}, 1;")
+        a.label(l_drain)
+        a(f"mov.u32 {failed}, 1;")
+        a.label(l_dl)
+        pdx = a.r("p")
+        a(f"setp.gt.u32 {pdx}, {jj}, {last};")
+        a(f"@{pdx} bra {l_sdone};")
+        turn_wait()
+        turn_pass()
+        a(f"add.u32 {jj}, {jj}, 1;")
+        a(f"bra {l_dl};")
     a.label(l_sdone)
     # epilogue: after the last PV, O / l to global memory as bf16
     l_noepi = a.L("noepi")
-    pok = a.r("p")
+    pok, pfl = a.r("p"), a.r("p")
     a(f"setp.le.u32 {pok}, {jj}, {last};")                  # left early (time-out): no store
+    a(f"setp.ne.u32 {pfl}, {failed}, 0;")
+    a(f"or.pred {pok}, {pok}, {pfl};")
     a(f"@{pok} bra {l_noepi};")
     pv_done(last, l_noepi, ERR_EPILOGUE)                    # the last PV, and so every earlier one
     a("tcgen05.fence::after_thread_sync;")
@@ -911,8 +985,9 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 def trace_events(buf, grid: int):
     """Split a ``trace`` buffer (u64 [grid, 66, 24]) into per-CTA timelines.  For kv block j, events
     0-7 are tile 0's issuer's iteration start, K_(j+1) arrived, S(j+1) issued and V_j arrived,
-    then P_0(j) ready, PV_0 issued, P_1(j) ready and PV_1 issued (each tile's issuer); 8-14 (tile 0)
-    and 16-22 (tile 1) are the softmax's S(j) ready, S loaded, row max, format known, exps done,
-    P stores issued and P(j) written.  Row 65 holds CTA start, end and the SM id."""
+    then P_0(j) ready, PV_0 issued, P_1(j) ready and PV_1 issued (each tile's issuer); 8-15 (tile 0)
+    and 16-23 (tile 1) are the softmax's S(j) ready, S loaded, row max, format known, exps done,
+    P stores issued, P(j) written and (last) MUFU turn taken.  Row 65 holds CTA start, end and the
+    SM id."""
     import numpy as np
     return np.asarray(buf, dtype=np.uint64).reshape(grid, TRACE_SLOTS, TRACE_EVENTS)

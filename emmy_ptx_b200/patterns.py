@@ -338,7 +338,8 @@ def try_lower(graph, node, kmeta, prefix, options):
                                             names=(Q.name, K.name, V.name, O.name), prefix=prefix,
                                             precise=precise, trace=bool(options.get("attn_trace", False)),
                                             half=half,
-                                            poly_every=int(options.get("attn_poly", tc_attention.POLY_EVERY)))
+                                            poly_every=int(options.get("attn_poly", tc_attention.POLY_EVERY)),
+                                            pingpong=bool(options.get("attn_pingpong", True)))
         if not half:
             return attn
         from .kernels import vconv
