@@ -385,8 +385,7 @@ def main() -> int:
         with torch.cuda.graph(g_kern):
             cs = torch.cuda.current_stream().cuda_stream
             for i in range(reps):
-                for k in range(len(mod.kernels)):     # every entry of the module (a pre-pass included)
-                    ex.launch(k, sets[i % rotate], cs, zero=False)
+                ex.run(sets[i % rotate], cs, zero=False)   # every entry of the module (a pre-pass included)
         graphs = [g_steps, g_kern]
         g_steps.replay()
         g_kern.replay()
@@ -420,8 +419,7 @@ def main() -> int:
         graphs[1].replay()
     else:
         for i in range(reps):
-            for k in range(len(mod.kernels)):
-                ex.launch(k, sets[i % rotate], stream, zero=False)
+            ex.run(sets[i % rotate], stream, zero=False)
     k1.record()
     torch.cuda.synchronize()
     clock = clocks.stop() if clocks else None

@@ -46,9 +46,11 @@ def launch_record(b: dict) -> dict:
         "zero_outputs": b.get("zero_outputs", []),
         "kind": b.get("kind", "generic"),
     }
-    for k in ("tmaps", "cluster", "extra", "pdl", "scratch"):
+    for k in ("tmaps", "cluster", "extra", "pdl", "scratch", "stream", "after"):
         if b.get(k):
             rec[k] = b[k]
+    if b.get("carveout") is not None:
+        rec["carveout"] = int(b["carveout"])
     return rec
 
 

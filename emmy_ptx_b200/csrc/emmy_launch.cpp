@@ -53,6 +53,9 @@ struct Driver {
   CUresult (*EventSynchronize)(CUevent);
   CUresult (*EventElapsedTime)(float*, CUevent, CUevent);
   CUresult (*StreamSynchronize)(CUstream);
+  CUresult (*StreamCreate)(CUstream*, unsigned int);
+  CUresult (*StreamDestroy)(CUstream);
+  CUresult (*StreamWaitEvent)(CUstream, CUevent, unsigned int);
   CUresult (*MemAlloc)(CUdeviceptr*, size_t);
   CUresult (*MemFree)(CUdeviceptr);
   CUresult (*MemsetD32Async)(CUdeviceptr, unsigned int, size_t, CUstream);
@@ -103,6 +106,9 @@ int load_driver() {
             sym(lib, d.EventSynchronize, "cuEventSynchronize") &&
             sym(lib, d.EventElapsedTime, "cuEventElapsedTime") &&
             sym(lib, d.StreamSynchronize, "cuStreamSynchronize") &&
+            sym(lib, d.StreamCreate, "cuStreamCreate") &&
+            sym(lib, d.StreamDestroy, "cuStreamDestroy_v2") &&
+            sym(lib, d.StreamWaitEvent, "cuStreamWaitEvent") &&
             sym(lib, d.MemAlloc, "cuMemAlloc_v2") && sym(lib, d.MemFree, "cuMemFree_v2") &&
             sym(lib, d.MemsetD32Async, "cuMemsetD32Async") &&
             sym(lib, d.MemcpyHtoDAsync, "cuMemcpyHtoDAsync_v2") &&
@@ -267,6 +273,15 @@ int emmy_set_max_dyn_smem(void* function, int bytes) {
             "cuFuncSetAttribute(MAX_DYNAMIC_SHARED_SIZE_BYTES)");
 }
 
+int emmy_set_smem_carveout(void* function, int percent) {
+  if (!function) return fail(EMMY_ERR_BAD_ARG, "null function");
+  if (percent < -1 || percent > 100) return fail(EMMY_ERR_BAD_ARG, "carveout outside -1..100");
+  if (int rc = ready()) return rc;
+  return cu(g_drv.FuncSetAttribute(static_cast<CUfunction>(function),
+                                   CU_FUNC_ATTRIBUTE_PREFERRED_SHARED_MEMORY_CARVEOUT, percent),
+            "cuFuncSetAttribute(PREFERRED_SHARED_MEMORY_CARVEOUT)");
+}
+
 int emmy_func_attribute(void* function, int attr, int* value) {
   if (!function || !value) return fail(EMMY_ERR_BAD_ARG, "null argument");
   if (int rc = ready()) return rc;
@@ -396,6 +411,38 @@ int emmy_event_elapsed_ms(void* start, void* stop, float* ms) {
   if (int rc = ready()) return rc;
   return cu(g_drv.EventElapsedTime(ms, static_cast<CUevent>(start), static_cast<CUevent>(stop)),
             "cuEventElapsedTime");
+}
+
+int emmy_event_create_flags(void** event, unsigned int flags) {
+  if (!event) return fail(EMMY_ERR_BAD_ARG, "null event pointer");
+  if (flags & ~0x3u) return fail(EMMY_ERR_BAD_ARG, "unknown event flags");
+  if (int rc = ready()) return rc;
+  CUevent ev;
+  if (int rc = cu(g_drv.EventCreate(&ev, flags), "cuEventCreate")) return rc;
+  *event = ev;
+  return 0;
+}
+
+int emmy_stream_create(void** stream) {
+  if (!stream) return fail(EMMY_ERR_BAD_ARG, "null stream pointer");
+  if (int rc = ready()) return rc;
+  CUstream s;
+  if (int rc = cu(g_drv.StreamCreate(&s, CU_STREAM_NON_BLOCKING), "cuStreamCreate")) return rc;
+  *stream = s;
+  return 0;
+}
+
+int emmy_stream_destroy(void* stream) {
+  if (!stream) return fail(EMMY_ERR_BAD_ARG, "null stream");
+  if (int rc = ready()) return rc;
+  return cu(g_drv.StreamDestroy(static_cast<CUstream>(stream)), "cuStreamDestroy");
+}
+
+int emmy_stream_wait_event(void* stream, void* event) {
+  if (!event) return fail(EMMY_ERR_BAD_ARG, "null event");
+  if (int rc = ready()) return rc;
+  return cu(g_drv.StreamWaitEvent(static_cast<CUstream>(stream), static_cast<CUevent>(event), 0),
+            "cuStreamWaitEvent");
 }
 
 int emmy_stream_synchronize(void* stream) {

@@ -88,10 +88,13 @@ def _f32(v: float) -> str:
 def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, scale: float,
                     names=("Q", "K", "V", "O"), prefix: str = "", precise: bool = True,
                     trace: bool = False, half: bool = True, poly_every: int = POLY_EVERY,
-                    pingpong: bool = True) -> dict:
+                    pingpong: bool = True, f16_int: int = 0, pack_after_turn: bool = False,
+                    defer_sum: bool = False, bh_range: tuple[int, int] | None = None,
+                    scratch_names: tuple[str, str] | None = None) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
-    ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps."""
+    ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps.
+    ``bh_range`` = (first, count) restricts the launch to those flattened (batch, head) pairs."""
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
@@ -99,10 +102,15 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     if trace and seq // BKV + 1 >= TRACE_SLOTS:
         raise ValueError("trace supports at most 64 key/value blocks")
     half = half and precise
+    if defer_sum and (poly_every or not pack_after_turn):
+        raise ValueError("defer_sum goes with the MUFU-only exps packed after the turn")
     threads = THREADS
     nblk = seq // BKV
     nt = seq // (BQ * TILES)
-    grid = batch * heads * nt
+    bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
+    if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):
+        raise ValueError(f"bh_range {bh_range} outside the {batch * heads} (batch, head) pairs")
+    grid = nbh * nt
     a = Asm()
     idesc_qk = idesc_f16(BQ, BKV, False, False)
     idesc_pv = idesc_f16(BQ, D, False, True)
@@ -158,9 +166,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 
     # work unit: longest causal rows first
     t, bh, bb, hh = a.r(), a.r(), a.r(), a.r()
-    a(f"div.u32 {t}, {cta}, {batch * heads};")
+    a(f"div.u32 {t}, {cta}, {nbh};")
     a(f"sub.u32 {t}, {nt - 1}, {t};")
-    a(f"rem.u32 {bh}, {cta}, {batch * heads};")
+    a(f"rem.u32 {bh}, {cta}, {nbh};")
+    if bh0:
+        a(f"add.u32 {bh}, {bh}, {bh0};")
     a(f"div.u32 {bb}, {bh}, {heads};")
     a(f"rem.u32 {hh}, {bh}, {heads};")
     nb, row0 = a.r(), a.r()
@@ -592,14 +602,14 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         # causal diagonal and runs those alone.  Every softmax thread executes the same sequence of
         # barrier operations whatever happens: a time-out leaves the work but not the hand-overs
         # (the drain below), so neither warpgroup can be left waiting on the other.
-        last0, bown, both_, arr_lim = a.r(), a.r(), a.r(), a.r()
+        last0, arr_lim = a.r(), a.r()
+        tile0 = a.r("p")
         if causal:
             a(f"shl.b32 {last0}, {t}, 2;")
             a(f"add.u32 {last0}, {last0}, 1;")             # tile 0's last kv block
         else:
             a(f"sub.u32 {last0}, {nb}, 1;")
-        a(f"add.u32 {bown}, {ti}, 1;")
-        a(f"xor.b32 {both_}, {bown}, 3;")
+        a(f"setp.eq.u32 {tile0}, {ti}, 0;")
         a(f"sub.u32 {arr_lim}, {last0}, {ti};")
         a(f"add.u32 {arr_lim}, {arr_lim}, 1;")             # pass the turn while jj < arr_lim
         pt1_, l_noinit = a.r("p"), a.L("noturn0")
@@ -614,7 +624,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         pw_, l_ = a.r("p"), a.L("noturnw")
         a(f"setp.gt.u32 {pw_}, {jj}, {last0};")
         a(f"@{pw_} bra {l_};")
-        a(f"bar.sync {bown}, 256;")
+        a(f"@{tile0} bar.sync 1, 256;")
+        a(f"@!{tile0} bar.sync 2, 256;")
         a.label(l_)
 
     def turn_pass():
@@ -623,7 +634,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         pp_, l_ = a.r("p"), a.L("noturnp")
         a(f"setp.ge.u32 {pp_}, {jj}, {arr_lim};")
         a(f"@{pp_} bra {l_};")
-        a(f"bar.arrive {both_}, 256;")
+        a(f"@{tile0} bar.arrive 2, 256;")
+        a(f"@!{tile0} bar.arrive 1, 256;")
         a.label(l_)
 
     s_ = [a.r("f") for _ in range(BKV)]
@@ -745,7 +757,19 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     parts = [a.r("f") for _ in range(4)]
     for pp in parts:
         a(f"mov.b32 {pp}, 0f00000000;")
-    def exp_block(poly_every, cols=range(BKV)):
+    def row_sum(cols):
+        """parts += the row's p values over ``cols`` (pairs, on the FMA pipe)."""
+        acc = [a.r("rd"), a.r("rd")]
+        a(f"mov.b64 {acc[0]}, {{{parts[0]}, {parts[1]}}};")
+        a(f"mov.b64 {acc[1]}, {{{parts[2]}, {parts[3]}}};")
+        for k, idx in enumerate(list(cols)[::2]):
+            ep = a.r("rd")
+            a(f"mov.b64 {ep}, {{{s_[idx]}, {s_[idx + 1]}}};")
+            a(f"add.rn.f32x2 {acc[k & 1]}, {acc[k & 1]}, {ep};")
+        a(f"mov.b64 {{{parts[0]}, {parts[1]}}}, {acc[0]};")
+        a(f"mov.b64 {{{parts[2]}, {parts[3]}}}, {acc[1]};")
+
+    def exp_block(poly_every, cols=range(BKV), sums=True):
         """p = 2^(s*c - m) for the row's BKV scores, summed into ``parts``.  With ``poly_every`` = n,
         every n-th value is taken on the FMA pipe instead of the MUFU (the softmax's bottleneck):
         x is clamped at -120, split as n + f with f in [-1/2, 1/2] by the 1.5*2^23 rounding trick,
@@ -769,9 +793,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                 a(f"mov.b64 {{{x0}, {x1}}}, {xp};")
                 a(f"ex2.approx.ftz.f32 {x0}, {x0};")
                 a(f"ex2.approx.ftz.f32 {x1}, {x1};")
-                ep = a.r("rd")
-                a(f"mov.b64 {ep}, {{{x0}, {x1}}};")
-                a(f"add.rn.f32x2 {acc[k & 1]}, {acc[k & 1]}, {ep};")
+                if sums:
+                    ep = a.r("rd")
+                    a(f"mov.b64 {ep}, {{{x0}, {x1}}};")
+                    a(f"add.rn.f32x2 {acc[k & 1]}, {acc[k & 1]}, {ep};")
             a(f"mov.b64 {{{parts[0]}, {parts[1]}}}, {acc[0]};")
             a(f"mov.b64 {{{parts[2]}, {parts[3]}}}, {acc[1]};")
             return
@@ -796,6 +821,27 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                 a(f"ex2.approx.ftz.f32 {x}, {x};")
             a(f"add.f32 {parts[idx & 3]}, {parts[idx & 3]}, {x};")
 
+    c112 = None
+
+    def f16_pack_int(w, x0, x1):
+        """w = the f16 pair (x1, x0) for 0 <= x <= 1, on the FMA and integer pipes instead of the
+        conversion unit: x * 2^-112 (subnormals kept) has the f16 exponent bias, so its bits >> 13 are
+        the f16 bits, normal and subnormal alike; adding 2^12 first rounds to nearest (ties away
+        from zero), and a carry out of the mantissa moves into the exponent as it should."""
+        nonlocal c112
+        if c112 is None:
+            c112 = a.r("rd")
+            a(f"mov.b64 {c112}, 0x0780000007800000;")     # {2^-112, 2^-112}
+        yp, y0, y1 = a.r("rd"), a.r(), a.r()
+        a(f"mov.b64 {yp}, {{{x0}, {x1}}};")
+        a(f"mul.rn.f32x2 {yp}, {yp}, {c112};")
+        a(f"mov.b64 {{{y0}, {y1}}}, {yp};")
+        a(f"add.u32 {y0}, {y0}, 4096;")
+        a(f"add.u32 {y1}, {y1}, 4096;")
+        a(f"shr.u32 {y0}, {y0}, 13;")
+        a(f"shl.b32 {y1}, {y1}, 3;")
+        a(f"lop3.b32 {w}, {y1}, {y0}, -65536, 0xEC;")     # (y1 & 0xFFFF0000) | y0
+
     l_pdone = a.L("pdone")
     if half:
         # the format the value pre-pass chose for this block (read once S was ready)
@@ -806,20 +852,36 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         l_pbf = a.L("pbf")
         a(f"@!{p16} bra {l_pbf};")
         half_n = BKV // 2
-        for h in range(2):
-            # each half of the row is packed and stored as soon as its exps are done
-            exp_block(poly_every, range(half_n * h, half_n * (h + 1)))
-            if h == 1:
-                sstamp(4)
-                turn_pass()
+
+        def pack_store(pairs, col):
             hw = []
-            for k in range(half_n * h // 2, half_n * (h + 1) // 2):
+            for k in pairs:
                 w = a.r()
-                a(f"cvt.rn.f16x2.f32 {w}, {s_[2 * k + 1]}, {s_[2 * k]};")
+                if f16_int and k % f16_int == f16_int - 1:
+                    f16_pack_int(w, s_[2 * k], s_[2 * k + 1])
+                else:
+                    a(f"cvt.rn.f16x2.f32 {w}, {s_[2 * k + 1]}, {s_[2 * k]};")
                 hw.append(w)
             dsth = a.r()
-            a(f"add.u32 {dsth}, {scol}, {len(hw) * h};")
-            a(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{dsth}], {{{', '.join(hw)}}};")
+            a(f"add.u32 {dsth}, {scol}, {col};")
+            a(f"tcgen05.st.sync.aligned.32x32b.x{len(hw)}.b32 [{dsth}], {{{', '.join(hw)}}};")
+        if pack_after_turn:
+            # only the exps hold the MUFU turn; the f16 packing and the TMEM store of P overlap the
+            # other tile's exps
+            exp_block(poly_every, sums=not defer_sum)
+            sstamp(4)
+            turn_pass()
+            if defer_sum:
+                row_sum(range(BKV))
+            pack_store(range(BKV // 2), 0)
+        else:
+            for h in range(2):
+                # each half of the row is packed and stored as soon as its exps are done
+                exp_block(poly_every, range(half_n * h, half_n * (h + 1)))
+                if h == 1:
+                    sstamp(4)
+                    turn_pass()
+                pack_store(range(half_n * h // 2, half_n * (h + 1) // 2), half_n * h // 2)
         sstamp(5)
         a(f"bra {l_pdone};")
         a.label(l_pbf)
@@ -965,7 +1027,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                "box": [64, BKV, 1, 1], "swizzle": "128B"} for x, nm in (("K", kn), ("V", vn))]
     uparams = [qn, kn, vn, on]
     if half:
-        v16n, vfn = f"{prefix}{name}__v16", f"{prefix}{name}__vflag"
+        v16n, vfn = scratch_names or (f"{prefix}{name}__v16", f"{prefix}{name}__vflag")
         uparams += [v16n, vfn]
         tmaps.append({"name": "tmV16", "tensor": v16n, "dtype": "f16", "dims": dims, "strides": strides,
                       "box": [64, BKV, 1, 1], "swizzle": "128B"})

@@ -19,19 +19,37 @@ BLOCK_BYTES = BLOCK_ROWS * D * 2          # 16 KiB of bf16 in, the same of f16 o
 F16_MAX_BF16_BITS = 0x477F
 
 
-def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16", "__vflag")) -> dict:
+def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16", "__vflag"),
+                bh_range: tuple[int, int] | None = None, ctas: int | None = None) -> dict:
+    """The pre-pass entry; ``bh_range`` = (first, count) converts only those flattened (batch, head)
+    pairs (their blocks and flags sit at the same places as in a whole-tensor launch).  ``ctas``
+    caps the grid: each CTA then strides over the blocks, which keeps the launch to one CTA per SM
+    when it shares the GPU with a concurrent kernel."""
     if seq % BLOCK_ROWS:
         raise ValueError("the value pre-pass needs S % 64 == 0")
-    blocks = batch * heads * (seq // BLOCK_ROWS)
+    bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
+    if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):
+        raise ValueError(f"bh_range {bh_range} outside the {batch * heads} (batch, head) pairs")
+    blocks = nbh * (seq // BLOCK_ROWS)
+    first = bh0 * (seq // BLOCK_ROWS)
     vec = BLOCK_BYTES // 16 // THREADS      # 16-byte vectors per thread
+    grid = blocks if not ctas else min(blocks, int(ctas))
     a = Asm()
     tid, blk = a.r(), a.r()
     a(f"mov.u32 {tid}, %tid.x;")
     a(f"mov.u32 {blk}, %ctaid.x;")
+    if first:
+        a(f"add.u32 {blk}, {blk}, {first};")
     pv, p16, pf = a.r("rd"), a.r("rd"), a.r("rd")
     for reg, pname in ((pv, "p_V"), (p16, "p_V16"), (pf, "p_flag")):
         a(f"ld.param.u64 {reg}, [{pname}];")
         a(f"cvta.to.global.u64 {reg}, {reg};")
+    l_top, l_done = a.L("blk"), a.L("alldone")
+    if grid < blocks:
+        a.label(l_top)
+        pend = a.r("p")
+        a(f"setp.ge.u32 {pend}, {blk}, {first + blocks};")
+        a(f"@{pend} bra {l_done};")
     off = a.r("rd")
     a(f"mul.wide.u32 {off}, {blk}, {BLOCK_BYTES};")
     t16 = a.r("rd")
@@ -73,13 +91,17 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
     a(f"mul.wide.u32 {fa}, {blk}, 4;")
     a(f"add.s64 {fa}, {fa}, {pf};")
     a(f"@{p0} st.global.u32 [{fa}], {fv};")
+    if grid < blocks:
+        a(f"add.u32 {blk}, {blk}, {grid};")
+        a(f"bra {l_top};")
+        a.label(l_done)
     entry = [f".visible .entry {name}(", "\t.param .u64 p_V,", "\t.param .u64 p_V16,", "\t.param .u64 p_flag", ")",
              f".reqntid {THREADS}, 1, 1", "{"] + a.decls() + a.lines + ["\tret;", "}"]
     vn, v16n, fn = names
     return {
         "name": name, "kind": "value_prepass", "params": [vn, v16n, fn], "raw_entry": entry,
-        "grid": [blocks, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": 0,
+        "grid": [grid, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": 0,
         "align": {vn: 16, v16n: 16, fn: 4}, "zero_outputs": [],
         "scratch": [{"name": v16n, "dtype": "f16", "shape": [batch, heads, seq, D]},
-                    {"name": fn, "dtype": "i32", "shape": [blocks]}],
+                    {"name": fn, "dtype": "i32", "shape": [batch * heads * (seq // BLOCK_ROWS)]}],
     }

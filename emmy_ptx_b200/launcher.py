@@ -28,6 +28,7 @@ SIGNATURES = {
     "emmy_module_unload": [vp],
     "emmy_get_function": [vp, ctypes.c_char_p, ctypes.POINTER(vp)],
     "emmy_set_max_dyn_smem": [vp, ctypes.c_int],
+    "emmy_set_smem_carveout": [vp, ctypes.c_int],
     "emmy_func_attribute": [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
     "emmy_launch": [vp, c_u32p, c_u32p, c_u32p, ctypes.c_uint32, vp, ctypes.POINTER(vp), ctypes.c_uint32],
     "emmy_launch_u64": [vp, c_u32p, c_u32p, ctypes.c_uint32, vp, c_u64p, c_u32p, ctypes.c_uint32],
@@ -43,6 +44,10 @@ SIGNATURES = {
     "emmy_event_synchronize": [vp],
     "emmy_event_elapsed_ms": [vp, vp, ctypes.POINTER(ctypes.c_float)],
     "emmy_stream_synchronize": [vp],
+    "emmy_event_create_flags": [ctypes.POINTER(vp), ctypes.c_uint],
+    "emmy_stream_create": [ctypes.POINTER(vp)],
+    "emmy_stream_destroy": [vp],
+    "emmy_stream_wait_event": [vp, vp],
     "emmy_ctx_synchronize": [],
     "emmy_mem_alloc": [c_u64p, ctypes.c_size_t],
     "emmy_mem_free": [ctypes.c_uint64],
@@ -169,6 +174,9 @@ class Device:
     def set_max_dyn_smem(self, fn, nbytes: int) -> None:
         check(self.lib.emmy_set_max_dyn_smem(fn, int(nbytes)), "emmy_set_max_dyn_smem")
 
+    def set_carveout(self, fn, percent: int) -> None:
+        check(self.lib.emmy_set_smem_carveout(fn, int(percent)), "emmy_set_smem_carveout")
+
     def launch_u64(self, fn, grid, block, dyn_smem: int, stream: int, params, align=None, pdl: bool = False) -> None:
         """Launch a kernel whose parameters are all 64-bit values.  ``pdl`` launches it as a
         programmatic dependent of the stream's previous work (the kernel must begin with
@@ -221,6 +229,24 @@ class Device:
         ev = vp()
         check(self.lib.emmy_event_create(ctypes.byref(ev)), "emmy_event_create")
         return ev
+
+    def sync_event(self):
+        """An event for ordering only (no timing)."""
+        ev = vp()
+        check(self.lib.emmy_event_create_flags(ctypes.byref(ev), 2), "emmy_event_create_flags")
+        return ev
+
+    def stream(self) -> int:
+        """A new non-blocking stream (its handle)."""
+        s = vp()
+        check(self.lib.emmy_stream_create(ctypes.byref(s)), "emmy_stream_create")
+        return s.value
+
+    def destroy_stream(self, stream: int) -> None:
+        check(self.lib.emmy_stream_destroy(vp(stream)), "emmy_stream_destroy")
+
+    def wait_event(self, stream: int, ev) -> None:
+        check(self.lib.emmy_stream_wait_event(vp(stream or 0), ev), "emmy_stream_wait_event")
 
     def record(self, ev, stream: int) -> None:
         check(self.lib.emmy_event_record(ev, vp(stream or 0)), "emmy_event_record")

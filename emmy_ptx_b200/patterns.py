@@ -334,15 +334,41 @@ def try_lower(graph, node, kmeta, prefix, options):
             return None
         precise = bool(options.get("attn_precise", True))
         half = bool(options.get("attn_half", True)) and precise
-        attn = tc_attention.attention_entry(node.op.name, bt, hd, seq, causal, scale,
-                                            names=(Q.name, K.name, V.name, O.name), prefix=prefix,
-                                            precise=precise, trace=bool(options.get("attn_trace", False)),
-                                            half=half,
-                                            poly_every=int(options.get("attn_poly", tc_attention.POLY_EVERY)),
-                                            pingpong=bool(options.get("attn_pingpong", True)))
+        name = node.op.name
+        kw = dict(names=(Q.name, K.name, V.name, O.name), prefix=prefix, precise=precise,
+                  trace=bool(options.get("attn_trace", False)), half=half,
+                  poly_every=int(options.get("attn_poly", tc_attention.POLY_EVERY)),
+                  pingpong=bool(options.get("attn_pingpong", True)),
+                  f16_int=int(options.get("attn_f16_int", 0)),
+                  pack_after_turn=bool(options.get("attn_pack_after_turn", False)),
+                  defer_sum=bool(options.get("attn_defer_sum", False)))
         if not half:
-            return attn
+            return tc_attention.attention_entry(name, bt, hd, seq, causal, scale, **kw)
         from .kernels import vconv
-        pre = vconv.vconv_entry(f"{node.op.name}_vconv", bt, hd, seq, names=(V.name,) + tuple(attn["params"][4:6]))
-        return [pre, attn]
+        scratch = (f"{prefix}{name}__v16", f"{prefix}{name}__vflag")
+        pairs = bt * hd
+        # opt-in: measured no faster on B200 (the co-running pre-pass takes the SM resources the
+        # attention is bound by), kept for the runtime's two-stream schedule it exercises
+        head = pairs // int(options.get("attn_overlap_split", 8)) if options.get("attn_overlap", False) else 0
+        if head < 1 or head >= pairs:
+            attn = tc_attention.attention_entry(name, bt, hd, seq, causal, scale, scratch_names=scratch, **kw)
+            pre = vconv.vconv_entry(f"{name}_vconv", bt, hd, seq, names=(V.name,) + scratch)
+            return [pre, attn]
+        # The value pre-pass of all but the first `head` (batch, head) pairs runs on a side stream while
+        # the attention of those first pairs runs: the pre-pass is bound by HBM bandwidth, which the
+        # attention barely uses, and its CTAs fit beside the attention's (one per SM).  Only the first
+        # group's pre-pass stays in the open.
+        pre0 = vconv.vconv_entry(f"{name}_vconv", bt, hd, seq, names=(V.name,) + scratch, bh_range=(0, head))
+        att0 = tc_attention.attention_entry(f"{name}_part0", bt, hd, seq, causal, scale, scratch_names=scratch,
+                                            bh_range=(0, head), **kw)
+        pre1 = vconv.vconv_entry(f"{name}_vconv1", bt, hd, seq, names=(V.name,) + scratch,
+                                 bh_range=(head, pairs - head), ctas=int(options.get("attn_overlap_ctas", 148)))
+        pre1["stream"] = 1
+        pre1["after"] = [f"{name}_vconv"]
+        pre1["carveout"] = 100          # the attention's shared-memory split, so the two can share an SM
+        att1 = tc_attention.attention_entry(name, bt, hd, seq, causal, scale, scratch_names=scratch,
+                                            bh_range=(head, pairs - head), **kw)
+        att1["after"] = [f"{name}_vconv1"]
+        att0["carveout"] = att1["carveout"] = 100
+        return [pre0, att0, pre1, att1]
     return None

@@ -5,6 +5,11 @@ tools/bench.py:86-115): it loads a module once, then each call zeroes the output
 record lists (``zero_outputs``, tools/stress.py:106-111), checks every pointer's alignment against
 what the emitted code assumes, encodes TMA descriptors for tensor-core kernels, and launches
 the entries in order on the caller's stream.  Buffers are caller-owned tensors on the device.
+
+An entry whose record says ``"stream": 1`` runs on the Executable's side stream instead, so that it
+overlaps the main stream's next entries; ``"after": [entry, ...]`` names entries it must follow
+(on the other stream: a fork or join through an event).  The side stream always rejoins the caller's
+stream before the call returns, so callers (and CUDA-graph capture) see one stream.
 """
 from __future__ import annotations
 
@@ -42,6 +47,8 @@ class Executable:
             fn = self.dev.function(self.module, rec["entry"])
             if rec.get("dyn_smem", 0) > 48 * 1024:
                 self.dev.set_max_dyn_smem(fn, rec["dyn_smem"])
+            if rec.get("carveout") is not None:
+                self.dev.set_carveout(fn, rec["carveout"])
             self.funcs.append(fn)
         self._tmap_cache: dict = {}
         # device scratch some lowerings need between their entries (e.g. the attention's f16 copy of V),
@@ -52,6 +59,16 @@ class Executable:
                 if spec["name"] not in self.scratch:
                     self.scratch[spec["name"]] = torch.empty(tuple(spec["shape"]), dtype=torch_dtype(spec["dtype"]),
                                                              device=f"cuda:{self.index}")
+        self.side = None
+        names = [rec["entry"] for rec in compiled.kernels]
+        for i, rec in enumerate(compiled.kernels):
+            for dep in rec.get("after", []):
+                if dep not in names[:i]:
+                    raise ValueError(f"entry {rec['entry']!r} follows {dep!r}, which is not an earlier entry")
+        if any(rec.get("stream") for rec in compiled.kernels):
+            self.side = self.dev.stream()
+            self._fork = self.dev.sync_event()
+            self._events = {rec["entry"]: self.dev.sync_event() for rec in compiled.kernels}
         self.err = None
         if any(spec.get("kind") == "errword" for rec in compiled.kernels for spec in rec.get("extra", [])):
             self.err = torch.zeros(4, dtype=torch.int32, device=f"cuda:{self.index}")
@@ -143,11 +160,37 @@ class Executable:
 
     def __call__(self, tensors: dict, stream: int | None = None) -> None:
         """Run every entry of the module once, in order, on ``stream`` (default: torch's current)."""
+        self.run(tensors, stream)
+
+    def run(self, tensors: dict, stream: int | None = None, zero: bool = True) -> None:
+        """Launch every entry once in module order: on ``stream`` or, for ``"stream": 1`` records, on
+        the side stream, forked from ``stream`` at the first such entry and joined back at the end.
+        ``zero=False`` skips the output zeroing (for replaying kernels only)."""
         import torch
         if stream is None:
             stream = torch.cuda.current_stream(self.index).cuda_stream
-        for i in range(len(self.records)):
-            self.launch(i, tensors, stream)
+        if self.side is None:
+            for i in range(len(self.records)):
+                self.launch(i, tensors, stream, zero=zero)
+            return
+        on = {}
+        last_side = None
+        for i, rec in enumerate(self.records):
+            s = self.side if rec.get("stream") else stream
+            if s == self.side and last_side is None:
+                # the side stream starts after everything queued on the caller's stream so far
+                self.dev.record(self._fork, stream)
+                self.dev.wait_event(self.side, self._fork)
+            for dep in rec.get("after", []):
+                if on[dep] != s:
+                    self.dev.wait_event(s, self._events[dep])
+            self.launch(i, tensors, s, zero=zero)
+            on[rec["entry"]] = s
+            self.dev.record(self._events[rec["entry"]], s)
+            if s == self.side:
+                last_side = rec["entry"]
+        if last_side is not None:
+            self.dev.wait_event(stream, self._events[last_side])
 
     @property
     def launches(self) -> int:
@@ -157,3 +200,8 @@ class Executable:
         if self.module is not None:
             self.dev.unload(self.module)
             self.module = None
+        if self.side is not None:
+            for ev in [self._fork, *self._events.values()]:
+                self.dev.destroy_event(ev)
+            self.dev.destroy_stream(self.side)
+            self.side = None

@@ -64,6 +64,11 @@ int emmy_get_function(void* module, const char* entry, void** function);
 /* CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, needed above 48 KiB (tools/localrun.py:96-98). */
 int emmy_set_max_dyn_smem(void* function, int bytes);
 
+/* The preferred shared-memory share of the L1/shared split, in percent (-1 = no preference).
+ * Kernels meant to share SMs (a pre-pass beside a large-shared-memory kernel) ask for the same
+ * split.  No reference counterpart. */
+int emmy_set_smem_carveout(void* function, int percent);
+
 /* cuFuncGetAttribute (registers, local memory, max threads, ...). */
 int emmy_func_attribute(void* function, int attr, int* value);
 
@@ -114,6 +119,15 @@ int emmy_event_synchronize(void* event);
 int emmy_event_elapsed_ms(void* start, void* stop, float* ms);
 int emmy_stream_synchronize(void* stream);
 int emmy_ctx_synchronize(void);
+
+/* An event with CUevent_flags (1 blocking sync, 2 no timing); a non-blocking stream of the
+ * context; a stream waiting on an event.  A module whose entries run on two streams (an
+ * overlapped pre-pass) forks and joins through these.  No reference counterpart: the reference
+ * launches one kernel on one stream (tools/localrun.py:98-105). */
+int emmy_event_create_flags(void** event, unsigned int flags);
+int emmy_stream_create(void** stream);
+int emmy_stream_destroy(void* stream);
+int emmy_stream_wait_event(void* stream, void* event);
 
 /* Memory (caller-owned device pointers). */
 int emmy_mem_alloc(uint64_t* dptr, size_t bytes);

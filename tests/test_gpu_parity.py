@@ -181,3 +181,29 @@ def test_attention_value_range_fallback(mode):
     got, ex = _run_ours(p, t_cpu)
     assert ex.error_code() == 0
     compare(got["O"], want["O"], "bf16", rtol_for(p), f"range {mode}", rms_floor=True)
+
+
+def test_attention_two_stream_schedule():
+    """The opt-in overlapped lowering: the second (batch, head) group's value pre-pass runs on the
+    runtime's side stream, and that group's attention waits for it through an event.  The f16 copy of
+    V and the block flags are poisoned before the call, so an attention that ran before its pre-pass
+    would read NaNs or the wrong format; the result must match the oracle."""
+    p = irgen.SMALL["c5tc"]()
+    t_cpu = data.make_inputs(p)
+    want = oracle_outputs(p, t_cpu)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"attn_overlap": True, "attn_overlap_split": 2})
+    assert [r.get("stream", 0) for r in mod.kernels] == [0, 0, 1, 0]
+    ex = Executable(mod)
+    t = {k: v.cuda() for k, v in t_cpu.items()}
+    for _ in range(2):
+        for v in ex.scratch.values():
+            if v.is_floating_point():
+                v.fill_(float("nan"))
+            else:
+                v.fill_(1)
+        t["O"].zero_()
+        ex(t)
+        torch.cuda.synchronize()
+        assert ex.error_code() == 0
+        compare(t["O"].cpu(), want["O"], "bf16", rtol_for(p), "two-stream attention", rms_floor=True)
+    ex.close()

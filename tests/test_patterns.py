@@ -81,10 +81,20 @@ def test_attention_ir_is_recognised():
         assert (bt, hd, seq, dim, c) == (p.params["batch"], p.params["heads"], p.params["seq"], p.params["dim"], causal)
         assert abs(scale - p.params["scale"]) < 1e-7
     full = irgen.FULL["c5"]()
-    recs = compile_graph(Graph.from_dict(full.graph), full.meta()).kernels
-    assert [r["kind"] for r in recs] == ["value_prepass", "tcgen05_attention"]
-    rec = recs[1]
-    assert rec["kind"] == "tcgen05_attention" and rec["block"] == [384, 1, 1] and rec["grid"] == [4096, 1, 1]
+    one = compile_graph(Graph.from_dict(full.graph), full.meta()).kernels
+    assert [r["kind"] for r in one] == ["value_prepass", "tcgen05_attention"] and one[1]["grid"] == [4096, 1, 1]
+    assert one[1]["block"] == [384, 1, 1]
+    recs = compile_graph(Graph.from_dict(full.graph), full.meta(), {"attn_overlap": True}).kernels
+    # opt-in: the pre-pass of 7/8 of the (batch, head) pairs runs on the side stream beside the
+    # attention of the first 1/8; the grids add up to the whole problem
+    assert [r["kind"] for r in recs] == ["value_prepass", "tcgen05_attention"] * 2
+    assert [r.get("stream", 0) for r in recs] == [0, 0, 1, 0]
+    assert recs[2]["after"] == [recs[0]["entry"]] and recs[3]["after"] == [recs[2]["entry"]]
+    assert recs[3]["entry"] == "attention_causal"
+    for rec in recs[1::2]:
+        assert rec["block"] == [384, 1, 1]
+    assert recs[1]["grid"][0] + recs[3]["grid"][0] == 4096 and recs[1]["grid"][0] == 512
+    assert recs[0]["grid"][0] == 32 * 64 and recs[2]["grid"][0] == 148      # the side pre-pass strides
 
 
 def test_attention_with_a_different_mask_is_refused():
