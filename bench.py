@@ -264,6 +264,13 @@ def parse():
     return ap.parse_args()
 
 
+def capture_steps(collective: bool, no_graph: bool) -> bool:
+    """Whether the timed steps are replayed from a CUDA graph: yes, unless graphs are off or a step
+    holds the ncclAllReduce.  NCCL calls stay out of graphs: a live graph that holds one keeps the
+    communicator's teardown waiting."""
+    return not no_graph and not collective
+
+
 def reference_arm(args, world, rank):
     """The reference's CPU implementation of the path (the oracle port) on every host core."""
     if rank != 0:
@@ -372,23 +379,26 @@ def main() -> int:
 
     launches0 = dev.launches
     reps = args.steps if units * 1.0 > 1e11 or kind == "FLOP" else max(args.steps, 200)
-    graphs = []
+    # launch-bound steps are replayed from CUDA graphs: exactly K steps in one graph, and a
+    # kernel-only graph of `reps` back-to-back launches for the per-launch duration.  A step with the
+    # ncclAllReduce stays a host launch: no NCCL call is captured in a graph (a graph that holds one
+    # keeps the communicator's teardown waiting).
+    step_graph = None
+    kern_graph = None
     if not args.no_graph:
-        # launch-bound steps are replayed from CUDA graphs: exactly K steps in one graph, and a
-        # kernel-only graph of `reps` back-to-back launches for the per-launch duration
-        g_steps = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_steps):
-            cs = torch.cuda.current_stream().cuda_stream
-            for i in range(args.steps):
-                step(sets[i % rotate], cs)
-        g_kern = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_kern):
+        if capture_steps(collective, args.no_graph):
+            step_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(step_graph):
+                cs = torch.cuda.current_stream().cuda_stream
+                for i in range(args.steps):
+                    step(sets[i % rotate], cs)
+            step_graph.replay()
+        kern_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(kern_graph):
             cs = torch.cuda.current_stream().cuda_stream
             for i in range(reps):
                 ex.run(sets[i % rotate], cs, zero=False)   # every entry of the module (a pre-pass included)
-        graphs = [g_steps, g_kern]
-        g_steps.replay()
-        g_kern.replay()
+        kern_graph.replay()
         torch.cuda.synchronize()
     gpu_launches = args.steps * len(mod.kernels)
     e0 = torch.cuda.Event(enable_timing=True)
@@ -401,8 +411,8 @@ def main() -> int:
     if dist:
         dist.barrier()
     e0.record()
-    if graphs:
-        graphs[0].replay()
+    if step_graph is not None:
+        step_graph.replay()
     else:
         for i in range(args.steps):
             step(sets[i % rotate])
@@ -415,8 +425,8 @@ def main() -> int:
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
     k0.record()
-    if graphs:
-        graphs[1].replay()
+    if kern_graph is not None:
+        kern_graph.replay()
     else:
         for i in range(reps):
             ex.run(sets[i % rotate], stream, zero=False)
@@ -543,12 +553,8 @@ def main() -> int:
                "sample": f"{pool.sample_blocks} of {p.grid} thread blocks ({100 * frac:.1f}% of one step) "
                          f"through the numpy oracle, one process", "seconds": dt}
 
-    for g in graphs:
-        del g
-    graphs = []
+    step_graph = kern_graph = None          # release the graphs before any teardown
     torch.cuda.synchronize()
-    if collective:
-        allreduce.close()
     if rank == 0:
         line = {
             "metric": f"{desc} {metric}", "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
@@ -558,12 +564,15 @@ def main() -> int:
                        "parallelism": f"dp{world} ({'sharded + ncclAllReduce of the partial' if collective else 'sharded, no collective'})",
                        "l2": ("inputs exceed L2 (126 MB)" if rotate == 1 else f"{rotate} rotating buffer sets exceed 2x L2"),
                        "grid": p.grid, "block": p.block},
-            "gpu_launches": gpu_launches, "timing": ("CUDA graph replay of the K steps" if not args.no_graph
-                                                     else "host launches"),
+            "gpu_launches": gpu_launches,
+            "timing": ("CUDA graph replay of the K steps" if capture_steps(collective, args.no_graph)
+                       else "host launches (kernel + ncclAllReduce per step)" if collective else "host launches"),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clock,
             "check": check, "kernel_kind": mod.kernels[-1].get("kind"),
         }
         print(json.dumps(line), flush=True)
+    if collective:
+        allreduce.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

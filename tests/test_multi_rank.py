@@ -97,3 +97,17 @@ def test_shards_cover_every_unit_once(n, world):
         for i in edist.shard(n, world, r):
             seen[i] += 1
     assert (seen == 1).all()
+
+
+def test_nccl_steps_are_never_captured_in_a_graph():
+    """The sum's multi-GPU step holds an ncclAllReduce; bench.py times it with host launches, since a
+    live CUDA graph that holds an NCCL call keeps the communicator's teardown waiting.  Steps without
+    a collective are graph-replayed unless graphs are switched off."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench.capture_steps(collective=True, no_graph=False) is False
+    assert bench.capture_steps(collective=False, no_graph=False) is True
+    assert bench.capture_steps(collective=False, no_graph=True) is False
