@@ -10,10 +10,11 @@
   plus 1e-6 absolute — bf16 keeps 8 significant bits, so two correct f32 computations that differ
   in the last f32 bits can round to neighbouring bf16 values;
 * bf16 attention from the tensor-core kernel: one bf16 unit of max(|ref|, rms of the query row).
-  The kernel rounds the softmax weights P to bf16 for the PV product (the tensor core multiplies
-  bf16 by bf16), which moves each term by up to 2**-9 relative before the f32 accumulation; an
-  output element that happens to cancel to near zero is held to its row's magnitude (rows that
-  attend to few keys have large outputs and the least averaging of that rounding).
+  The kernel rounds the softmax weights P for the PV product (the tensor core multiplies operands of
+  one type: f16 P with an f16 copy of V, 2**-12 relative, or P as two bf16 parts with bf16 V, 2**-14),
+  which moves each term slightly before the f32 accumulation; an output element that happens to
+  cancel to near zero is held to its row's magnitude (rows that attend to few keys have large outputs
+  and the least averaging of that rounding).
 """
 from __future__ import annotations
 
