@@ -1,0 +1,96 @@
+"""The tensor-core kernels' synchronisation, simulated on the CPU for every CTA of small launches.
+
+:mod:`tests.ctasim` runs one thread per warp of the emitted PTX with shared mbarriers (counts,
+transaction bytes, parity), named barriers and randomly delayed TMA / ``tcgen05.commit`` completions.
+A kernel passes when every CTA runs to its end under several interleavings with no time-out code
+written and no deadlock.  The planted-mistake tests show the simulation notices a missing hand-over.
+"""
+import math
+import re
+
+import pytest
+
+from emmy_ptx_b200 import irgen
+from emmy_ptx_b200.codegen.module import module_text, parse_records
+from emmy_ptx_b200.compiler import compile_graph
+from emmy_ptx_b200.ir import Graph
+from emmy_ptx_b200.kernels import tc_attention as ta
+
+from tests.ctasim import CtaSim, Deadlock
+
+
+def _attention(**kw):
+    causal = kw.pop("causal", True)
+    seq = kw.pop("seq", 1024)
+    b = ta.attention_entry("attn", 1, 1, seq, causal, 1 / math.sqrt(128), **kw)
+    txt = module_text([b])
+    return txt, parse_records(txt)[0]
+
+
+def _run_all(txt, rec, seeds=(0, 1), **kw):
+    sim = CtaSim(txt, rec)
+    for cta in range(rec["grid"][0]):
+        for seed in seeds:
+            r = sim.run(ctaid=cta, seed=1000 * cta + seed, **kw)
+            assert r["errors"] == [], (cta, seed, r["errors"])
+
+
+@pytest.mark.parametrize("variant", [
+    {}, {"pingpong": False}, {"half": False}, {"causal": False}, {"precise": False},
+    {"pack_after_turn": True, "defer_sum": True},
+])
+def test_attention_pipeline_completes(variant):
+    txt, rec = _attention(**variant)
+    _run_all(txt, rec)
+
+
+def test_attention_flagged_blocks_take_the_bf16_path():
+    # every value block flagged as not fitting f16: the producer loads V itself and the MMA issuers
+    # and softmax take the two-part P path; the hand-overs are the same
+    txt, rec = _attention()
+    _run_all(txt, rec, seeds=(0,), global_load=lambda ins, regs: 1)
+
+
+def test_attention_long_delays():
+    # completions far slower than the threads: every wait really sleeps
+    txt, rec = _attention(seq=512)
+    _run_all(txt, rec, seeds=(3,), delay=(200, 2000))
+
+
+def test_gemm_pipeline_completes():
+    p = irgen.SMALL["c4tc"]()
+    for sms in (1, 3, 4):
+        mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": sms})
+        rec = mod.kernels[0]
+        assert rec["kind"] == "tcgen05_gemm"
+        _run_all(mod.ptx, rec, seeds=(0, 1))
+
+
+def _expect_deadlock(txt, rec):
+    sim = CtaSim(txt, rec)
+    with pytest.raises(Deadlock):
+        for cta in range(rec["grid"][0]):
+            sim.run(ctaid=cta, seed=cta)
+
+
+def test_planted_missing_turn_hand_over_deadlocks():
+    txt, rec = _attention()
+    lines = txt.splitlines()
+    k = next(i for i, ln in enumerate(lines) if "bar.arrive 2, 256" in ln)
+    _expect_deadlock("\n".join(lines[:k] + lines[k + 1:]), rec)
+
+
+def test_planted_wrong_arrival_count_deadlocks():
+    # the P-full barriers expect one arrival per softmax warp (4); asking for 5 stalls the issuers
+    txt, rec = _attention()
+    bad = re.sub(r"(mbarrier\.init\.shared::cta\.b64 \[[^\]]+\]), 4;", r"\1, 5;", txt)
+    assert bad != txt
+    _expect_deadlock(bad, rec)
+
+
+def test_planted_missing_commit_deadlocks():
+    p = irgen.SMALL["c4tc"]()
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": 2})
+    lines = mod.ptx.splitlines()
+    k = next(i for i, ln in enumerate(lines) if "tcgen05.commit" in ln)
+    _expect_deadlock("\n".join(lines[:k] + lines[k + 1:]), mod.kernels[0])
