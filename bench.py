@@ -264,11 +264,18 @@ def parse():
     return ap.parse_args()
 
 
-def capture_steps(collective: bool, no_graph: bool) -> bool:
-    """Whether the timed steps are replayed from a CUDA graph: yes, unless graphs are off or a step
-    holds the ncclAllReduce.  NCCL calls stay out of graphs: a live graph that holds one keeps the
-    communicator's teardown waiting."""
-    return not no_graph and not collective
+def use_graphs(world: int, no_graph: bool) -> bool:
+    """Whether this run captures CUDA graphs at all: single-GPU runs only.  Multi-GPU runs launch from
+    the host, the multi-GPU path measured on B200, so no capture runs beside the process group's NCCL
+    watchdog and no NCCL call is ever captured."""
+    return not no_graph and world == 1
+
+
+def capture_steps(collective: bool, no_graph: bool, world: int = 1) -> bool:
+    """Whether the timed steps are replayed from a CUDA graph: yes, unless graphs are off, the run has
+    several ranks, or a step holds the ncclAllReduce.  NCCL calls stay out of graphs: a live graph
+    that holds one keeps the communicator's teardown waiting."""
+    return use_graphs(world, no_graph) and not collective
 
 
 def reference_arm(args, world, rank):
@@ -379,14 +386,13 @@ def main() -> int:
 
     launches0 = dev.launches
     reps = args.steps if units * 1.0 > 1e11 or kind == "FLOP" else max(args.steps, 200)
-    # launch-bound steps are replayed from CUDA graphs: exactly K steps in one graph, and a
-    # kernel-only graph of `reps` back-to-back launches for the per-launch duration.  A step with the
-    # ncclAllReduce stays a host launch: no NCCL call is captured in a graph (a graph that holds one
-    # keeps the communicator's teardown waiting).
+    # single-GPU runs replay launch-bound steps from CUDA graphs: exactly K steps in one graph, and a
+    # kernel-only graph of `reps` back-to-back launches for the per-launch duration.  Multi-GPU runs,
+    # and any step holding the ncclAllReduce, launch from the host (see use_graphs / capture_steps).
     step_graph = None
     kern_graph = None
-    if not args.no_graph:
-        if capture_steps(collective, args.no_graph):
+    if use_graphs(world, args.no_graph):
+        if capture_steps(collective, args.no_graph, world):
             step_graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(step_graph):
                 cs = torch.cuda.current_stream().cuda_stream
@@ -498,7 +504,7 @@ def main() -> int:
     # (half read, half written), rotated and graph-replayed like the kernel, shows what this launch
     # size allows; the roofline fraction itself stays against the measured 1 GiB copy peak
     copy_ref = None
-    if kind == "B" and not args.no_graph:
+    if kind == "B" and use_graphs(world, args.no_graph):
         nb = int(units // 2) // 4
         pairs = [(torch.ones(nb, dtype=torch.float32, device="cuda"), torch.empty(nb, dtype=torch.float32, device="cuda"))
                  for _ in range(rotate)]
@@ -565,7 +571,7 @@ def main() -> int:
                        "l2": ("inputs exceed L2 (126 MB)" if rotate == 1 else f"{rotate} rotating buffer sets exceed 2x L2"),
                        "grid": p.grid, "block": p.block},
             "gpu_launches": gpu_launches,
-            "timing": ("CUDA graph replay of the K steps" if capture_steps(collective, args.no_graph)
+            "timing": ("CUDA graph replay of the K steps" if capture_steps(collective, args.no_graph, world)
                        else "host launches (kernel + ncclAllReduce per step)" if collective else "host launches"),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clock,
             "check": check, "kernel_kind": mod.kernels[-1].get("kind"),

@@ -111,3 +111,7 @@ def test_nccl_steps_are_never_captured_in_a_graph():
     assert bench.capture_steps(collective=True, no_graph=False) is False
     assert bench.capture_steps(collective=False, no_graph=False) is True
     assert bench.capture_steps(collective=False, no_graph=True) is False
+    # several ranks: no graph capture at all (host launches, the measured multi-GPU path)
+    assert bench.use_graphs(world=2, no_graph=False) is False
+    assert bench.capture_steps(collective=False, no_graph=False, world=8) is False
+    assert bench.use_graphs(world=1, no_graph=False) is True
