@@ -90,11 +90,13 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                     trace: bool = False, half: bool = True, poly_every: int = POLY_EVERY,
                     pingpong: bool = True, f16_int: int = 0, pack_after_turn: bool = False,
                     defer_sum: bool = False, bh_range: tuple[int, int] | None = None,
-                    scratch_names: tuple[str, str] | None = None) -> dict:
+                    scratch_names: tuple[str, str] | None = None, prefetch_next: int = 0) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
     ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps.
-    ``bh_range`` = (first, count) restricts the launch to those flattened (batch, head) pairs."""
+    ``bh_range`` = (first, count) restricts the launch to those flattened (batch, head) pairs.
+    ``prefetch_next`` = n > 0 makes the producer prefetch into L2, after its last load, the Q tiles and
+    first K / V block of CTA index + n (the one likely to start when this one ends)."""
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
@@ -336,6 +338,33 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"add.u32 {n_}, {n_}, 1;")
     a(f"bra {l_pl};")
     a.label(l_pdone)
+    if prefetch_next:
+        # the CTA that starts about when this one ends (index + prefetch_next, the SMs' worth of
+        # CTAs ahead in launch order) will first read its two Q tiles and K_0 / V_0: ask L2 for them
+        # now, while this CTA's last blocks run (a prefetch has no completion to wait for)
+        l_nopf = a.L("nopf")
+        cn, pnx = a.r(), a.r("p")
+        a(f"add.u32 {cn}, {cta}, {prefetch_next};")
+        a(f"setp.ge.u32 {pnx}, {cn}, {grid};")
+        a(f"@{pnx} bra {l_nopf};")
+        tn, bhn, bbn, hhn, rown = a.r(), a.r(), a.r(), a.r(), a.r()
+        a(f"div.u32 {tn}, {cn}, {nbh};")
+        a(f"sub.u32 {tn}, {nt - 1}, {tn};")
+        a(f"rem.u32 {bhn}, {cn}, {nbh};")
+        if bh0:
+            a(f"add.u32 {bhn}, {bhn}, {bh0};")
+        a(f"div.u32 {bbn}, {bhn}, {heads};")
+        a(f"rem.u32 {hhn}, {bhn}, {heads};")
+        a(f"shl.b32 {rown}, {tn}, 8;")
+        for i in range(TILES):
+            r_i = a.r()
+            a(f"add.u32 {r_i}, {rown}, {BQ * i};")
+            for hb in range(2):
+                a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tq}, {{{64 * hb}, {r_i}, {hhn}, {bbn}}}];")
+        for tmn in (tk, tv16 if half else tv):
+            for hb in range(2):
+                a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tmn}, {{{64 * hb}, 0, {hhn}, {bbn}}}];")
+        a.label(l_nopf)
     for s in range(STAGES):
         skip = a.L("dskip")
         pn = a.r("p")

@@ -341,7 +341,8 @@ def try_lower(graph, node, kmeta, prefix, options):
                   pingpong=bool(options.get("attn_pingpong", True)),
                   f16_int=int(options.get("attn_f16_int", 0)),
                   pack_after_turn=bool(options.get("attn_pack_after_turn", False)),
-                  defer_sum=bool(options.get("attn_defer_sum", False)))
+                  defer_sum=bool(options.get("attn_defer_sum", False)),
+                  prefetch_next=int(options.get("attn_prefetch_next", 0)))
         if not half:
             return tc_attention.attention_entry(name, bt, hd, seq, causal, scale, **kw)
         from .kernels import vconv
