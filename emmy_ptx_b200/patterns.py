@@ -343,6 +343,17 @@ def try_lower(graph, node, kmeta, prefix, options):
                   pack_after_turn=bool(options.get("attn_pack_after_turn", False)),
                   defer_sum=bool(options.get("attn_defer_sum", False)),
                   prefetch_next=int(options.get("attn_prefetch_next", 0)))
+        if options.get("attn_persistent", False):
+            # opt-in persistent schedule (one CTA per SM, alternating row halves; see the module)
+            from .kernels import tc_attention_persistent as tap, vconv
+            scratch = (f"{prefix}{name}__v16", f"{prefix}{name}__vflag")
+            att = tap.persistent_attention_entry(name, bt, hd, seq, causal, scale,
+                                                 names=(Q.name, K.name, V.name, O.name), prefix=prefix,
+                                                 half=half, ctas=int(options.get("sms", 148)),
+                                                 scratch_names=scratch if half else None)
+            if not half:
+                return att
+            return [vconv.vconv_entry(f"{name}_vconv", bt, hd, seq, names=(V.name,) + scratch), att]
         if not half:
             return tc_attention.attention_entry(name, bt, hd, seq, causal, scale, **kw)
         from .kernels import vconv

@@ -71,7 +71,13 @@ def alu(op: str, ops: list, regs: dict, val) -> bool:
         return True
     if op.startswith(("mov.u32", "mov.b32", "mov.u64", "mov.b64", "mov.s32")) and not ops[0].startswith("{"):
         src = ops[1].strip()
-        if src.startswith("{") or src.startswith(("0f", "0d")):
+        if src.startswith("{"):
+            parts = [val(x) for x in src.strip("{}").split(",")]
+            if op.startswith("mov.b64") and len(parts) == 2 and all(isinstance(x, int) for x in parts):
+                regs[ops[0]] = (parts[0] & _M32) | ((parts[1] & _M32) << 32)
+            else:
+                regs[ops[0]] = None
+        elif src.startswith(("0f", "0d")):
             regs[ops[0]] = None
         elif re.match(r"^[A-Za-z_$]", src):
             regs[ops[0]] = val(src)
@@ -170,9 +176,11 @@ class CtaSim:
         # every parameter symbol gets a distinct fake address, so a tensor-map operand names its map
         self.symbols: dict[str, int] = {}
         self.tmap_bytes: dict[int, int] = {}
+        self.tmap_name: dict[int, str] = {}
         for k, spec in enumerate(rec.get("tmaps", [])):
             addr = 0x7000_0000 + 0x1000 * k
             self.symbols[f"p_{spec['name']}"] = addr
+            self.tmap_name[addr] = spec["name"]
             nbytes = _DTYPE_BYTES[spec["dtype"]]
             for b in spec["box"]:
                 nbytes *= int(b)
@@ -192,9 +200,11 @@ class CtaSim:
         return b + off
 
     def run(self, ctaid: int = 0, seed: int = 0, delay=(1, 60), max_steps: int = 20_000_000,
-            global_load=None) -> dict:
-        """Simulate one CTA.  Returns ``{"errors": [...], "steps": n}``; raises :class:`Deadlock` with
-        each waiting thread's position when nothing can run."""
+            global_load=None, log_tma: bool = False) -> dict:
+        """Simulate one CTA.  Returns ``{"errors": [...], "steps": n, "stores": [(warp, address)],
+        "tma": [(warp, map name, coordinates)] or None}``: error codes written, global stores (from
+        address 0 for every pointer parameter) and, with ``log_tma``, every TMA load issued.  Raises
+        :class:`Deadlock` with each waiting thread's position when nothing can run."""
         rng = random.Random(seed)
         smem: dict[int, int] = {}
         mbars: dict[int, _MBar] = {}
@@ -207,6 +217,8 @@ class CtaSim:
                     "%laneid": 0, "%nctaid.x": int(self.rec["grid"][0])}
             threads.append({"w": w, "pc": 0, "regs": regs, "state": "run", "on": None})
         errors = []
+        stores = []
+        tma_log = [] if log_tma else None
         now = 0
         seq = 0
         steps = 0
@@ -269,8 +281,9 @@ class CtaSim:
                         wake_mbar(addr)
                     continue
                 if all(t["state"] == "done" for t in threads):
-                    return {"errors": errors, "steps": steps}
-                where = [(t["w"], t["state"], t["on"], self.ins[t["pc"]].op) for t in threads if t["state"] != "done"]
+                    return {"errors": errors, "steps": steps, "stores": stores, "tma": tma_log}
+                where = [(t["w"], t["state"], t["on"], t.get("par") if t["state"] == "mbar" else None,
+                          self.ins[t["pc"]].line) for t in threads if t["state"] != "done"]
                 raise Deadlock(f"CTA {ctaid}: no thread can run: {where}")
             # deliver completions that are due
             while inflight and inflight[0][0] <= now:
@@ -320,6 +333,7 @@ class CtaSim:
                 else:
                     th["pc"] -= 1                 # sleep on the barrier and retry the wait
                     th["state"], th["on"] = "mbar", addr
+                    th["par"] = (par, b.phase)
                 continue
             if op.startswith("mbarrier.arrive.expect_tx"):
                 addr = self._addr(regs, ops[1])
@@ -338,6 +352,10 @@ class CtaSim:
                 if tmap not in self.tmap_bytes:
                     raise AssertionError(f"TMA with an unknown tensor map at line {x.line}")
                 schedule("tx", self._addr(regs, ops[2]), self.tmap_bytes[tmap])
+                if tma_log is not None:
+                    coords = ops[1].strip()[1:-1].split(",", 1)[1]
+                    cs = tuple(val(c) for c in coords.strip().strip("{}").split(","))
+                    tma_log.append((th["w"], self.tmap_name.get(tmap), cs, self._addr(regs, ops[0])))
                 continue
             if op.startswith("tcgen05.commit"):
                 schedule("commit", self._addr(regs, ops[0]), 1, th["w"])
@@ -381,6 +399,13 @@ class CtaSim:
                 continue
             if op.startswith("st.global") and len(ops) == 2 and _IMM.match(ops[1].strip()):
                 errors.append(int(ops[1], 0))
+                continue
+            if op.startswith("st.global"):
+                stores.append((th["w"], self._addr(regs, ops[0])))
+                continue
+
+            if op.startswith("vote.sync.ballot"):
+                regs[ops[0]] = _M32 if regs.get(ops[1]) else 0     # every lane of the warp agrees
                 continue
             if op.startswith("vote.sync"):
                 regs[ops[0]] = bool(regs.get(ops[1]))

@@ -17,22 +17,14 @@ import re
 
 from emmy_ptx_b200.codegen.ptxcheck import _entries, _instructions
 
-_M32, _M64 = (1 << 32) - 1, (1 << 64) - 1
+from tests.ctasim import alu
+
+_M32 = (1 << 32) - 1
 _IMM = re.compile(r"^-?(?:0[xX][0-9a-fA-F]+|\d+)$")
 
 
 class StepLimit(RuntimeError):
     pass
-
-
-def _bits(op: str) -> int:
-    m = re.search(r"\.[usb](8|16|32|64)\b", op)
-    return int(m.group(1)) if m else 32
-
-
-def _signed(v: int, bits: int) -> int:
-    v &= (1 << bits) - 1
-    return v - (1 << bits) if v >> (bits - 1) else v
 
 
 class Walk:
@@ -64,6 +56,8 @@ class Walk:
                 return int(o, 0)
             if o.startswith("0f") or o.startswith("0d"):
                 return None
+            if re.match(r"^[A-Za-z_$]", o):
+                return 0                      # a symbol: shared-memory offsets are taken from 0
             return regs.get(o)
 
         while pc < len(self.ins):
@@ -101,31 +95,9 @@ class Walk:
             if op.startswith("vote.sync"):
                 regs[ops[0]] = bool(regs.get(ops[1]))
                 continue
-            if op.startswith("setp."):
-                parts = op.split(".")
-                cmp, ty = parts[1], parts[-1]
-                if ty.startswith("f"):
-                    r = False if fcmp is None else bool(fcmp(nf))
-                    nf += 1
-                else:
-                    a_, b_ = val(ops[1]), val(ops[2])
-                    if a_ is None or b_ is None:
-                        raise ValueError(f"unknown operand at line {x.line}: {op} {ops}")
-                    bits = int(ty[1:])
-                    if ty[0] == "s":
-                        a_, b_ = _signed(a_, bits), _signed(b_, bits)
-                    else:
-                        a_, b_ = a_ & ((1 << bits) - 1), b_ & ((1 << bits) - 1)
-                    r = {"eq": a_ == b_, "ne": a_ != b_, "lt": a_ < b_, "le": a_ <= b_,
-                         "gt": a_ > b_, "ge": a_ >= b_}[cmp]
-                regs[ops[0]] = r
-                continue
-            if op in ("and.pred", "or.pred", "xor.pred", "not.pred"):
-                if op == "not.pred":
-                    regs[ops[0]] = not regs.get(ops[1])
-                else:
-                    a_, b_ = bool(regs.get(ops[1])), bool(regs.get(ops[2]))
-                    regs[ops[0]] = {"and": a_ and b_, "or": a_ or b_, "xor": a_ != b_}[head]
+            if op.startswith("setp.") and op.split(".")[-1].startswith("f"):
+                regs[ops[0]] = False if fcmp is None else bool(fcmp(nf))
+                nf += 1
                 continue
             if op.startswith(("ld.", "ldu.")):
                 if op.startswith("ld.param") or load is None:
@@ -142,71 +114,14 @@ class Walk:
             if op.startswith("st.global") and len(ops) == 2 and _IMM.match(ops[1].strip()):
                 events.append(("store_err", int(ops[1], 0)))
                 continue
-            if op.startswith(("mov.u32", "mov.b32", "mov.u64", "mov.b64", "mov.s32")) and not ops[0].startswith("{"):
-                src = ops[1].strip()
-                if src.startswith("{"):
-                    regs[ops[0]] = None
-                elif src.startswith("%") and src not in regs and not src[1:].replace("_", "").isalnum():
-                    regs[ops[0]] = None
-                else:
-                    regs[ops[0]] = val(src) if not re.match(r"^[A-Za-z_]", src) else 0
+            if op.startswith("vote.sync.ballot"):
+                regs[ops[0]] = _M32 if regs.get(ops[1]) else 0
                 continue
-            if head in ("add", "sub", "mul", "mad", "shl", "shr", "and", "or", "xor", "div", "rem", "min",
-                        "max", "neg", "not", "cvt", "cvta", "selp") and not ops[0].startswith("{"):
-                ty = op.split(".")[-1]
-                if ty.startswith("f") or ".f32" in op or ".f64" in op or "x2" in op:
-                    regs[ops[0]] = None
+            try:
+                if alu(op, ops, regs, val):
                     continue
-                srcs = [val(o) for o in ops[1:]]
-                if head == "selp":
-                    p = regs.get(ops[3])
-                    regs[ops[0]] = srcs[0] if p else srcs[1]
-                    continue
-                if head in ("cvt", "cvta"):
-                    regs[ops[0]] = srcs[0]
-                    continue
-                if any(s is None for s in srcs):
-                    regs[ops[0]] = None
-                    continue
-                bits = 64 if (".wide" in op or _bits(op) == 64) else _bits(op)
-                m = (1 << bits) - 1
-                a_ = srcs[0]
-                b_ = srcs[1] if len(srcs) > 1 else 0
-                if head == "add":
-                    r = a_ + b_
-                elif head == "sub":
-                    r = a_ - b_
-                elif head == "mul":
-                    r = (a_ & _M32) * (b_ & _M32) if ".wide" in op else a_ * b_
-                elif head == "mad":
-                    r = ((a_ & _M32) * (b_ & _M32) if ".wide" in op else a_ * b_) + srcs[2]
-                elif head == "shl":
-                    r = a_ << (b_ & 63)
-                elif head == "shr":
-                    r = ((_signed(a_, bits) if ".s" in op else a_ & m) >> b_)
-                elif head == "and":
-                    r = a_ & b_
-                elif head == "or":
-                    r = a_ | b_
-                elif head == "xor":
-                    r = a_ ^ b_
-                elif head in ("div", "rem"):
-                    if ".s" in op:
-                        sa, sb = _signed(a_, bits), _signed(b_, bits)
-                        q = abs(sa) // abs(sb) * (1 if (sa >= 0) == (sb >= 0) else -1)
-                        r = q if head == "div" else sa - q * sb
-                    else:
-                        r = (a_ & m) // (b_ & m) if head == "div" else (a_ & m) % (b_ & m)
-                elif head == "min":
-                    r = min(a_, b_)
-                elif head == "max":
-                    r = max(a_, b_)
-                elif head == "neg":
-                    r = -a_
-                else:
-                    r = ~a_
-                regs[ops[0]] = r & m
-                continue
+            except ValueError as e:
+                raise ValueError(f"line {x.line}: {e}") from None
             # anything else: its register results are unknown
             if ops and not op.startswith(("st.", "tcgen05.st", "tcgen05.mma", "tcgen05.commit", "cp.",
                                           "fence", "mbarrier.init", "mbarrier.arrive", "red.", "bar.warp")):

@@ -94,3 +94,16 @@ def test_planted_missing_commit_deadlocks():
     lines = mod.ptx.splitlines()
     k = next(i for i, ln in enumerate(lines) if "tcgen05.commit" in ln)
     _expect_deadlock("\n".join(lines[:k] + lines[k + 1:]), mod.kernels[0])
+
+
+def test_attention_writes_every_row_once():
+    # one CTA per 256 query rows: every output row (the simulated lane 0 of each warp covers rows
+    # 0, 32, 64, 96 of each tile) is written by exactly one thread, in 8 pieces of 32 bytes
+    import collections
+    txt, rec = _attention(seq=1024)
+    sim = CtaSim(txt, rec)
+    rows = collections.Counter()
+    for cta in range(rec["grid"][0]):
+        for _, addr in sim.run(ctaid=cta, seed=cta)["stores"]:
+            rows[addr // 256] += 1
+    assert set(rows) == set(range(0, 1024, 32)) and set(rows.values()) == {8}
