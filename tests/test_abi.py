@@ -46,3 +46,18 @@ def test_launch_flags_are_checked_before_the_driver():
     rc = lib.emmy_launch_ex(fake_fn, grid, block, None, 0, None, None, 0, 0x80)
     assert rc != 0
     assert "unknown launch flags" in launcher.last_error()
+
+
+def test_stream_and_event_arguments_are_checked_before_the_driver():
+    lib = launcher.load_library()
+    vp = ctypes.c_void_p
+    ev = vp()
+    assert lib.emmy_event_create_flags(ctypes.byref(ev), 8) != 0          # unknown CUevent flag
+    assert "unknown event flags" in launcher.last_error()
+    assert lib.emmy_event_create_flags(None, 2) != 0
+    assert lib.emmy_stream_create(None) != 0
+    assert lib.emmy_stream_destroy(None) != 0
+    assert lib.emmy_stream_wait_event(None, None) != 0
+    assert lib.emmy_set_smem_carveout(None, 50) != 0
+    assert lib.emmy_set_smem_carveout(vp(0x1000), 101) != 0              # outside -1..100
+    assert "carveout" in launcher.last_error()
