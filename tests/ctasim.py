@@ -103,14 +103,17 @@ def alu(op: str, ops: list, regs: dict, val) -> bool:
         bits = 64 if (".wide" in op or _bits(op) == 64) else _bits(op)
         m = (1 << bits) - 1
         a_, b_ = srcs[0], (srcs[1] if len(srcs) > 1 else 0)
+        signed = bool(re.search(r"\.s(8|16|32|64)\b", op))
+        if ".wide" in op:
+            w = (lambda v: _signed(v, 32)) if signed else (lambda v: v & _M32)
         if head == "add":
             r = a_ + b_
         elif head == "sub":
             r = a_ - b_
         elif head == "mul":
-            r = (a_ & _M32) * (b_ & _M32) if ".wide" in op else a_ * b_
+            r = w(a_) * w(b_) if ".wide" in op else a_ * b_
         elif head == "mad":
-            r = ((a_ & _M32) * (b_ & _M32) if ".wide" in op else a_ * b_) + srcs[2]
+            r = (w(a_) * w(b_) if ".wide" in op else a_ * b_) + srcs[2]
         elif head == "shl":
             r = a_ << (b_ & 63)
         elif head == "shr":
@@ -128,10 +131,9 @@ def alu(op: str, ops: list, regs: dict, val) -> bool:
                 r = q if head == "div" else sa - q * sb
             else:
                 r = (a_ & m) // (b_ & m) if head == "div" else (a_ & m) % (b_ & m)
-        elif head == "min":
-            r = min(a_, b_)
-        elif head == "max":
-            r = max(a_, b_)
+        elif head in ("min", "max"):
+            x_, y_ = (_signed(a_, bits), _signed(b_, bits)) if signed else (a_ & m, b_ & m)
+            r = min(x_, y_) if head == "min" else max(x_, y_)
         elif head == "neg":
             r = -a_
         else:
