@@ -61,7 +61,8 @@ def _bf16_rn(x: np.float32) -> int:
 
 
 def _f16_rn(x: np.float32) -> int:
-    return int(np.array([x], dtype=np.float32).astype(np.float16).view(np.uint16)[0])
+    with np.errstate(over="ignore"):                  # beyond the f16 range: infinity, as cvt.rn does
+        return int(np.array([x], dtype=np.float32).astype(np.float16).view(np.uint16)[0])
 
 
 _PI, _PF = struct.Struct("<I"), struct.Struct("<f")
@@ -229,6 +230,7 @@ class Emulator:
                 sym[name] = smem_size
                 smem_size += size if size is not None else dyn_smem
             smem = bytearray(max(smem_size, 16))
+            self._cta_begin(cta, smem)
             threads = []
             for t in range(block):
                 regs = {"%tid.x": t, "%tid.y": 0, "%tid.z": 0, "%ntid.x": block, "%ntid.y": 1, "%ntid.z": 1,
@@ -259,6 +261,7 @@ class Emulator:
             resolved = False
             waiting_bar = [t for t in live if t.state == "bar"]
             if waiting_bar and len(waiting_bar) == len(live):
+                self._bar_release(waiting_bar)
                 for t in waiting_bar:
                     t.state, t.coll = "run", None
                 resolved = True
@@ -370,9 +373,9 @@ class Emulator:
             if op in ("ret", "exit"):
                 th.state = "done"
                 return n
-            if op.startswith("bar.sync") or op.startswith("barrier.sync"):
+            if (op.startswith("bar.sync") or op.startswith("barrier.sync")) and len(ops) == 1 and val(ops[0]) == 0:
                 th.pc += 1
-                th.state = "bar"
+                th.state = "bar"                      # the whole CTA
                 return n
             if op.startswith(("shfl.sync", "redux.sync", "vote.sync")):
                 th.state, th.coll = "coll", (op, val(ops[-1]) & _M32)
@@ -402,6 +405,11 @@ class Emulator:
             if op.startswith(("cp.async.commit", "cp.async.wait", "fence", "membar", "griddepcontrol",
                               "prefetch")):
                 continue
+            r = self._extra(th, x, op, ops, regs, val, addr, smem, mem)
+            if r is not None:
+                if r == "block":
+                    return n
+                continue
             try:
                 if self._float(op, ops, regs, val):
                     continue
@@ -413,6 +421,16 @@ class Emulator:
             except (TypeError, ValueError) as e:
                 raise RuntimeError(f"thread {th.tid} line {x.line}: {op} {ops}: {e}") from None
             raise NotImplementedError(f"line {x.line}: {op} {ops}")
+
+    # hooks for the tensor-core extension (tests/tcemu.py)
+    def _cta_begin(self, cta, smem):
+        pass
+
+    def _bar_release(self, threads):
+        pass
+
+    def _extra(self, th, x, op, ops, regs, val, addr, smem, mem):
+        return None
 
     @staticmethod
     def _decode(x):

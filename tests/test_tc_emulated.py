@@ -1,0 +1,100 @@
+"""CPU parity of the tensor-core kernels: the emitted tcgen05 / TMA PTX run by the tensor-core emulator
+(:mod:`tests.tcemu`) against the oracle, for the attention (default, variants, the value-range
+fallback and the persistent schedule) and the batched matmul.
+
+The GPU tests compare the same kernels on a B200; these also cover kernel forms that have not yet
+run on a GPU, so their data path (descriptors, swizzled tiles, TMEM columns, row mapping) is checked
+before any GPU time.
+"""
+import numpy as np
+import pytest
+import torch
+
+from emmy_ptx_b200 import data, irgen
+from emmy_ptx_b200.compiler import compile_graph
+from emmy_ptx_b200.ir import Graph
+from oracle.run import oracle_outputs
+from tests.checks import compare, rms_floor_for, rtol_for
+from tests.ptxemu import Memory
+from tests.tcemu import TcEmulator
+
+_BYTES = {"f16": 2, "bf16": 2, "f32": 4, "i32": 4}
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def run_emulated(p, t, opts):
+    """Compile ``p`` with ``opts`` and run every entry through the emulator on tensors ``t``; returns
+    the outputs and the error word."""
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), opts)
+    mem = Memory()
+    addr = {name: mem.alloc(_np(ten).copy()) for name, ten in t.items()}
+    for rec in mod.kernels:
+        for spec in rec.get("scratch", []):
+            if spec["name"] not in addr:
+                addr[spec["name"]] = mem.alloc(np.zeros(int(np.prod(spec["shape"])) * _BYTES[spec["dtype"]], np.uint8))
+    err = mem.alloc(np.zeros(16, np.uint8))
+    for rec in mod.kernels:
+        tm = {f"p_{spec['name']}": (addr[spec["tensor"]], spec) for spec in rec.get("tmaps", [])}
+        emu = TcEmulator(mod.ptx, rec["entry"], tm)
+        plain = [q for q in emu.params if not q.startswith("p_tm") and q not in ("p_err", "p_trace")]
+        args = dict(zip(plain, [addr[n] for n in rec["params"]]))
+        args.update(emu.tmap_args())
+        args["p_err"] = err
+        emu.run(rec["grid"][0], rec["block"][0], args, mem, rec.get("dyn_smem", 0))
+    out = {}
+    for a in p.outputs:
+        ten = t[a.name]
+        arr = mem.array(addr[a.name], _np(ten).dtype, tuple(ten.shape)).copy()
+        g = torch.from_numpy(arr)
+        out[a.name] = g.view(torch.bfloat16) if ten.dtype == torch.bfloat16 else g
+    return out, int(mem.array(err, np.int32, (4,))[0]), mod
+
+
+def _check(p, t, opts, kind):
+    got, code, mod = run_emulated(p, t, opts)
+    assert mod.kernels[-1]["kind"] == kind
+    assert code == 0
+    want = oracle_outputs(p, t)
+    for a in p.outputs:
+        compare(got[a.name], want[a.name], a.dtype, rtol_for(p), f"tc-emu {opts}", rms_floor=rms_floor_for(p))
+
+
+def _causal():
+    # causal, one (batch, head), 512 rows: two work units (the longest first), so a persistent CTA
+    # walks both, its warpgroups swapping the lower and upper rows between them
+    return irgen.attention_ir(1, 1, 512, 128, True)
+
+
+@pytest.mark.parametrize("key,opts", [
+    ("c5tcnc", {}),
+    ("c5tcnc", {"attn_half": False}),                  # P as two bf16 parts for every block
+    ("c5tcnc", {"attn_pingpong": False}),
+    ("causal", {}),
+    ("causal", {"attn_persistent": True, "sms": 1}),
+    ("c5tcnc", {"attn_persistent": True, "sms": 1}),
+    ("c5tcnc", {"attn_prefetch_next": 1}),
+], ids=["nc", "nc-bf16", "nc-noturns", "causal", "causal-persistent", "nc-persistent", "nc-prefetch"])
+def test_attention_emulated_matches_oracle(key, opts):
+    p = _causal() if key == "causal" else irgen.SMALL[key]()
+    _check(p, data.make_inputs(p), opts, "tcgen05_attention")
+
+
+@pytest.mark.parametrize("persistent", [False, True])
+def test_attention_value_range_fallback_emulated(persistent):
+    # one 64-row block of V scaled by 2^20 does not fit f16: that block takes the two-part bf16 path
+    p = irgen.SMALL["c5tcnc"]()
+    t = data.make_inputs(p)
+    V = t["V"].float()
+    V[:, :, 64:128] *= 2.0 ** 20
+    t["V"] = V.to(torch.bfloat16)
+    opts = {"attn_persistent": True, "sms": 1} if persistent else {}
+    _check(p, t, opts, "tcgen05_attention")
+
+
+@pytest.mark.parametrize("sms", [1, 2, 3])
+def test_gemm_emulated_matches_oracle(sms):
+    p = irgen.SMALL["c4tc"]()
+    _check(p, data.make_inputs(p), {"sms": sms}, "tcgen05_gemm")
