@@ -90,13 +90,15 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                     trace: bool = False, half: bool = True, poly_every: int = POLY_EVERY,
                     pingpong: bool = True, f16_int: int = 0, pack_after_turn: bool = False,
                     defer_sum: bool = False, bh_range: tuple[int, int] | None = None,
-                    scratch_names: tuple[str, str] | None = None, prefetch_next: int = 0) -> dict:
+                    scratch_names: tuple[str, str] | None = None, prefetch_next: int = 0,
+                    pack_in_turn: bool = False) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
     ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps.
     ``bh_range`` = (first, count) restricts the launch to those flattened (batch, head) pairs.
     ``prefetch_next`` = n > 0 makes the producer prefetch into L2, after its last load, the Q tiles and
-    first K / V block of CTA index + n (the one likely to start when this one ends)."""
+    first K / V block of CTA index + n (the one likely to start when this one ends).  ``pack_in_turn``
+    keeps all of a block's f16 packing inside its MUFU turn."""
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
@@ -104,6 +106,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     if trace and seq // BKV + 1 >= TRACE_SLOTS:
         raise ValueError("trace supports at most 64 key/value blocks")
     half = half and precise
+    if pack_in_turn and (pack_after_turn or not pingpong):
+        raise ValueError("pack_in_turn applies to the default split packing with turns")
     if defer_sum and (poly_every or not pack_after_turn):
         raise ValueError("defer_sum goes with the MUFU-only exps packed after the turn")
     threads = THREADS
@@ -905,12 +909,17 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             pack_store(range(BKV // 2), 0)
         else:
             for h in range(2):
-                # each half of the row is packed and stored as soon as its exps are done
+                # each half of the row is packed and stored as soon as its exps are done; with
+                # pack_in_turn the second half's packing stays inside the MUFU turn too, so no f16
+                # conversion of this tile runs during the other tile's exps
                 exp_block(poly_every, range(half_n * h, half_n * (h + 1)))
                 if h == 1:
                     sstamp(4)
-                    turn_pass()
+                    if not pack_in_turn:
+                        turn_pass()
                 pack_store(range(half_n * h // 2, half_n * (h + 1) // 2), half_n * h // 2)
+            if pack_in_turn:
+                turn_pass()
         sstamp(5)
         a(f"bra {l_pdone};")
         a.label(l_pbf)

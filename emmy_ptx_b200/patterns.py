@@ -342,7 +342,8 @@ def try_lower(graph, node, kmeta, prefix, options):
                   f16_int=int(options.get("attn_f16_int", 0)),
                   pack_after_turn=bool(options.get("attn_pack_after_turn", False)),
                   defer_sum=bool(options.get("attn_defer_sum", False)),
-                  prefetch_next=int(options.get("attn_prefetch_next", 0)))
+                  prefetch_next=int(options.get("attn_prefetch_next", 0)),
+                  pack_in_turn=bool(options.get("attn_pack_in_turn", False)))
         if options.get("attn_persistent", False):
             # opt-in persistent schedule (one CTA per SM, alternating row halves; see the module)
             from .kernels import tc_attention_persistent as tap, vconv

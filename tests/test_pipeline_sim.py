@@ -37,7 +37,7 @@ def _run_all(txt, rec, seeds=(0, 1), **kw):
 
 @pytest.mark.parametrize("variant", [
     {}, {"pingpong": False}, {"half": False}, {"causal": False}, {"precise": False},
-    {"pack_after_turn": True, "defer_sum": True}, {"prefetch_next": 2},
+    {"pack_after_turn": True, "defer_sum": True}, {"prefetch_next": 2}, {"pack_in_turn": True},
 ])
 def test_attention_pipeline_completes(variant):
     txt, rec = _attention(**variant)

@@ -76,7 +76,9 @@ def _causal():
     ("causal", {"attn_persistent": True, "sms": 1}),
     ("c5tcnc", {"attn_persistent": True, "sms": 1}),
     ("c5tcnc", {"attn_prefetch_next": 1}),
-], ids=["nc", "nc-bf16", "nc-noturns", "causal", "causal-persistent", "nc-persistent", "nc-prefetch"])
+    ("causal", {"attn_pack_in_turn": True}),
+], ids=["nc", "nc-bf16", "nc-noturns", "causal", "causal-persistent", "nc-persistent", "nc-prefetch",
+        "causal-pack-in-turn"])
 def test_attention_emulated_matches_oracle(key, opts):
     p = _causal() if key == "causal" else irgen.SMALL[key]()
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
