@@ -395,6 +395,64 @@ class MultiProblem(Problem):
         return {"kernels": ks, "rtol": self.rtol, "atol": self.atol}
 
 
+def bcast3d(a=3, b=5, c=37):
+    """y[i, j, k] = relu(x[i, j, k] * w[i] + bias[k]) in bf16: broadcasts along the leading and the
+    trailing axis of an odd 3-D shape (555 cells over 64-thread blocks, so the last block is partial)."""
+    body = [Tile([Axis("i", a), Axis("j", b), Axis("k", c)], [
+        Load(["x"], "x", [V("i"), V("j"), V("k")], "f32"),
+        Load(["w"], "w", [V("i")], "f32"),
+        Load(["bias"], "bias", [V("k")], "f32"),
+        Assign("m", "multiply", ["x", "w"]),
+        Assign("s", "add", ["m", "bias"]),
+        Assign("y", "maximum", ["s", Lit(0.0)], "bf16"),
+        Write("y", ["y"], [V("i"), V("j"), V("k")], "bf16"),
+    ])]
+    args = [TensorSpec("x", (a, b, c), "f32", ("normal", 1.0)), TensorSpec("w", (a,), "f32", ("normal", 1.0)),
+            TensorSpec("bias", (c,), "f32", ("normal", 0.5)), TensorSpec("y", (a, b, c), "bf16", output=True)]
+    return _problem("bcast3d", f"bcast3d_{a}x{b}x{c}", "bcast3d", args, body, (a * b * c + 63) // 64, 64)
+
+
+def row_minmax(rows=19, cols=777):
+    """mx[r] = max and mn[r] = min of an odd-length row: a warp per row, lanes striding the columns,
+    one warp shuffle over both states."""
+    body = [Tile([Axis("row", rows), Axis("t", 32)], [
+        StridedLoop("c", cols, V("t"), 32, [
+            Load(["x"], "x", [V("row"), V("c")], "f32"),
+            Accum("mx", "maximum", "x"),
+            Accum("mn", "minimum", "x"),
+        ], end=cols),
+        WarpShuffle(["mx", "mn"], ["mx_o", "mn_o"], [Assign("mx", "maximum", ["mx", "mx_o"]),
+                                                     Assign("mn", "minimum", ["mn", "mn_o"])]),
+        Cond(Bin("==", V("t"), 0), [Write("mx", ["mx"], [V("row")], "f32"), Write("mn", ["mn"], [V("row")], "f32")]),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("mx", (rows,), "f32", output=True),
+            TensorSpec("mn", (rows,), "f32", output=True)]
+    return _problem("minmax", f"minmax_{rows}x{cols}", "row_minmax", args, body, rows, 32)
+
+
+def small_softmax(a=2, b=3, c=45):
+    """softmax over the last axis of a [2, 3, 45] tensor, a thread per row: three rolled loops (max,
+    sum of exps, normalised write) over a length that is not a power of two."""
+    body = [Tile([Axis("i", a), Axis("j", b)], [
+        Loop("k", c, [Load(["x"], "x", [V("i"), V("j"), V("k")], "f32"), Accum("m", "maximum", "x")]),
+        Loop("k1", c, [
+            Load(["x1"], "x", [V("i"), V("j"), V("k1")], "f32"),
+            Assign("z", "subtract", ["x1", "m"]),
+            Assign("e", "exp", ["z"]),
+            Accum("s", "add", "e"),
+        ]),
+        Loop("k2", c, [
+            Load(["x2"], "x", [V("i"), V("j"), V("k2")], "f32"),
+            Assign("z2", "subtract", ["x2", "m"]),
+            Assign("e2", "exp", ["z2"]),
+            Assign("y", "divide", ["e2", "s"]),
+            Write("y", ["y"], [V("i"), V("j"), V("k2")], "f32"),
+        ]),
+    ])]
+    args = [TensorSpec("x", (a, b, c), "f32", ("normal", 2.0)), TensorSpec("y", (a, b, c), "f32", output=True)]
+    return _problem("softmax3d", f"softmax3d_{a}x{b}x{c}", "small_softmax", args, body, 1, a * b)
+
+
 def _kernel_node(entry, inputs, outputs, body):
     return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
             "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
@@ -461,4 +519,7 @@ CORPUS = {
     "k_exprs": exprs,
     "k_chain": chain_mul_relu,
     "k_hist": zero_then_histogram,
+    "k_bcast3d": bcast3d,
+    "k_minmax": row_minmax,
+    "k_softmax3d": small_softmax,
 }

@@ -154,4 +154,8 @@ CORPUS = {
     "exprs": _exprs,
     "chain": _chain,
     "hist": lambda t, p: {"hist": __import__("torch").bincount(t["x"].long() % p["bins"], minlength=p["bins"])},
+    "bcast3d": lambda t, p: {"y": __import__("torch").relu(t["x"].double() * t["w"].double()[:, None, None]
+                                                           + t["bias"].double()[None, None, :])},
+    "minmax": lambda t, p: {"mx": t["x"].double().amax(-1), "mn": t["x"].double().amin(-1)},
+    "softmax3d": lambda t, p: {"y": __import__("torch").softmax(t["x"].double(), -1)},
 }
