@@ -60,9 +60,20 @@ def _bf16_rn(x: np.float32) -> int:
     return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) & 0xFFFF
 
 
-def _f16_rn(x: np.float32) -> int:
-    with np.errstate(over="ignore"):                  # beyond the f16 range: infinity, as cvt.rn does
-        return int(np.array([x], dtype=np.float32).astype(np.float16).view(np.uint16)[0])
+_PH = struct.Struct("<e")
+_PU16 = struct.Struct("<H")
+
+
+def _f16_rn(x) -> int:
+    """f16 bits of x, rounded to nearest even; beyond the f16 range: infinity, as cvt.rn does."""
+    x = float(x)
+    try:
+        return _PU16.unpack(_PH.pack(x))[0]
+    except OverflowError:
+        if x != x:
+            return 0x7E00
+        # |x| at or above 65520 (the midpoint above 65504) rounds to infinity; below it to 65504
+        return (0xFC00 if x < 0 else 0x7C00) if abs(x) >= 65520.0 else (0xFBFF if x < 0 else 0x7BFF)
 
 
 _PI, _PF = struct.Struct("<I"), struct.Struct("<f")
@@ -282,6 +293,8 @@ class Emulator:
                     resolved = True
                 elif any(t.state == "done" for t in members):
                     raise RuntimeError(f"warp {w}: a collective's member lane has exited")
+            if not resolved and not any(t.state == "run" for t in live) and self._drain_async():
+                continue                               # deferred asynchronous work completed: retry
             if not resolved and not progressed:
                 where = sorted({(t.state, self.ins[t.pc].op if t.pc < len(self.ins) else "end") for t in live})
                 raise RuntimeError(f"deadlock: {where}")
@@ -338,6 +351,14 @@ class Emulator:
             if d is None:
                 d = dec[th.pc] = self._decode(x)
             code = d[0]
+            if code == 7:                               # tensor-core / barrier extension
+                th.pc += 1
+                r = self._extra(th, x, x.op, x.ops, regs, val, addr, smem, mem)
+                if r is None:
+                    raise NotImplementedError(f"line {x.line}: {x.op}")
+                if r == "block":
+                    return n
+                continue
             if code == 2:                               # integer / predicate / move
                 th.pc += 1
                 if not alu(x.op, x.ops, regs, val):
@@ -432,14 +453,24 @@ class Emulator:
     def _extra(self, th, x, op, ops, regs, val, addr, smem, mem):
         return None
 
+    def _drain_async(self) -> bool:
+        """Complete deferred asynchronous work when no thread can run; True if there was some."""
+        return False
+
     @staticmethod
     def _decode(x):
         """(1, function, destination, sources, ftz) for plain f32 arithmetic; (0,) otherwise.  Sources
         are register names or, for immediates, Python floats."""
-        if x.label or not x.ops:
+        if x.label:
+            return (0,)
+        op = x.op
+        if op.startswith(("mbarrier.", "tcgen05.", "cp.async.bulk", "prmt.", "max.u16x2", "min.u16x2")) or (
+                ".f32x2" in op) or (op.startswith(("bar.arrive", "bar.red")) or (
+                op.startswith(("bar.sync", "barrier.sync")) and len(x.ops) == 2)):
+            return (7,)
+        if not x.ops:
             return (0,)
         parts = x.op.split(".")
-        op = x.op
         if op.startswith(("ld.global", "ld.shared", "ldu.global")):
             return (3,)
         if op.startswith(("st.global", "st.shared")) and not (len(x.ops) == 2 and _IMM.match(x.ops[1].strip())):

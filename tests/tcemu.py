@@ -49,8 +49,13 @@ def _halves_to_float(bits: np.ndarray, fmt: int) -> np.ndarray:
 class TcEmulator(Emulator):
     """``tmaps``: parameter name (``p_tmQ``) -> (global address of the tensor, tensor-map spec)."""
 
-    def __init__(self, ptx: str, entry: str, tmaps: dict | None = None):
+    def __init__(self, ptx: str, entry: str, tmaps: dict | None = None, defer: bool = False):
         super().__init__(ptx, entry)
+        # defer: TMA loads, MMAs and commits are queued and run only when no thread can run, TMA
+        # writes first, then the MMAs and commits in issue order.  Anything the barrier protocol does
+        # not order (an MMA reading a stage a later load overwrites, a load of data whose barrier was not
+        # waited on) then reads the wrong data and shows in the result.
+        self.defer = defer
         self.tmaps_by_param = tmaps or {}
         self.fake = {}
         for k, (pname, (gaddr, spec)) in enumerate(self.tmaps_by_param.items()):
@@ -61,6 +66,9 @@ class TcEmulator(Emulator):
 
     # ------------------------------------------------------------------ per-CTA state
     def _cta_begin(self, cta, smem):
+        self.smem = smem
+        self.queue_tma: list = []
+        self.queue_mma: list = []
         self.mbars: dict[int, _MBar] = {}
         self.nbars: dict[int, list] = {}
         self.tmem = np.zeros((128, 512), dtype=np.uint32)
@@ -92,6 +100,24 @@ class TcEmulator(Emulator):
 
     # ------------------------------------------------------------------ instructions
     def _extra(self, th, x, op, ops, regs, val, addr, smem, mem):
+        if ".f32x2" in op:
+            head = op.split(".")[0]
+            if head in ("fma", "add", "mul", "sub"):
+                vs = [val(o) for o in ops[1:]]
+                out = 0
+                for h in range(2):
+                    f = [_bf((v >> (32 * h)) & _M32) for v in vs]
+                    r = (f[0] * f[1] + f[2] if head == "fma" else f[0] + f[1] if head == "add"
+                         else f[0] * f[1] if head == "mul" else f[0] - f[1])
+                    out |= _fb(r) << (32 * h)
+                regs[ops[0]] = out
+                return "cont"
+        if op.startswith("tcgen05.ld"):
+            self._tmem_ld(th, op, ops, regs, addr)
+            return "cont"
+        if op.startswith("tcgen05.st"):
+            self._tmem_st(th, op, ops, regs, addr, val)
+            return "cont"
         if op.startswith("mbarrier.init"):
             self.mbars[addr(ops[0]) & _M32] = _MBar(val(ops[1]))
             return "cont"
@@ -135,7 +161,11 @@ class TcEmulator(Emulator):
             th.coll = ("bar.red.or", bool(regs.get(ops[2])), ops[0])
             return "block"
         if op.startswith("cp.async.bulk.tensor") and "complete_tx" in op:
-            self._tma_load(ops, regs, val, addr, smem, mem)
+            if self.defer:
+                dst, tm, cs, mb = self._tma_args(ops, val, addr)
+                self.queue_tma.append((dst, tm, cs, mb, mem))
+            else:
+                self._tma_load(ops, regs, val, addr, smem, mem)
             return "cont"
         if op.startswith("cp.async.bulk.prefetch"):
             return "cont"
@@ -146,10 +176,25 @@ class TcEmulator(Emulator):
         if op.startswith(("tcgen05.relinquish", "tcgen05.dealloc", "tcgen05.fence", "tcgen05.wait")):
             return "cont"
         if op.startswith("tcgen05.commit"):
-            self._arrive(addr(ops[0]) & _M32)
+            if self.defer:
+                self.queue_mma.append(("commit", addr(ops[0]) & _M32))
+            else:
+                self._arrive(addr(ops[0]) & _M32)
             return "cont"
         if op.startswith("tcgen05.mma"):
-            self._mma(op, ops, regs, val, smem)
+            if self.defer:
+                # operands evaluated now (as the instruction reads its registers at issue)
+                snap = {o.strip(): val(o.strip()) for o in ops if o.strip().startswith("%")}
+                for o in ops:
+                    o = o.strip()
+                    if o.startswith("[") and "%" in o:
+                        r = o[1:-1].split("+")[0].strip()
+                        snap[r] = val(r)
+                en = ops[4].strip()
+                snap["__acc"] = bool(regs.get(en)) if en.startswith("%") else bool(int(en, 0))
+                self.queue_mma.append(("mma", op, list(ops), snap))
+            else:
+                self._mma(op, ops, regs, val, smem)
             return "cont"
         if op.startswith("tcgen05.ld"):
             self._tmem_ld(th, op, ops, regs, addr)
@@ -183,14 +228,46 @@ class TcEmulator(Emulator):
             return "cont"
         return None
 
+    def _drain_async(self) -> bool:
+        if not (self.queue_tma or self.queue_mma):
+            return False
+        tmas, self.queue_tma = self.queue_tma, []
+        for dst, tm, cs, mb, mem in tmas:
+            self._tma_write(dst, tm, cs, mb, self.smem, mem)
+        mmas, self.queue_mma = self.queue_mma, []
+        for item in mmas:
+            if item[0] == "commit":
+                self._arrive(item[1])
+            else:
+                _, op, ops, snap = item
+                regs = dict(snap)
+                en = ops[4].strip()
+                if en.startswith("%"):
+                    regs[en] = snap["__acc"]
+
+                def val(o, regs=regs):
+                    o = o.strip()
+                    if _IMM.match(o):
+                        return int(o, 0)
+                    return regs[o]
+                self._mma(op, ops, regs, val, self.smem)
+        return True
+
     # ------------------------------------------------------------------ TMA
-    def _tma_load(self, ops, regs, val, addr, smem, mem):
+    def _tma_args(self, ops, val, addr):
         dst = addr(ops[0]) & _M32
         inner = ops[1].strip()[1:-1]
         tm_op, coords = inner.split(",", 1)
         tm = val(tm_op.strip())
-        gaddr, spec = self.fake[tm]
         cs = [val(c) for c in coords.strip().strip("{}").split(",")]
+        return dst, tm, cs, addr(ops[2]) & _M32
+
+    def _tma_load(self, ops, regs, val, addr, smem, mem):
+        dst, tm, cs, mb = self._tma_args(ops, val, addr)
+        self._tma_write(dst, tm, cs, mb, smem, mem)
+
+    def _tma_write(self, dst, tm, cs, mb, smem, mem):
+        gaddr, spec = self.fake[tm]
         es = _DTYPE_BYTES[spec["dtype"]]
         box = [int(b) for b in spec["box"]]
         dims = [int(d) for d in spec["dims"]]
@@ -223,11 +300,11 @@ class TcEmulator(Emulator):
             if a + 16 > len(smem):
                 raise IndexError(f"TMA box past shared memory ({a})")
             smem[a:a + 16] = out[off:off + 16]
-        b = self.mbars[addr(ops[2]) & _M32]
+        b = self.mbars[mb]
         b.tx -= len(out)
         if b.tx < 0:
             raise RuntimeError("TMA delivered more bytes than the mbarrier expects")
-        self._settle(addr(ops[2]) & _M32, b)
+        self._settle(mb, b)
 
     # ------------------------------------------------------------------ tensor memory
     def _tmem_lane_col(self, th, a):

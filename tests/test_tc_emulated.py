@@ -25,7 +25,7 @@ def _np(t: torch.Tensor) -> np.ndarray:
     return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
 
 
-def run_emulated(p, t, opts):
+def run_emulated(p, t, opts, defer=False):
     """Compile ``p`` with ``opts`` and run every entry through the emulator on tensors ``t``; returns
     the outputs and the error word."""
     mod = compile_graph(Graph.from_dict(p.graph), p.meta(), opts)
@@ -38,7 +38,7 @@ def run_emulated(p, t, opts):
     err = mem.alloc(np.zeros(16, np.uint8))
     for rec in mod.kernels:
         tm = {f"p_{spec['name']}": (addr[spec["tensor"]], spec) for spec in rec.get("tmaps", [])}
-        emu = TcEmulator(mod.ptx, rec["entry"], tm)
+        emu = TcEmulator(mod.ptx, rec["entry"], tm, defer=defer)
         plain = [q for q in emu.params if not q.startswith("p_tm") and q not in ("p_err", "p_trace")]
         args = dict(zip(plain, [addr[n] for n in rec["params"]]))
         args.update(emu.tmap_args())
@@ -53,8 +53,8 @@ def run_emulated(p, t, opts):
     return out, int(mem.array(err, np.int32, (4,))[0]), mod
 
 
-def _check(p, t, opts, kind):
-    got, code, mod = run_emulated(p, t, opts)
+def _check(p, t, opts, kind, defer=False):
+    got, code, mod = run_emulated(p, t, opts, defer)
     assert mod.kernels[-1]["kind"] == kind
     assert code == 0
     want = oracle_outputs(p, t)
@@ -76,9 +76,9 @@ def _causal():
     ("causal", {"attn_persistent": True, "sms": 1}),
     ("c5tcnc", {"attn_persistent": True, "sms": 1}),
     ("c5tcnc", {"attn_prefetch_next": 1}),
-    ("causal", {"attn_pack_in_turn": True}),
+    ("c5tcnc", {"attn_pack_in_turn": True}),
 ], ids=["nc", "nc-bf16", "nc-noturns", "causal", "causal-persistent", "nc-persistent", "nc-prefetch",
-        "causal-pack-in-turn"])
+        "nc-pack-in-turn"])
 def test_attention_emulated_matches_oracle(key, opts):
     p = _causal() if key == "causal" else irgen.SMALL[key]()
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
@@ -100,3 +100,20 @@ def test_attention_value_range_fallback_emulated(persistent):
 def test_gemm_emulated_matches_oracle(sms):
     p = irgen.SMALL["c4tc"]()
     _check(p, data.make_inputs(p), {"sms": sms}, "tcgen05_gemm")
+
+
+@pytest.mark.parametrize("key,opts", [
+    ("c5tcnc", {}),
+    ("causal", {"attn_persistent": True, "sms": 1}),
+    ("c5tcnc", {"attn_persistent": True, "sms": 1, "attn_half": False}),
+], ids=["nc", "causal-persistent", "nc-persistent-bf16"])
+def test_attention_with_late_completions(key, opts):
+    # loads, MMAs and commits complete only when every thread waits, loads first: a stage, Q tile,
+    # score buffer or O accumulator reused before the hardware is done with it would change the result
+    p = _causal() if key == "causal" else irgen.SMALL[key]()
+    _check(p, data.make_inputs(p), opts, "tcgen05_attention", defer=True)
+
+
+def test_gemm_with_late_completions():
+    p = irgen.SMALL["c4tc"]()
+    _check(p, data.make_inputs(p), {"sms": 2}, "tcgen05_gemm", defer=True)
