@@ -234,10 +234,15 @@ class TcEmulator(Emulator):
         tmas, self.queue_tma = self.queue_tma, []
         for dst, tm, cs, mb, mem in tmas:
             self._tma_write(dst, tm, cs, mb, self.smem, mem)
-        mmas, self.queue_mma = self.queue_mma, []
-        for item in mmas:
+        # the tensor core then advances only until some thread can run again, so work that the barrier
+        # protocol lets other threads overtake stays pending as long as possible
+        woke = [False]
+        while self.queue_mma and not woke[0]:
+            item = self.queue_mma.pop(0)
             if item[0] == "commit":
+                before = sum(len(v) for v in self.mbar_waiters.values())
                 self._arrive(item[1])
+                woke[0] = sum(len(v) for v in self.mbar_waiters.values()) < before
             else:
                 _, op, ops, snap = item
                 regs = dict(snap)

@@ -25,10 +25,10 @@ def _np(t: torch.Tensor) -> np.ndarray:
     return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
 
 
-def run_emulated(p, t, opts, defer=False):
-    """Compile ``p`` with ``opts`` and run every entry through the emulator on tensors ``t``; returns
-    the outputs and the error word."""
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), opts)
+def run_emulated(p, t, opts, defer=False, mod=None):
+    """Compile ``p`` with ``opts`` (or take ``mod``) and run every entry through the emulator on
+    tensors ``t``; returns the outputs and the error word."""
+    mod = mod or compile_graph(Graph.from_dict(p.graph), p.meta(), opts)
     mem = Memory()
     addr = {name: mem.alloc(_np(ten).copy()) for name, ten in t.items()}
     for rec in mod.kernels:
@@ -53,8 +53,8 @@ def run_emulated(p, t, opts, defer=False):
     return out, int(mem.array(err, np.int32, (4,))[0]), mod
 
 
-def _check(p, t, opts, kind, defer=False):
-    got, code, mod = run_emulated(p, t, opts, defer)
+def _check(p, t, opts, kind, defer=False, mod=None):
+    got, code, mod = run_emulated(p, t, opts, defer, mod)
     assert mod.kernels[-1]["kind"] == kind
     assert code == 0
     want = oracle_outputs(p, t)
@@ -103,17 +103,39 @@ def test_gemm_emulated_matches_oracle(sms):
 
 
 @pytest.mark.parametrize("key,opts", [
-    ("c5tcnc", {}),
+    ("nc512", {}),
     ("causal", {"attn_persistent": True, "sms": 1}),
     ("c5tcnc", {"attn_persistent": True, "sms": 1, "attn_half": False}),
 ], ids=["nc", "causal-persistent", "nc-persistent-bf16"])
 def test_attention_with_late_completions(key, opts):
-    # loads, MMAs and commits complete only when every thread waits, loads first: a stage, Q tile,
-    # score buffer or O accumulator reused before the hardware is done with it would change the result
-    p = _causal() if key == "causal" else irgen.SMALL[key]()
+    # loads, MMAs and commits complete only when every thread waits, loads first, and the tensor core
+    # advances only until a thread can run: a ring stage, Q tile, score buffer or O accumulator reused
+    # before the hardware is done with it changes the result (8 kv blocks: every ring stage is reused)
+    p = {"causal": _causal, "nc512": lambda: irgen.attention_ir(1, 1, 512, 128, False)}.get(
+        key, lambda: irgen.SMALL[key]())()
     _check(p, data.make_inputs(p), opts, "tcgen05_attention", defer=True)
 
 
 def test_gemm_with_late_completions():
     p = irgen.SMALL["c4tc"]()
     _check(p, data.make_inputs(p), {"sms": 2}, "tcgen05_gemm", defer=True)
+
+
+def test_late_completions_expose_a_planted_early_release():
+    # the ring's empty barriers wait for both issuers (count 2); with a count of 1 a stage is refilled
+    # after the first issuer's MMAs, while the other tile's may still read it: with late completions
+    # the run must fail (a wrong result, or the barrier accounting going wrong)
+    import re
+    from emmy_ptx_b200.compiler import CompiledModule
+    from emmy_ptx_b200.kernels import tc_attention as ta
+    p = irgen.attention_ir(1, 1, 512, 128, False)            # 8 kv blocks: every ring stage is reused
+    t = data.make_inputs(p)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {})
+    bad = mod.ptx
+    for s_ in range(ta.STAGES):
+        pat = r"(mbarrier\.init\.shared::cta\.b64 \[%r\d+\+" + str(ta.EMPTY + 8 * s_) + r"\]), 2;"
+        bad, n = re.subn(pat, r"\1, 1;", bad)
+        assert n == 1
+    _check(p, t, {}, "tcgen05_attention", defer=True)            # the real kernel passes
+    with pytest.raises((AssertionError, RuntimeError)):
+        _check(p, t, {}, "tcgen05_attention", defer=True, mod=CompiledModule(bad, mod.kernels))
