@@ -77,7 +77,6 @@ def _f16_rn(x) -> int:
 
 
 _PI, _PF = struct.Struct("<I"), struct.Struct("<f")
-_FLT_MAX = 3.4028234663852886e38
 _FLT_ROUND_UP = 3.4028235677973366e38          # 2^128 - 2^103: the midpoint above the largest float
 _TINY = 1.1754943508222875e-38                 # 2^-126
 

@@ -28,9 +28,6 @@ import numpy as np
 from tests.ptxemu import Emulator, _M32, _bf, _fb, _IMM
 from tests.ctasim import _DTYPE_BYTES
 
-_NP = {"bf16": np.uint16, "f16": np.uint16, "f32": np.uint32, "u8": np.uint8, "i32": np.uint32}
-
-
 class _MBar:
     __slots__ = ("count", "pending", "tx", "phase")
 
@@ -73,7 +70,6 @@ class TcEmulator(Emulator):
         self.nbars: dict[int, list] = {}
         self.tmem = np.zeros((128, 512), dtype=np.uint32)
         self.mbar_waiters: dict[int, list] = {}
-        self.threads_by_state = None
 
     def _bar_release(self, threads):
         red = [t for t in threads if t.coll and t.coll[0] == "bar.red.or"]
