@@ -249,17 +249,18 @@ def _combine(name, other, op, dtype):
 # ---- config 1: row softmax ------------------------------------------------------------------
 
 
-def softmax_ir(rows: int = 4096, cols: int = 1024, schedule: str | None = None) -> Problem:
+def softmax_ir(rows: int = 4096, cols: int = 1024, schedule: str | None = None, recip: bool = False) -> Problem:
     """y = softmax(x, -1) for x f32 [rows, cols].
 
     ``schedule="warp"`` (the default up to 1024 columns): one warp per row, each lane holding cols/32
     values from cols/128 coalesced 16-byte loads issued back to back, both reductions inside the warp.
     ``schedule="block"``: one block of cols/4 threads per row, WarpShuffle then TreeHalve across warps.
+    ``recip`` (warp schedule): y = e * (1 / s) with one division per row instead of one per element.
     """
     if schedule is None:
         schedule = "warp" if cols <= 1024 else "block"
     if schedule == "warp":
-        return _softmax_warp_ir(rows, cols)
+        return _softmax_warp_ir(rows, cols, recip)
     if cols % 128 or cols // 4 > 1024:
         raise ValueError("softmax_ir needs cols % 128 == 0 and cols <= 4096")
     t = cols // 4
@@ -314,7 +315,7 @@ def _tree(op: str, names: list, prefix: str, final: str) -> list:
     return stmts
 
 
-def _softmax_warp_ir(rows: int, cols: int) -> Problem:
+def _softmax_warp_ir(rows: int, cols: int, recip: bool = False) -> Problem:
     if cols % 128 or cols > 1024:
         raise ValueError("the warp-per-row softmax needs cols % 128 == 0 and cols <= 1024")
     chunks = cols // 128
@@ -333,7 +334,8 @@ def _softmax_warp_ir(rows: int, cols: int) -> Problem:
         *[Assign(f"e_{n}", "exp", [f"z_{n}"]) for n in flat],
         *_tree("add", es, "sm", "s"),
         WarpShuffle(["s"], ["s_o"], _combine("s", "s_o", "add", "f32")),
-        *[Assign(f"y_{n}", "divide", [f"e_{n}", "s"]) for n in flat],
+        *([Assign("rs", "divide", [Lit(1.0), "s"]), *[Assign(f"y_{n}", "multiply", [f"e_{n}", "rs"]) for n in flat]]
+          if recip else [Assign(f"y_{n}", "divide", [f"e_{n}", "s"]) for n in flat]),
         *[Write("y", [f"y_{n}" for n in xs[c]], [V("row"), V(f"col{c}")], "f32") for c in range(chunks)],
     ])]
     args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)),
@@ -341,7 +343,7 @@ def _softmax_warp_ir(rows: int, cols: int) -> Problem:
     threads = 128
     return Problem(f"softmax_{rows}x{cols}", "softmax", "row_softmax", _graph("row_softmax", args, body),
                    args, grid=(rows * 32 + threads - 1) // threads, block=threads, rtol=1e-5, atol=1e-7,
-                   params={"rows": rows, "cols": cols, "schedule": "warp"})
+                   params={"rows": rows, "cols": cols, "schedule": "warp", **({"recip": True} if recip else {})})
 
 
 # ---- config 2: full-array sum ---------------------------------------------------------------

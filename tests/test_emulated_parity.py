@@ -117,3 +117,10 @@ def test_small_cuda_core_bmm_and_attention():
         mod_opts = {"patterns": False}
         t, got = _run_ours(p, mod_opts)
         _check(p, t, got, f"emu:{p.name}")
+
+
+def test_softmax_with_one_division_per_row():
+    # the warp-per-row softmax with y = e * (1 / s): one IEEE division per row instead of per element
+    p = irgen.softmax_ir(64, 1024, "warp", recip=True)
+    t, got = _run_ours(p)
+    _check(p, t, got, "emu:softmax-recip")
