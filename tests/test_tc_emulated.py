@@ -77,8 +77,9 @@ def _causal():
     ("c5tcnc", {"attn_persistent": True, "sms": 1}),
     ("c5tcnc", {"attn_prefetch_next": 1}),
     ("c5tcnc", {"attn_pack_in_turn": True}),
+    ("c5tc", {"attn_persistent": True, "sms": 2}),        # 4 units over 2 CTAs: each walks a long and a short one
 ], ids=["nc", "nc-bf16", "nc-noturns", "causal", "causal-persistent", "nc-persistent", "nc-prefetch",
-        "nc-pack-in-turn"])
+        "nc-pack-in-turn", "causal-persistent-2ctas"])
 def test_attention_emulated_matches_oracle(key, opts):
     p = _causal() if key == "causal" else irgen.SMALL[key]()
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
