@@ -71,6 +71,11 @@ struct Driver {
 Driver g_drv;
 std::mutex g_mu;
 bool g_loaded = false;
+// The selected device: every call after emmy_init(d) runs in d's primary context.  Each device's
+// primary context is retained once, on its first emmy_init, and kept for the process's lifetime.
+constexpr int kMaxDevices = 64;
+CUcontext g_ctxs[kMaxDevices] = {};
+CUdevice g_devs[kMaxDevices] = {};
 CUcontext g_ctx = nullptr;
 CUdevice g_dev = 0;
 
@@ -200,15 +205,21 @@ int emmy_last_error(char* buf, size_t n) {
 }
 
 int emmy_init(int device) {
+  if (device < 0 || device >= kMaxDevices) return fail(EMMY_ERR_BAD_ARG, "device %d out of range", device);
   if (int rc = load_driver()) return rc;
-  if (int rc = cu(g_drv.Init(0), "cuInit")) return rc;
-  CUdevice dev;
-  if (int rc = cu(g_drv.DeviceGet(&dev, device), "cuDeviceGet")) return rc;
-  CUcontext ctx;
-  if (int rc = cu(g_drv.PrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain")) return rc;
-  if (int rc = cu(g_drv.CtxSetCurrent(ctx), "cuCtxSetCurrent")) return rc;
-  g_ctx = ctx;
-  g_dev = dev;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_ctxs[device]) {
+    if (int rc = cu(g_drv.Init(0), "cuInit")) return rc;
+    CUdevice dev;
+    if (int rc = cu(g_drv.DeviceGet(&dev, device), "cuDeviceGet")) return rc;
+    CUcontext ctx;
+    if (int rc = cu(g_drv.PrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain")) return rc;
+    g_ctxs[device] = ctx;
+    g_devs[device] = dev;
+  }
+  if (int rc = cu(g_drv.CtxSetCurrent(g_ctxs[device]), "cuCtxSetCurrent")) return rc;
+  g_ctx = g_ctxs[device];
+  g_dev = g_devs[device];
   return 0;
 }
 

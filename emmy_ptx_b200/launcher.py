@@ -123,12 +123,20 @@ class Device:
     """The launcher bound to one CUDA device (its primary context)."""
 
     _inited: dict[int, "Device"] = {}
+    _active: int | None = None          # the device the library has selected (emmy_init)
 
     def __init__(self, index: int = 0):
         self.lib = load_library()
         self.index = index
-        check(self.lib.emmy_init(index), f"emmy_init({index})")
         self.launches = 0
+        self._use()
+
+    def _use(self) -> None:
+        """Select this device in the library before a call that runs in its context, so that objects
+        bound to different devices in one process each reach their own."""
+        if Device._active != self.index:
+            check(self.lib.emmy_init(self.index), f"emmy_init({self.index})")
+            Device._active = self.index
 
     @classmethod
     def get(cls, index: int = 0) -> "Device":
@@ -136,16 +144,17 @@ class Device:
         if dev is None:
             dev = cls(index)
             cls._inited[index] = dev
-        else:
-            check(dev.lib.emmy_init(index), f"emmy_init({index})")
+        dev._use()
         return dev
 
     def attribute(self, attr: int) -> int:
+        self._use()
         v = ctypes.c_int()
         check(self.lib.emmy_device_attribute(attr, ctypes.byref(v)), "emmy_device_attribute")
         return v.value
 
     def load_ptx(self, ptx: str):
+        self._use()
         mod = vp()
         log = ctypes.create_string_buffer(16384)
         check(self.lib.emmy_module_load_ptx(ptx.encode("ascii"), ctypes.byref(mod), log, len(log)),
@@ -153,34 +162,41 @@ class Device:
         return mod
 
     def load_image(self, image: bytes):
+        self._use()
         mod = vp()
         buf = ctypes.create_string_buffer(image, len(image))
         check(self.lib.emmy_module_load_image(ctypes.cast(buf, vp), ctypes.byref(mod)), "emmy_module_load_image")
         return mod
 
     def unload(self, mod) -> None:
+        self._use()
         check(self.lib.emmy_module_unload(mod), "emmy_module_unload")
 
     def function(self, mod, entry: str):
+        self._use()
         fn = vp()
         check(self.lib.emmy_get_function(mod, entry.encode(), ctypes.byref(fn)), f"emmy_get_function({entry})")
         return fn
 
     def func_attribute(self, fn, attr: int) -> int:
+        self._use()
         v = ctypes.c_int()
         check(self.lib.emmy_func_attribute(fn, attr, ctypes.byref(v)), "emmy_func_attribute")
         return v.value
 
     def set_max_dyn_smem(self, fn, nbytes: int) -> None:
+        self._use()
         check(self.lib.emmy_set_max_dyn_smem(fn, int(nbytes)), "emmy_set_max_dyn_smem")
 
     def set_carveout(self, fn, percent: int) -> None:
+        self._use()
         check(self.lib.emmy_set_smem_carveout(fn, int(percent)), "emmy_set_smem_carveout")
 
     def launch_u64(self, fn, grid, block, dyn_smem: int, stream: int, params, align=None, pdl: bool = False) -> None:
         """Launch a kernel whose parameters are all 64-bit values.  ``pdl`` launches it as a
         programmatic dependent of the stream's previous work (the kernel must begin with
         ``griddepcontrol.wait``, as the launch record's ``pdl`` says)."""
+        self._use()
         n = len(params)
         p = (ctypes.c_uint64 * n)(*[int(x) for x in params])
         a = (ctypes.c_uint32 * n)(*[int(x) for x in align]) if align is not None else None
@@ -190,6 +206,7 @@ class Device:
 
     def launch(self, fn, grid, block, dyn_smem: int, stream: int, arg_ptrs, cluster=(1, 1, 1),
                pdl: bool = False) -> None:
+        self._use()
         n = len(arg_ptrs)
         args = (vp * n)(*arg_ptrs)
         check(self.lib.emmy_launch_ex(fn, dims3(grid), dims3(block), dims3(cluster), int(dyn_smem),
@@ -207,18 +224,22 @@ class Device:
                                               swizzle, l2promo, oob_fill), "emmy_tmap_encode_tiled")
 
     def memset_d32(self, dptr: int, value: int, count: int, stream: int) -> None:
+        self._use()
         check(self.lib.emmy_memset_d32_async(int(dptr), value & 0xFFFFFFFF, int(count), vp(stream or 0)),
               "emmy_memset_d32_async")
 
     def htod(self, dst: int, src_ptr: int, nbytes: int, stream: int) -> None:
+        self._use()
         check(self.lib.emmy_memcpy_htod_async(int(dst), vp(src_ptr), int(nbytes), vp(stream or 0)),
               "emmy_memcpy_htod_async")
 
     def dtoh(self, dst_ptr: int, src: int, nbytes: int, stream: int) -> None:
+        self._use()
         check(self.lib.emmy_memcpy_dtoh_async(vp(dst_ptr), int(src), int(nbytes), vp(stream or 0)),
               "emmy_memcpy_dtoh_async")
 
     def sync(self, stream: int | None = None) -> None:
+        self._use()
         if stream is None:
             check(self.lib.emmy_ctx_synchronize(), "emmy_ctx_synchronize")
         else:
@@ -226,38 +247,46 @@ class Device:
 
     # events
     def event(self):
+        self._use()
         ev = vp()
         check(self.lib.emmy_event_create(ctypes.byref(ev)), "emmy_event_create")
         return ev
 
     def sync_event(self):
         """An event for ordering only (no timing)."""
+        self._use()
         ev = vp()
         check(self.lib.emmy_event_create_flags(ctypes.byref(ev), 2), "emmy_event_create_flags")
         return ev
 
     def stream(self) -> int:
         """A new non-blocking stream (its handle)."""
+        self._use()
         s = vp()
         check(self.lib.emmy_stream_create(ctypes.byref(s)), "emmy_stream_create")
         return s.value
 
     def destroy_stream(self, stream: int) -> None:
+        self._use()
         check(self.lib.emmy_stream_destroy(vp(stream)), "emmy_stream_destroy")
 
     def wait_event(self, stream: int, ev) -> None:
+        self._use()
         check(self.lib.emmy_stream_wait_event(vp(stream or 0), ev), "emmy_stream_wait_event")
 
     def record(self, ev, stream: int) -> None:
+        self._use()
         check(self.lib.emmy_event_record(ev, vp(stream or 0)), "emmy_event_record")
 
     def elapsed_ms(self, a, b) -> float:
+        self._use()
         check(self.lib.emmy_event_synchronize(b), "emmy_event_synchronize")
         ms = ctypes.c_float()
         check(self.lib.emmy_event_elapsed_ms(a, b, ctypes.byref(ms)), "emmy_event_elapsed_ms")
         return ms.value
 
     def destroy_event(self, ev) -> None:
+        self._use()
         check(self.lib.emmy_event_destroy(ev), "emmy_event_destroy")
 
     # NCCL
@@ -267,9 +296,11 @@ class Device:
         return buf.raw[:128]
 
     def nccl_init(self, rank: int, nranks: int, uid: bytes) -> None:
+        self._use()
         check(self.lib.emmy_nccl_init(rank, nranks, ctypes.create_string_buffer(uid, 128)), "emmy_nccl_init")
 
     def allreduce_sum(self, dptr: int, count: int, dtype: str, stream: int) -> None:
+        self._use()
         code = {"f32": 0, "i32": 1}[dtype]
         check(self.lib.emmy_allreduce_sum(int(dptr), int(count), code, vp(stream or 0)), "emmy_allreduce_sum")
 
@@ -277,10 +308,12 @@ class Device:
                     dyn_smem: int, scratch_bytes: int, stream: int) -> None:
         """The tensor-core bmm through the entry point that allocates nothing (its scratch is a fixed
         array inside the library)."""
+        self._use()
         check(self.lib.emmy_bmm_bf16_noalloc(fn, vp(tmap_a), vp(tmap_b), int(a), int(b), int(c), int(grid),
                                              int(block), int(dyn_smem), int(scratch_bytes), vp(stream or 0)),
               "emmy_bmm_bf16_noalloc")
         self.launches += 1
 
     def nccl_destroy(self) -> None:
+        self._use()
         check(self.lib.emmy_nccl_destroy(), "emmy_nccl_destroy")

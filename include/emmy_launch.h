@@ -14,8 +14,8 @@
  *  - Device pointers are CUdeviceptr values (uint64_t) owned by the caller; module, function,
  *    event and communicator handles are owned by the library.
  *  - One CUDA context per device: the device's primary context (the one the CUDA runtime and
- *    PyTorch use), made current on the calling thread by emmy_init().  Multi-GPU runs use one
- *    process per GPU.
+ *    PyTorch use), selected by emmy_init().  Multi-GPU runs use one process per GPU; a process
+ *    that drives several devices calls emmy_init(d) before working on device d.
  *  - libcuda.so.1 and libnccl.so.2 are opened on first use, so the library itself loads on a
  *    host without a GPU.
  */
@@ -41,8 +41,9 @@ int emmy_version(void);
 /* Copies the last error message of this thread into buf (always NUL-terminated). */
 int emmy_last_error(char* buf, size_t n);
 
-/* Opens the driver, retains device `device`'s primary context and makes it current.
- * Replaces cuInit/cuDeviceGet/cuCtxCreate in tools/localrun.py:33-46. */
+/* Opens the driver and selects device `device`: its primary context (retained on the first call
+ * for that device) becomes current, and every later call runs in it until emmy_init selects
+ * another device.  Replaces cuInit/cuDeviceGet/cuCtxCreate in tools/localrun.py:33-46. */
 int emmy_init(int device);
 
 /* cuDeviceGetAttribute for the initialised device. */

@@ -61,3 +61,44 @@ def test_stream_and_event_arguments_are_checked_before_the_driver():
     assert lib.emmy_set_smem_carveout(None, 50) != 0
     assert lib.emmy_set_smem_carveout(vp(0x1000), 101) != 0              # outside -1..100
     assert "carveout" in launcher.last_error()
+
+
+def test_device_index_is_checked_before_the_driver():
+    lib = launcher.load_library()
+    for bad in (-1, 64):
+        assert lib.emmy_init(bad) == 10003                                # EMMY_ERR_BAD_ARG
+        assert "out of range" in launcher.last_error()
+
+
+class _FakeLib:
+    """Records which device the library has selected when each context-bound call arrives."""
+
+    def __init__(self):
+        self.selected = None
+        self.calls = []
+
+    def emmy_init(self, index):
+        self.selected = index
+        return 0
+
+    def __getattr__(self, name):
+        def call(*args):
+            self.calls.append((name, self.selected))
+            return 0
+        return call
+
+
+def test_each_device_object_selects_its_own_device(monkeypatch):
+    fake = _FakeLib()
+    monkeypatch.setattr(launcher, "load_library", lambda: fake)
+    monkeypatch.setattr(launcher.Device, "_inited", {})
+    monkeypatch.setattr(launcher.Device, "_active", None)
+    d0 = launcher.Device.get(0)
+    d1 = launcher.Device.get(1)
+    d0.memset_d32(0x1000, 0, 4, 0)                # after d1 was selected: must switch back to 0
+    d1.memset_d32(0x2000, 0, 4, 0)
+    d1.sync()
+    d0.sync(0)
+    assert fake.calls == [("emmy_memset_d32_async", 0), ("emmy_memset_d32_async", 1),
+                          ("emmy_ctx_synchronize", 1), ("emmy_stream_synchronize", 0)]
+    assert launcher.Device.get(0) is d0 and fake.selected == 0
