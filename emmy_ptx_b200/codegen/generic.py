@@ -644,7 +644,7 @@ class KernelEmitter:
     def addr(base: str, imm: int) -> str:
         if imm == 0:
             return f"[{base}]"
-        return f"[{base}+{imm}]" if imm > 0 else f"[{base}{imm}]"
+        return f"[{base}+{imm}]"                     # a negative offset is written +-N
 
     def _base_align(self, buf: str, shared: bool) -> int:
         if shared:

@@ -453,6 +453,166 @@ def small_softmax(a=2, b=3, c=45):
     return _problem("softmax3d", f"softmax3d_{a}x{b}x{c}", "small_softmax", args, body, 1, a * b)
 
 
+def _int_op(name, identity):
+    """A reduce op over i32 with an explicit identity (the float table's infinities do not fit)."""
+    return {"kind": "ReduceOp", "name": name, "identity": identity, "has_identity": True}
+
+
+def row_argmax(rows=37, cols=333, thresh=2.0):
+    """idx[r] = argmax of row r (the first index holding the maximum) and cnt[r] = the number of
+    entries above ``thresh``, a warp per row of an odd length.  Pass 1 reduces the max (f32) and the
+    count (i32) in one two-state shuffle; pass 2 takes the smallest column whose value equals the max
+    (a Select feeding an i32 min accumulator), so ties resolve as torch.argmax does."""
+    body = [Tile([Axis("row", rows), Axis("t", 32)], [
+        StridedLoop("c", cols, V("t"), 32, [
+            Load(["x"], "x", [V("row"), V("c")], "f32"),
+            Accum("m", "maximum", "x"),
+            Assign("hi", "greater", ["x", Lit(thresh)], "bool"),
+            Select("one", [(V("hi"), 1), (None, 0)]),
+            {**Accum("n", "add", "one", "i32"), "op": _int_op("add", 0)},
+        ], end=cols),
+        WarpShuffle(["m", "n"], ["m_o", "n_o"], [Assign("m", "maximum", ["m", "m_o"]),
+                                                 Assign("n", "add", ["n", "n_o"], "i32")]),
+        StridedLoop("c2", cols, V("t"), 32, [
+            Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+            Assign("hit", "equal", ["x2", "m"], "bool"),
+            Select("cand", [(V("hit"), "c2"), (None, cols)]),
+            {**Accum("idx", "minimum", "cand", "i32"), "op": _int_op("minimum", 2 ** 31 - 1)},
+        ], end=cols),
+        WarpShuffle(["idx"], ["idx_o"], [Assign("idx", "minimum", ["idx", "idx_o"], "i32")]),
+        Cond(Bin("==", V("t"), 0), [Write("idx", ["idx"], [V("row")], "i32"),
+                                    Write("cnt", ["n"], [V("row")], "i32")]),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("idx", (rows,), "i32", output=True),
+            TensorSpec("cnt", (rows,), "i32", output=True)]
+    return _problem("argmax", f"argmax_{rows}x{cols}", "row_argmax", args, body, rows, 32, rtol=0.0, atol=0.0,
+                    thresh=thresh)
+
+
+def row_var_std(rows=4, cols=128):
+    """var[r] (unbiased, n - 1) and std[r] of each row, two passes: the mean, then the sum of squared
+    deviations; a warp per row, lanes striding the columns."""
+    body = [Tile([Axis("row", rows), Axis("t", 32)], [
+        StridedLoop("c", cols, V("t"), 32, [Load(["x"], "x", [V("row"), V("c")], "f32"), Accum("s", "add", "x")],
+                    end=cols),
+        WarpShuffle(["s"], ["s_o"], [Assign("s", "add", ["s", "s_o"])]),
+        Assign("mean", "divide", ["s", Lit(float(cols))]),
+        StridedLoop("c2", cols, V("t"), 32, [
+            Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+            Assign("d", "subtract", ["x2", "mean"]),
+            Assign("d2", "multiply", ["d", "d"]),
+            Accum("q", "add", "d2"),
+        ], end=cols),
+        WarpShuffle(["q"], ["q_o"], [Assign("q", "add", ["q", "q_o"])]),
+        Assign("var", "divide", ["q", Lit(float(cols - 1))]),
+        Assign("sd", "sqrt", ["var"]),
+        Cond(Bin("==", V("t"), 0), [Write("var", ["var"], [V("row")], "f32"), Write("std", ["sd"], [V("row")], "f32")]),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("var", (rows,), "f32", output=True),
+            TensorSpec("std", (rows,), "f32", output=True)]
+    return _problem("varstd", f"varstd_{rows}x{cols}", "row_var_std", args, body, rows, 32)
+
+
+def group_norm(n=1, c=4, h=8, w=16, groups=2, eps=1e-5, threads=64):
+    """group_norm(x, groups) without affine parameters: a block per (sample, group) reduces the
+    group's sum and sum of squares (two states), then normalises.  The group's flat element e maps
+    to x[s, g*cpg + e // (h*w), (e % (h*w)) // w, e % w]: integer division and remainder by
+    constants in the index."""
+    cpg = c // groups
+    hw = h * w
+    ne = cpg * hw
+    nw = threads // 32
+
+    def index(e):
+        return [V("s"), Bin("+", Bin("*", V("g"), cpg), Bin("/", V(e), hw)), Bin("/", Bin("%", V(e), hw), w),
+                Bin("%", V(e), w)]
+    body = [
+        Smem("red_s", [nw], "f32", 16),
+        Smem("red_q", [nw], "f32", 16),
+        Tile([Axis("s", n), Axis("g", groups), Axis("t", threads)], [
+            StridedLoop("e", ne, V("t"), threads, [
+                Load(["x"], "x", index("e"), "f32"),
+                Accum("sm", "add", "x"),
+                Assign("x2", "multiply", ["x", "x"]),
+                Accum("sq", "add", "x2"),
+            ], end=ne),
+            *_block_reduce(["sm", "sq"], ["red_s", "red_q"], {"sm": "add", "sq": "add"}, nw),
+            Assign("mean", "multiply", ["sm", Lit(1.0 / ne)]),
+            Assign("ex2", "multiply", ["sq", Lit(1.0 / ne)]),
+            Assign("mm", "multiply", ["mean", "mean"]),
+            Assign("var", "subtract", ["ex2", "mm"]),
+            Assign("ve", "add", ["var", Lit(eps)]),
+            Assign("rs", "rsqrt", ["ve"]),
+            StridedLoop("e2", ne, V("t"), threads, [
+                Load(["x3"], "x", index("e2"), "f32"),
+                Assign("dx", "subtract", ["x3", "mean"]),
+                Assign("y", "multiply", ["dx", "rs"]),
+                Write("y", ["y"], index("e2"), "f32"),
+            ], end=ne),
+        ]),
+    ]
+    args = [TensorSpec("x", (n, c, h, w), "f32", ("normal", 1.0)), TensorSpec("y", (n, c, h, w), "f32", output=True)]
+    return _problem("groupnorm", f"groupnorm_{n}x{c}x{h}x{w}_g{groups}", "group_norm", args, body, n * groups,
+                    threads, groups=groups, eps=eps)
+
+
+def pad_rows(rows=3, cols=64, left=2, right=3):
+    """y = pad(x, (left, right)) along the last axis: a cell inside the source range loads and copies
+    x[r, j - left], the others write zero (a Cond with an else branch around a guarded load)."""
+    out = cols + left + right
+    inside = Bin("&&", Bin(">=", V("j"), left), Bin("<", V("j"), left + cols))
+    body = [Tile([Axis("r", rows), Axis("j", out)], [
+        Cond(inside,
+             [Let("src", Bin("-", V("j"), left)), Load(["x"], "x", [V("r"), V("src")], "f32"),
+              Write("y", ["x"], [V("r"), V("j")], "f32")],
+             [Let("zero", Lit(0.0), "f32"), Write("y", ["zero"], [V("r"), V("j")], "f32")]),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("y", (rows, out), "f32", output=True)]
+    return _problem("pad", f"pad_{rows}x{cols}_{left}_{right}", "pad_rows", args, body, (rows * out + 63) // 64, 64,
+                    left=left, right=right)
+
+
+def log_sum_exp(a=2, b=32, c=64):
+    """logsumexp over the last axis, a warp per row of 64 (two columns a lane): the max, the sum of
+    exp(x - max), then max + log(sum)."""
+    body = [Tile([Axis("i", a), Axis("j", b), Axis("t", 32)], [
+        StridedLoop("k", c, V("t"), 32, [Load(["x"], "x", [V("i"), V("j"), V("k")], "f32"),
+                                         Accum("m", "maximum", "x")], end=c),
+        WarpShuffle(["m"], ["m_o"], [Assign("m", "maximum", ["m", "m_o"])]),
+        StridedLoop("k2", c, V("t"), 32, [
+            Load(["x2"], "x", [V("i"), V("j"), V("k2")], "f32"),
+            Assign("z", "subtract", ["x2", "m"]),
+            Assign("e", "exp", ["z"]),
+            Accum("s", "add", "e"),
+        ], end=c),
+        WarpShuffle(["s"], ["s_o"], [Assign("s", "add", ["s", "s_o"])]),
+        Assign("ls", "log", ["s"]),
+        Assign("y", "add", ["m", "ls"]),
+        Cond(Bin("==", V("t"), 0), [Write("y", ["y"], [V("i"), V("j")], "f32")]),
+    ])]
+    args = [TensorSpec("x", (a, b, c), "f32", ("normal", 1.0)), TensorSpec("y", (a, b), "f32", output=True)]
+    return _problem("logsumexp", f"logsumexp_{a}x{b}x{c}", "log_sum_exp", args, body, a * b * 32 // 128, 128)
+
+
+def matmul_odd(m=65, k=127, n=33):
+    """C = A @ B for odd sizes, a thread per output cell with a rolled Loop over k: the shape the
+    tensor-core lowering declines (no dimension is a multiple of its tile), so it stays on the CUDA
+    cores.  Held to the matmul tolerance."""
+    body = [Tile([Axis("i", m), Axis("j", n)], [
+        Loop("kk", k, [
+            Load(["a"], "A", [V("i"), V("kk")], "f32"),
+            Load(["b"], "B", [V("kk"), V("j")], "f32"),
+            Assign("p", "multiply", ["a", "b"]),
+            Accum("acc", "add", "p"),
+        ]),
+        Write("C", ["acc"], [V("i"), V("j")], "f32"),
+    ])]
+    args = [TensorSpec("A", (m, k), "f32", ("normal", 1.0)), TensorSpec("B", (k, n), "f32", ("normal", 1.0)),
+            TensorSpec("C", (m, n), "f32", output=True)]
+    return _problem("matmul", f"matmul_{m}x{k}x{n}", "matmul_odd", args, body, (m * n + 127) // 128, 128,
+                    rtol=1e-4, contraction=True)
+
+
 def _kernel_node(entry, inputs, outputs, body):
     return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
             "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
@@ -522,4 +682,10 @@ CORPUS = {
     "k_bcast3d": bcast3d,
     "k_minmax": row_minmax,
     "k_softmax3d": small_softmax,
+    "k_argmax": row_argmax,
+    "k_varstd": row_var_std,
+    "k_groupnorm": group_norm,
+    "k_pad": pad_rows,
+    "k_logsumexp": log_sum_exp,
+    "k_matmul_odd": matmul_odd,
 }

@@ -158,4 +158,11 @@ CORPUS = {
                                                            + t["bias"].double()[None, None, :])},
     "minmax": lambda t, p: {"mx": t["x"].double().amax(-1), "mn": t["x"].double().amin(-1)},
     "softmax3d": lambda t, p: {"y": __import__("torch").softmax(t["x"].double(), -1)},
+    "argmax": lambda t, p: {"idx": t["x"].double().argmax(-1), "cnt": (t["x"].double() > p["thresh"]).sum(-1)},
+    "varstd": lambda t, p: {"var": t["x"].double().var(-1), "std": t["x"].double().std(-1)},
+    "groupnorm": lambda t, p: {"y": __import__("torch").nn.functional.group_norm(t["x"].double(), p["groups"],
+                                                                                 eps=p["eps"])},
+    "pad": lambda t, p: {"y": __import__("torch").nn.functional.pad(t["x"].double(), (p["left"], p["right"]))},
+    "logsumexp": lambda t, p: {"y": __import__("torch").logsumexp(t["x"].double(), -1)},
+    "matmul": lambda t, p: {"C": t["A"].double() @ t["B"].double()},
 }
