@@ -119,6 +119,14 @@ def test_small_cuda_core_bmm_and_attention():
         _check(p, t, got, f"emu:{p.name}")
 
 
+def test_attention_the_tensor_core_lowering_declines():
+    # head dim 32 and 48 rows (not a multiple of the 256-row query tile pair): the attention pattern
+    # declines it with the default options, so the CUDA-core form runs (every record generic)
+    p = irgen.attention_ir(1, 1, 48, 32, True)
+    t, got = _run_ours(p)
+    _check(p, t, got, f"emu:{p.name}")
+
+
 def test_softmax_with_one_division_per_row():
     # the warp-per-row softmax with y = e * (1 / s): one IEEE division per row instead of per element
     p = irgen.softmax_ir(64, 1024, "warp", recip=True)
