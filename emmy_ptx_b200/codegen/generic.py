@@ -22,7 +22,7 @@ import math
 import os
 
 from ..ir import dim_int, dt_name, dt_bytes, IRError
-from .affine import Affine, Atom, reg_atom, div_const, rem_const, recombine, INT_MIN, INT_MAX
+from .affine import Affine, Atom, reg_atom, div_const, rem_const, recombine, INT_MAX
 from .ptx import PtxBuilder, f32_imm
 from . import mathlib
 

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import re
 
-from .ptxcheck import _instructions, _LABEL, _NO_DEST
+from .ptxcheck import _instructions, _NO_DEST
 
 _REG = re.compile(r"%(rd|r|f|p|h)(\d+)\b")
 # register-class prefixes as the PTX builder names them, longest first

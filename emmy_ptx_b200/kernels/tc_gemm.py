@@ -44,7 +44,7 @@ ERR_EPILOGUE = 4
 ERR_DRAIN = 5
 
 
-from .ptxasm import Asm, WAIT_LIMIT, WAIT_HINT_NS, idesc_f16, smem_desc_hi, wait_bar as _wait, wait_bar_warp as _wait_warp
+from .ptxasm import Asm, idesc_f16, smem_desc_hi, wait_bar as _wait, wait_bar_warp as _wait_warp
 
 
 def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,

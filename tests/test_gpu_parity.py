@@ -4,7 +4,6 @@ Every launch goes through the C ABI (``libemmy_launch.so``).  Small configuratio
 with the oracle interpreter element by element; the full benchmark sizes are checked against
 float64 / fp32 references of the source expression (exact for the integer sum).
 """
-import json
 from pathlib import Path
 
 import numpy as np
