@@ -613,6 +613,38 @@ def matmul_odd(m=65, k=127, n=33):
                     rtol=1e-4, contraction=True)
 
 
+def special_values(n=777):
+    """IEEE special values through the elementwise forms (the input holds NaN, +-inf, +0, 1e30 and a
+    small negative number at fixed positions, normal values elsewhere).  The results follow the PTX
+    instructions the reference emits: ``max.f32`` / ``min.f32`` return the non-NaN operand (relu of
+    NaN is 0), ``setp`` comparisons are ordered (NaN > 0 is false, and so is NaN != NaN), ``testp``
+    detects NaN; exp, log, sqrt and 1/x give IEEE's infinities and NaNs."""
+    outs = ["relu", "mn", "ex", "lg", "sq", "rc", "wh"]
+    body = [Tile([Axis("i", n)], [
+        Load(["x"], "x", [V("i")], "f32"),
+        Assign("relu", "maximum", ["x", Lit(0.0)]),
+        Assign("mn", "minimum", ["x", Lit(1.0)]),
+        Assign("ex", "exp", ["x"]),
+        Assign("lg", "log", ["x"]),
+        Assign("sq", "sqrt", ["x"]),
+        Assign("rc", "divide", [Lit(1.0), "x"]),
+        Assign("pos", "greater", ["x", Lit(0.0)], "bool"),
+        Assign("wh", "where", ["pos", "x", Lit(-1.0)]),
+        Assign("isn", "isnan", ["x"], "bool"),
+        Assign("ne", "not_equal", ["x", "x"], "bool"),
+        Assign("xb", "multiply", ["x", Lit(2.0)], "bf16"),
+        *[Write(o, [o], [V("i")], "f32") for o in outs],
+        Write("nanm", ["isn"], [V("i")], "u8"),
+        Write("nem", ["ne"], [V("i")], "u8"),
+        Write("xb", ["xb"], [V("i")], "bf16"),
+    ])]
+    args = [TensorSpec("x", (n,), "f32", ("special", 1.0)),
+            *[TensorSpec(o, (n,), "f32", output=True) for o in outs],
+            TensorSpec("nanm", (n,), "u8", output=True), TensorSpec("nem", (n,), "u8", output=True),
+            TensorSpec("xb", (n,), "bf16", output=True)]
+    return _problem("special", f"special_{n}", "special_values", args, body, (n + 127) // 128, 128)
+
+
 def _kernel_node(entry, inputs, outputs, body):
     return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
             "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
@@ -688,4 +720,5 @@ CORPUS = {
     "k_pad": pad_rows,
     "k_logsumexp": log_sum_exp,
     "k_matmul_odd": matmul_odd,
+    "k_special": special_values,
 }

@@ -6,6 +6,8 @@ see identical bits.  Outputs start as zeros.
 """
 from __future__ import annotations
 
+import math
+
 import numpy as np
 
 TORCH_DTYPE = {}
@@ -32,6 +34,15 @@ def make_tensor(spec, device="cpu", seed_offset: int = 0):
         t = torch.rand(shape, generator=g, dtype=torch.float32) * (hi - lo) + lo
     elif kind == "randint":
         t = torch.randint(int(spec.dist[1]), int(spec.dist[2]), shape, generator=g, dtype=torch.int32)
+    elif kind == "special":
+        # normal values with IEEE special and boundary values at fixed positions (flat index i):
+        # NaN, +inf, -inf, +0, a magnitude whose exp overflows, and a small negative number
+        t = torch.randn(shape, generator=g, dtype=torch.float32) * float(spec.dist[1])
+        flat = t.reshape(-1)
+        i = torch.arange(flat.numel())
+        for mod, rem, val in ((17, 3, math.nan), (23, 5, math.inf), (29, 7, -math.inf), (31, 11, 0.0),
+                              (37, 13, 1e30), (41, 17, -1e-3)):
+            flat[(i % mod) == rem] = val
     else:
         raise ValueError(f"unknown distribution {spec.dist!r}")
     t = t.to(torch_dtype(spec.dtype))

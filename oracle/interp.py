@@ -222,9 +222,20 @@ BINARY_I = {
     "left_shift": lambda a, b: _wrap(np.left_shift(np.asarray(a, np.int64), b)),
     "right_shift": lambda a, b: np.right_shift(np.asarray(a, np.int32), b),
 }
+def _not_equal(a, b):
+    """``setp.ne``: an ordered comparison, false when either float operand is NaN (the reference maps
+    not_equal and ``!=`` to ``ne``, compile.py:84 and 760), where numpy's ``!=`` is true."""
+    r = np.not_equal(a, b)
+    for x in (a, b):
+        x = np.asarray(x)
+        if x.dtype.kind == "f":
+            r = r & ~np.isnan(x)
+    return r
+
+
 COMPARE = {"greater": np.greater, "less": np.less, "greater_equal": np.greater_equal,
-           "less_equal": np.less_equal, "equal": np.equal, "not_equal": np.not_equal}
-EXPR_CMP = {"==": np.equal, "!=": np.not_equal, "<": np.less, "<=": np.less_equal,
+           "less_equal": np.less_equal, "equal": np.equal, "not_equal": _not_equal}
+EXPR_CMP = {"==": np.equal, "!=": _not_equal, "<": np.less, "<=": np.less_equal,
             ">": np.greater, ">=": np.greater_equal}
 EXPR_I = {"+": "add", "-": "subtract", "*": "multiply", "/": "divide", "%": "modulo",
           "&": "bitwise_and", "|": "bitwise_or", "^": "bitwise_xor", "<<": "left_shift",

@@ -135,7 +135,22 @@ def _exprs(t, p):
     return {"y": torch.where(~pa, e, tt)}
 
 
+def _special(t, p):
+    """The special-value kernel in float64, under the PTX rules the IR lowers to: max/min return the
+    non-NaN operand, comparisons with NaN are false (including NaN != NaN)."""
+    import torch
+    x = t["x"].double()
+    nan = torch.isnan(x)
+    return {"relu": torch.where(nan, torch.zeros_like(x), x.clamp_min(0.0)),
+            "mn": torch.where(nan, torch.ones_like(x), x.clamp_max(1.0)),
+            "ex": torch.exp(x), "lg": torch.log(x), "sq": torch.sqrt(x), "rc": 1.0 / x,
+            "wh": torch.where(x > 0, x, -torch.ones_like(x)),
+            "nanm": nan.to(torch.uint8), "nem": torch.zeros_like(x, dtype=torch.uint8),
+            "xb": x * 2.0}
+
+
 CORPUS = {
+    "special": _special,
     "rmsnorm": _rmsnorm,
     "layernorm": _layernorm,
     "logsoftmax": lambda t, p: {"y": __import__("torch").log_softmax(t["x"].double(), -1)},

@@ -53,8 +53,12 @@ def compare(got: torch.Tensor, ref: torch.Tensor, dtype: str, rtol: float, what:
         return {"max_abs": 0.0}
     g = g.double()
     r = r.double()
-    assert torch.isfinite(g).all() == torch.isfinite(r).all() or bool((torch.isfinite(g) == torch.isfinite(r)).all()), \
-        f"{what}: non-finite pattern differs"
+    # special values must match exactly: NaN where the reference has NaN, the same infinities
+    bad_nan = torch.isnan(g) != torch.isnan(r)
+    assert not bad_nan.any(), f"{what}: NaN at {int(bad_nan.sum())} positions differs, first {int(bad_nan.reshape(-1).nonzero()[0])}"
+    inf = torch.isinf(r)
+    bad_inf = (torch.isinf(g) != inf) | (inf & (g != r))
+    assert not bad_inf.any(), f"{what}: infinities differ at {int(bad_inf.sum())} positions"
     fin = torch.isfinite(r)
     err = (g - r).abs()
     err = torch.where(fin, err, torch.zeros_like(err))

@@ -577,6 +577,14 @@ class Emulator:
             d0, d1 = [r.strip() for r in ops[0].strip("{}").split(",")]
             regs[d0], regs[d1] = v & 0xFFFF, (v >> 16) & 0xFFFF
             return True
+        if op.startswith("testp.") and parts[-1] in ("f32", "f64"):
+            x = self._fv(parts[-1], val(ops[1]))
+            tiny = 2.0 ** -126 if parts[-1] == "f32" else 2.0 ** -1022
+            fin = math.isfinite(x)
+            regs[ops[0]] = {"finite": fin, "infinite": math.isinf(x), "number": not math.isnan(x),
+                            "notanumber": math.isnan(x), "normal": fin and abs(x) >= tiny,
+                            "subnormal": fin and 0 < abs(x) < tiny}[parts[1]]
+            return True
         if op.startswith("setp.") and parts[-1] in ("f32", "f64"):
             a_, b_ = self._fv(parts[-1], val(ops[1])), self._fv(parts[-1], val(ops[2]))
             cmp = parts[1]
