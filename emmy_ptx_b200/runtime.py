@@ -57,8 +57,7 @@ class Executable:
         for rec in compiled.kernels:
             for spec in rec.get("scratch", []):
                 if spec["name"] not in self.scratch:
-                    self.scratch[spec["name"]] = torch.empty(tuple(spec["shape"]), dtype=torch_dtype(spec["dtype"]),
-                                                             device=f"cuda:{self.index}")
+                    self.scratch[spec["name"]] = self._device_tensor(tuple(spec["shape"]), torch_dtype(spec["dtype"]))
         self.side = None
         names = [rec["entry"] for rec in compiled.kernels]
         for i, rec in enumerate(compiled.kernels):
@@ -71,7 +70,13 @@ class Executable:
             self._events = {rec["entry"]: self.dev.sync_event() for rec in compiled.kernels}
         self.err = None
         if any(spec.get("kind") == "errword" for rec in compiled.kernels for spec in rec.get("extra", [])):
-            self.err = torch.zeros(4, dtype=torch.int32, device=f"cuda:{self.index}")
+            self.err = self._device_tensor((4,), torch.int32)
+            self.err.zero_()
+
+    def _device_tensor(self, shape, dtype):
+        """Device memory the Executable owns (scratch between entries, the error word)."""
+        import torch
+        return torch.empty(shape, dtype=dtype, device=f"cuda:{self.index}")
 
     def error_code(self) -> int:
         """The error word a tensor-core kernel writes when one of its bounded waits times out
@@ -125,6 +130,8 @@ class Executable:
         g = grid or rec["grid"]
         if not g or not rec["block"]:
             raise ValueError(f"kernel {rec['entry']!r} has no launch geometry (no meta.json record)")
+        if 0 in list(g)[:3]:
+            return                   # an empty input: no blocks to run (CUDA refuses a zero-sized grid)
         if rec.get("tmaps") or rec.get("extra"):
             args = []
             keep = []

@@ -127,6 +127,18 @@ def test_attention_the_tensor_core_lowering_declines():
     _check(p, t, got, f"emu:{p.name}")
 
 
+@pytest.mark.parametrize("build,shape", [(corpus.col_sum, (0, 96)), (corpus.mid_sum, (2, 0, 32)),
+                                         (corpus.rmsnorm, (0, 512))], ids=["colsum-0rows", "midsum-0mid", "rmsnorm-0rows"])
+def test_empty_extents(build, shape):
+    # a reduction over an empty axis leaves its identity (0 for a sum, as torch's sum of nothing);
+    # a tile with no rows writes nothing
+    p = build(*shape)
+    t, got = _run_ours(p)
+    _check(p, t, got, f"emu:{p.name}")
+    for a in p.outputs:
+        assert not got[a.name].numel() or not got[a.name].any()
+
+
 def test_softmax_with_one_division_per_row():
     # the warp-per-row softmax with y = e * (1 / s): one IEEE division per row instead of per element
     p = irgen.softmax_ir(64, 1024, "warp", recip=True)
