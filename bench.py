@@ -261,7 +261,23 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host instead of CUDA graphs")
     ap.add_argument("--size", default="full", choices=["full", "small"],
                     help="small: a reduced instance of the same kernel (still larger than L2) for ncu captures")
+    ap.add_argument("--opt", action="append", default=[], metavar="KEY=VALUE",
+                    help="a compile option (value read as JSON when it parses), e.g. --opt attn_persistent=true")
     return ap.parse_args()
+
+
+def compile_options(pairs) -> dict:
+    """``--opt KEY=VALUE`` flags as the compiler's options dict."""
+    out = {}
+    for item in pairs:
+        key, sep, val = item.partition("=")
+        if not sep or not key:
+            raise SystemExit(f"--opt wants KEY=VALUE, got {item!r}")
+        try:
+            out[key] = json.loads(val)
+        except ValueError:
+            out[key] = val
+    return out
 
 
 def use_graphs(world: int, no_graph: bool) -> bool:
@@ -342,7 +358,8 @@ def main() -> int:
     scale = 1e9 if unit == "GB/s" else 1e12
     peaks, peak_src = load_peaks()
 
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    options = compile_options(args.opt)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), options)
     ex = Executable(mod, device=local)
     dev = ex.dev
     stream = torch.cuda.current_stream().cuda_stream
@@ -569,7 +586,7 @@ def main() -> int:
             "config": {"workload": key, "description": desc, "per_rank_units": units, "unit_kind": kind,
                        "parallelism": f"dp{world} ({'sharded + ncclAllReduce of the partial' if collective else 'sharded, no collective'})",
                        "l2": ("inputs exceed L2 (126 MB)" if rotate == 1 else f"{rotate} rotating buffer sets exceed 2x L2"),
-                       "grid": p.grid, "block": p.block},
+                       "grid": p.grid, "block": p.block, **({"compile_options": options} if options else {})},
             "gpu_launches": gpu_launches,
             "timing": ("CUDA graph replay of the K steps" if capture_steps(collective, args.no_graph, world)
                        else "host launches (kernel + ncclAllReduce per step)" if collective else "host launches"),

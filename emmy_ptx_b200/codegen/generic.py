@@ -493,6 +493,8 @@ class KernelEmitter:
     def fbin(self, op: str, x: str, y: str) -> Sym:
         ins = {"add": "add.f32", "subtract": "sub.f32", "multiply": "mul.f32", "divide": "div.rn.f32",
                "maximum": "max.f32", "minimum": "min.f32"}[op]
+        if op == "divide" and self.opts.get("fast_div"):
+            ins = "div.full.f32"       # option: the 2-ulp division instead of IEEE round-to-nearest
         r = self.b.reg("f32")
         if not x.startswith("%") and not y.startswith("%"):
             x = self.freg(x)
@@ -567,7 +569,7 @@ class KernelEmitter:
         fn = mathlib.UNARY.get(name) if len(xs) == 1 else mathlib.BINARY.get(name)
         if fn is None:
             raise Unsupported(f"unsupported elementwise op {name!r}")
-        return Sym("f32", op=fn(mathlib.Ops(self.b, self.freg), *xs))
+        return Sym("f32", op=fn(mathlib.Ops(self.b, self.freg, ftz=bool(self.opts.get("approx_ftz"))), *xs))
 
     # ---- indexing (compile.py:594-679) -----------------------------------------------------
     def linear(self, buf: str, index) -> Affine:

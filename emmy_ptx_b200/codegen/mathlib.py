@@ -22,15 +22,20 @@ COMPARISONS = {"greater": "gt", "less": "lt", "greater_equal": "ge", "less_equal
 class Ops:
     """Instruction helpers over a :class:`~.ptx.PtxBuilder` (first operands forced to registers)."""
 
-    def __init__(self, b, freg):
+    def __init__(self, b, freg, ftz: bool = False):
         self.b = b
         self.freg = freg
+        self.ftz = ftz          # option approx_ftz: ex2/lg2 flush subnormal inputs and results to zero
+
+    _FTZ = {"ex2.approx.f32": "ex2.approx.ftz.f32", "lg2.approx.f32": "lg2.approx.ftz.f32"}
 
     @staticmethod
     def c(v: float) -> str:
         return f32_imm(v)
 
     def un(self, ins: str, x: str) -> str:
+        if self.ftz:
+            ins = self._FTZ.get(ins, ins)
         r = self.b.reg("f32")
         self.b.emit(f"{ins} {r}, {self.freg(x)};")
         return r

@@ -139,6 +139,26 @@ def test_empty_extents(build, shape):
         assert not got[a.name].numel() or not got[a.name].any()
 
 
+@pytest.mark.parametrize("key", ["c1", "c1w", "k_logsoftmax", "k_mathzoo"])
+def test_fast_math_options_match_oracle(key, tmp_path):
+    # opt-in approx_ftz (ex2/lg2 flush subnormals) and fast_div (div.full, 2 ulp): within the
+    # tolerances on normal data; the PTX must still assemble
+    import shutil
+    import subprocess
+    p = _problem(key)
+    opts = {"approx_ftz": True, "fast_div": True}
+    t, got = _run_ours(p, opts)
+    _check(p, t, got, f"emu-fast:{key}")
+    ptx = compile_graph(Graph.from_dict(p.graph), p.meta(), opts).ptx
+    assert "ex2.approx.ftz.f32" in ptx or "lg2.approx.ftz.f32" in ptx
+    src = tmp_path / "k.ptx"
+    src.write_text(ptx)
+    ptxas = shutil.which("ptxas") or "/usr/local/cuda/bin/ptxas"
+    r = subprocess.run([ptxas, "-arch=sm_100a", str(src), "-o", str(tmp_path / "k.cubin")], capture_output=True,
+                       text=True)
+    assert r.returncode == 0, r.stderr
+
+
 def test_softmax_with_one_division_per_row():
     # the warp-per-row softmax with y = e * (1 / s): one IEEE division per row instead of per element
     p = irgen.softmax_ir(64, 1024, "warp", recip=True)

@@ -115,3 +115,11 @@ def test_nccl_steps_are_never_captured_in_a_graph():
     assert bench.use_graphs(world=2, no_graph=False) is False
     assert bench.capture_steps(collective=False, no_graph=False, world=8) is False
     assert bench.use_graphs(world=1, no_graph=False) is True
+
+
+def test_bench_compile_options_parse():
+    import bench
+    assert bench.compile_options(["attn_persistent=true", "sms=148", "name=x"]) == {
+        "attn_persistent": True, "sms": 148, "name": "x"}
+    with pytest.raises(SystemExit):
+        bench.compile_options(["novalue"])
