@@ -463,7 +463,7 @@ class Emulator:
         if x.label:
             return (0,)
         op = x.op
-        if op.startswith(("mbarrier.", "tcgen05.", "cp.async.bulk", "prmt.", "max.u16x2", "min.u16x2")) or (
+        if op.startswith(("mbarrier.", "tcgen05.", "cp.async.bulk", "prmt.", "lop3.", "max.u16x2", "min.u16x2")) or (
                 ".f32x2" in op) or (op.startswith(("bar.arrive", "bar.red")) or (
                 op.startswith(("bar.sync", "barrier.sync")) and len(x.ops) == 2)):
             return (7,)

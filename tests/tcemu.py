@@ -203,6 +203,15 @@ class TcEmulator(Emulator):
             src = (a_ | (b_ << 32)).to_bytes(8, "little")
             regs[ops[0]] = int.from_bytes(bytes(src[(sel >> (4 * i)) & 7] for i in range(4)), "little")
             return "cont"
+        if op.startswith("lop3.b32"):
+            # d = LUT(a, b, c) bitwise: bit i of the immediate is the result for (a, b, c) = bits of i
+            a_, b_, c_, lut = (val(o) & _M32 for o in ops[1:5])
+            r = 0
+            for i in range(8):
+                if lut >> i & 1:
+                    r |= ((a_ if i & 4 else ~a_) & (b_ if i & 2 else ~b_) & (c_ if i & 1 else ~c_)) & _M32
+            regs[ops[0]] = r
+            return "cont"
         if op.startswith("max.u16x2") or op.startswith("min.u16x2"):
             a_, b_ = val(ops[1]) & _M32, val(ops[2]) & _M32
             f = max if op.startswith("max") else min

@@ -78,8 +78,13 @@ def _causal():
     ("c5tcnc", {"attn_prefetch_next": 1}),
     ("c5tcnc", {"attn_pack_in_turn": True}),
     ("c5tc", {"attn_persistent": True, "sms": 2}),        # 4 units over 2 CTAs: each walks a long and a short one
+    ("c5tcnc", {"attn_pack_after_turn": True}),
+    ("c5tcnc", {"attn_pack_after_turn": True, "attn_defer_sum": True}),
+    ("c5tcnc", {"attn_poly": 8}),
+    ("c5tcnc", {"attn_f16_int": 4}),
 ], ids=["nc", "nc-bf16", "nc-noturns", "causal", "causal-persistent", "nc-persistent", "nc-prefetch",
-        "nc-pack-in-turn", "causal-persistent-2ctas"])
+        "nc-pack-in-turn", "causal-persistent-2ctas", "nc-pack-after-turn", "nc-defer-sum", "nc-poly8",
+        "nc-f16-int4"])
 def test_attention_emulated_matches_oracle(key, opts):
     p = _causal() if key == "causal" else irgen.SMALL[key]()
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
