@@ -178,14 +178,24 @@ ATTN_VARIANTS = {
 }
 
 
+_ORACLE_CACHE: dict = {}
+
+
+def _small_with_oracle(key):
+    """A small configuration's inputs and oracle outputs, computed once per key."""
+    if key not in _ORACLE_CACHE:
+        p = irgen.SMALL[key]()
+        t = data.make_inputs(p)
+        _ORACLE_CACHE[key] = (p, t, oracle_outputs(p, t))
+    return _ORACLE_CACHE[key]
+
+
 @pytest.mark.parametrize("key", ["c5tc", "c5tcnc"])
 @pytest.mark.parametrize("variant", sorted(ATTN_VARIANTS))
 def test_attention_variants_match_oracle(key, variant):
     """The opt-in attention variants (measured against the default for speed) give the default's
     results: each against the oracle on the small causal and non-causal configurations."""
-    p = irgen.SMALL[key]()
-    t = data.make_inputs(p)
-    want = oracle_outputs(p, t)
+    p, t, want = _small_with_oracle(key)
     got, ex = _run_ours(p, t, **ATTN_VARIANTS[variant])
     assert ex.records[-1]["kind"] == "tcgen05_attention"
     assert ex.error_code() == 0
