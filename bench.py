@@ -48,12 +48,12 @@ CONFIGS = {
 def _small_for_profile():
     from emmy_ptx_b200 import irgen
     return {
-        "c1": lambda: irgen.softmax_ir(4096, 1024),
-        "c2": lambda: irgen.sum_ir(1 << 26, "f32"),
-        "c2i": lambda: irgen.sum_ir(1 << 26, "i32"),
-        "c3": lambda: irgen.fused_ir(4096, 8192),
-        "c4": lambda: irgen.bmm_ir(2, 4096, 4096, 4096),
-        "c5": lambda: irgen.attention_ir(2, 16, 4096, 128),
+        "c1": lambda **kw: irgen.softmax_ir(4096, 1024, **kw),
+        "c2": lambda **kw: irgen.sum_ir(1 << 26, "f32", **kw),
+        "c2i": lambda **kw: irgen.sum_ir(1 << 26, "i32", **kw),
+        "c3": lambda **kw: irgen.fused_ir(4096, 8192, **kw),
+        "c4": lambda **kw: irgen.bmm_ir(2, 4096, 4096, 4096, **kw),
+        "c5": lambda **kw: irgen.attention_ir(2, 16, 4096, 128, **kw),
     }
 
 
@@ -178,12 +178,12 @@ class ClockSampler:
 
 def _oracle_worker(args):
     """Interpret a block range of the problem's kernel; returns the output arrays (spawned process)."""
-    key, files, block_lo, block_hi = args
+    key, ir_kw, files, block_lo, block_hi = args
     import numpy as np
     from emmy_ptx_b200 import irgen
     from emmy_ptx_b200.ir import Graph
     from oracle.interp import Interpreter, storage_dtype
-    p = irgen.FULL[key]()
+    p = irgen.FULL[key](**ir_kw)
     bufs = {}
     for a in p.args:
         n = 1
@@ -200,12 +200,13 @@ def _oracle_worker(args):
 class OraclePool:
     """The oracle over a bounded sample of the workload, on ``workers`` spawned processes."""
 
-    def __init__(self, key: str, tensors: dict, workers: int, sample_blocks: int):
+    def __init__(self, key: str, tensors: dict, workers: int, sample_blocks: int, ir_kw: dict | None = None):
         import multiprocessing as mp
         from emmy_ptx_b200 import irgen
         from emmy_ptx_b200.data import to_numpy_storage
         self.key = key
-        self.p = irgen.FULL[key]()
+        self.ir_kw = dict(ir_kw or {})
+        self.p = irgen.FULL[key](**self.ir_kw)
         # inputs shared with the workers as read-only memory-mapped files (page cache, not /dev/shm)
         self.dir = tempfile.TemporaryDirectory(prefix="emmy_oracle_")
         self.files = {}
@@ -221,7 +222,7 @@ class OraclePool:
         n = self.sample_blocks
         w = max(1, min(self.workers, n))
         edges = [n * i // w for i in range(w + 1)]
-        return [(self.key, self.files, edges[i], edges[i + 1]) for i in range(w)]
+        return [(self.key, self.ir_kw, self.files, edges[i], edges[i + 1]) for i in range(w)]
 
     def step(self):
         if self.pool is None:
@@ -263,6 +264,8 @@ def parse():
                     help="small: a reduced instance of the same kernel (still larger than L2) for ncu captures")
     ap.add_argument("--opt", action="append", default=[], metavar="KEY=VALUE",
                     help="a compile option (value read as JSON when it parses), e.g. --opt attn_persistent=true")
+    ap.add_argument("--ir", action="append", default=[], metavar="KEY=VALUE",
+                    help="an argument of the workload's IR builder, e.g. --ir recip=true for config 1")
     return ap.parse_args()
 
 
@@ -352,7 +355,8 @@ def main() -> int:
     dist = edist.init(world, local)
     max_over_ranks = edist.max_over_ranks
     key = args.config
-    p = (SMALL_FOR_PROFILE[key] if args.size == "small" else irgen.FULL[key])()
+    ir_kw = compile_options(args.ir)
+    p = (SMALL_FOR_PROFILE[key] if args.size == "small" else irgen.FULL[key])(**ir_kw)
     units, kind = work_units(p)
     desc, metric, unit = CONFIGS[key]
     scale = 1e9 if unit == "GB/s" else 1e12
@@ -566,7 +570,7 @@ def main() -> int:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tc = {a.name: sets[0][a.name].cpu() for a in p.args}
         blocks = sample_blocks_for(key, p, 1)
-        pool = OraclePool(key, tc, 1, blocks)
+        pool = OraclePool(key, tc, 1, blocks, ir_kw)
         t0 = time.perf_counter()
         pool.step()
         dt = time.perf_counter() - t0
@@ -586,7 +590,8 @@ def main() -> int:
             "config": {"workload": key, "description": desc, "per_rank_units": units, "unit_kind": kind,
                        "parallelism": f"dp{world} ({'sharded + ncclAllReduce of the partial' if collective else 'sharded, no collective'})",
                        "l2": ("inputs exceed L2 (126 MB)" if rotate == 1 else f"{rotate} rotating buffer sets exceed 2x L2"),
-                       "grid": p.grid, "block": p.block, **({"compile_options": options} if options else {})},
+                       "grid": p.grid, "block": p.block, **({"compile_options": options} if options else {}),
+                       **({"ir_options": ir_kw} if ir_kw else {})},
             "gpu_launches": gpu_launches,
             "timing": ("CUDA graph replay of the K steps" if capture_steps(collective, args.no_graph, world)
                        else "host launches (kernel + ncclAllReduce per step)" if collective else "host launches"),

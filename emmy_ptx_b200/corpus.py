@@ -594,7 +594,7 @@ def log_sum_exp(a=2, b=32, c=64):
     return _problem("logsumexp", f"logsumexp_{a}x{b}x{c}", "log_sum_exp", args, body, a * b * 32 // 128, 128)
 
 
-def matmul_odd(m=65, k=127, n=33):
+def matmul_odd(m=33, k=65, n=17):
     """C = A @ B for odd sizes, a thread per output cell with a rolled Loop over k: the shape the
     tensor-core lowering declines (no dimension is a multiple of its tile), so it stays on the CUDA
     cores.  Held to the matmul tolerance."""

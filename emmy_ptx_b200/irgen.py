@@ -577,13 +577,13 @@ def attention_ir(batch: int = 8, heads: int = 32, seq: int = 4096, dim: int = 12
 
 
 #: The five BASELINE configurations at full size.
-FULL = {
-    "c1": lambda: softmax_ir(4096, 1024),
-    "c2": lambda: sum_ir(1 << 28, "f32"),
-    "c2i": lambda: sum_ir(1 << 28, "i32"),
-    "c3": lambda: fused_ir(8192, 8192),
-    "c4": lambda: bmm_ir(16, 4096, 4096, 4096),
-    "c5": lambda: attention_ir(8, 32, 4096, 128),
+FULL = {          # keyword arguments pass through to the builder (e.g. softmax_ir's recip)
+    "c1": lambda **kw: softmax_ir(4096, 1024, **kw),
+    "c2": lambda **kw: sum_ir(1 << 28, "f32", **kw),
+    "c2i": lambda **kw: sum_ir(1 << 28, "i32", **kw),
+    "c3": lambda **kw: fused_ir(8192, 8192, **kw),
+    "c4": lambda **kw: bmm_ir(16, 4096, 4096, 4096, **kw),
+    "c5": lambda **kw: attention_ir(8, 32, 4096, 128, **kw),
 }
 
 #: Small instances of the same kernels, sized so the CPU oracle finishes in seconds.

@@ -25,20 +25,20 @@
 	mad.lo.s32 %r4, %r2, %r3, %r1;
 	and.b32 %r5, %r1, 31;
 	shr.u32 %r6, %r1, 5;
-	setp.lt.s32 %p1, %r4, 2145;
+	setp.lt.s32 %p1, %r4, 561;
 	@!%p1 bra L1_end;
-	div.s32 %r7, %r4, 33;
-	mul.lo.s32 %r8, %r7, 33;
+	div.s32 %r7, %r4, 17;
+	mul.lo.s32 %r8, %r7, 17;
 	sub.s32 %r9, %r4, %r8;
 	mov.b32 %f1, 0f00000000;
 	mov.s32 %r10, 0;
 L3_top:
-	setp.ge.s32 %p2, %r10, 127;
+	setp.ge.s32 %p2, %r10, 65;
 	@%p2 bra L2_lend;
-	mad.lo.s32 %r12, %r7, 127, %r10;
+	mad.lo.s32 %r12, %r7, 65, %r10;
 	mad.wide.s32 %rd4, %r12, 4, %rd1;
 	ld.global.f32 %f2, [%rd4];
-	mad.lo.s32 %r14, %r10, 33, %r9;
+	mad.lo.s32 %r14, %r10, 17, %r9;
 	mad.wide.s32 %rd5, %r14, 4, %rd2;
 	ld.global.f32 %f3, [%rd5];
 	mul.f32 %f4, %f2, %f3;
@@ -46,7 +46,7 @@ L3_top:
 	add.s32 %r10, %r10, 1;
 	bra L3_top;
 L2_lend:
-	mad.lo.s32 %r16, %r7, 33, %r9;
+	mad.lo.s32 %r16, %r7, 17, %r9;
 	mad.wide.s32 %rd6, %r16, 4, %rd3;
 	st.global.f32 [%rd6], %f1;
 L1_end:

@@ -123,3 +123,25 @@ def test_bench_compile_options_parse():
         "attn_persistent": True, "sms": 148, "name": "x"}
     with pytest.raises(SystemExit):
         bench.compile_options(["novalue"])
+
+
+def test_bench_reference_arm_runs_on_the_host():
+    # the reference arm (the oracle port on host cores) needs no GPU: one line from rank 0, with the
+    # contract's keys; another rank of a multi-GPU launch prints nothing and exits 0
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    cmd = [sys.executable, str(root / "bench.py"), "--impl", "reference", "--config", "c1", "--steps", "1",
+           "--warmup", "0"]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["h2d_bytes_per_step"] == 0
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300,
+                       env={**env, "RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
+    assert r.returncode == 0 and not r.stdout.strip()
