@@ -502,7 +502,7 @@ def bmm_ir(batch: int = 16, m: int = 4096, n: int = 4096, k: int = 4096) -> Prob
 
 
 def attention_ir(batch: int = 8, heads: int = 32, seq: int = 4096, dim: int = 128,
-                 causal: bool = True) -> Problem:
+                 causal: bool = True, scale: float | None = None) -> Problem:
     """O = softmax(Q K^T / sqrt(D) + causal mask) V, bf16 in and out, f32 math.
 
     One warp per query row; each lane holds D/32 contiguous dims.  Scores come from a lane dot
@@ -513,7 +513,7 @@ def attention_ir(batch: int = 8, heads: int = 32, seq: int = 4096, dim: int = 12
         raise ValueError("attention_ir needs dim in {32, 64, 128, 256}")
     per = dim // 32
     P = range(per)
-    scale = 1.0 / math.sqrt(dim)
+    scale = 1.0 / math.sqrt(dim) if scale is None else float(scale)
     qs = [f"q{i}" for i in P]
     ks = [f"k{i}" for i in P]
     vs = [f"v{i}" for i in P]

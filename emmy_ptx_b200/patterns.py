@@ -16,12 +16,40 @@ structural and fails closed — anything not recognised exactly is left to the C
   seeded with 0; every Write goes to the output and writes only accumulators; nothing else is
   written to global memory;
 * the tile sizes divide the shapes (M % 128, N % 256, K % 64).
+
+Those checks find the operands, shapes and (for attention) the mask and scale.  The final gate is
+stricter: the kernel body must equal, up to the buffer names, the canonical CUDA-core nest for those
+parameters (:func:`.irgen.bmm_ir`, :func:`.irgen.attention_ir`).  A structural check alone let a
+store to C[b, j, i] or two swapped accumulators through; with the equality gate no variation of the
+nest can reach a tensor-core kernel that computes something else, and every other form runs, correctly,
+on the CUDA cores.
 """
 from __future__ import annotations
 
 import os
 
-from .ir import dt_name, walk
+from .ir import Graph, dt_name, walk
+
+
+def _body_data(node, rename=None) -> list:
+    """The kernel body as plain data, with every string equal to a key of ``rename`` mapped."""
+    def ren(v):
+        if isinstance(v, str):
+            return rename.get(v, v)
+        if isinstance(v, list):
+            return [ren(x) for x in v]
+        if isinstance(v, dict):
+            return {k: ren(x) for k, x in v.items()}
+        return v
+    data = [st.to_dict() for st in node.op.body]
+    return ren(data) if rename else data
+
+
+def is_canonical(node, template, rename: dict) -> bool:
+    """True when ``node``'s body, its buffers renamed by ``rename``, equals the body of the single
+    kernel of ``template`` (a problem from :mod:`.irgen`)."""
+    tnode = Graph.from_dict(template.graph).kernels()[0]
+    return _body_data(node, rename) == _body_data(tnode)
 
 
 def _names_in(e, out: set) -> set:
@@ -157,6 +185,9 @@ def match_bmm(graph, node):
                 return None
         if cls == "ZeroPrologue":
             return None
+    from .irgen import bmm_ir
+    if not is_canonical(node, bmm_ir(bt, m, n, k), {X.name: "A", Y.name: "B", C.name: "C"}):
+        return None
     return X, Y, C, bt, m, n, k
 
 
@@ -304,6 +335,10 @@ def match_attention(graph, node):
             return None
     K = vals[kname]
     V = vals[vname]
+    from .irgen import attention_ir
+    if not is_canonical(node, attention_ir(bt, hd, seq, dim, causal, scale=scale),
+                        {Q.name: "Q", K.name: "K", V.name: "V", O.name: "O"}):
+        return None
     return Q, K, V, O, bt, hd, seq, dim, causal, scale
 
 

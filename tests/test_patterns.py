@@ -1,5 +1,6 @@
 """The dense-contraction matcher: what it accepts and what it must refuse (CPU only)."""
 import copy
+import json
 
 from emmy_ptx_b200 import irgen
 from emmy_ptx_b200.compiler import compile_graph
@@ -116,3 +117,80 @@ def test_attention_with_a_different_mask_is_refused():
 def test_small_head_dim_stays_on_cuda_cores():
     p = irgen.SMALL["c5nc"]()                 # D = 64: not the 128-wide tensor-core tile
     assert compile_graph(Graph.from_dict(p.graph), p.meta()).kernels[0]["kind"] == "generic"
+
+
+def _mutated(p, entry, edit):
+    d = copy.deepcopy(p.graph)
+
+    def visit(stmts):
+        for st in stmts:
+            edit(st)
+            for key in ("body", "else_body"):
+                if isinstance(st.get(key), list):
+                    visit(st[key])
+    visit(d["nodes"][entry]["op_fields"]["body"])
+    g = Graph.from_dict(d)
+    return g, g.kernels()[0]
+
+
+def _swap_first_write_values():
+    done = []
+
+    def edit(st):
+        if st.get("kind") == "Write" and not done:
+            st["values"][0], st["values"][1] = st["values"][1], st["values"][0]
+            done.append(st)
+    return edit
+
+
+def test_bmm_near_misses_are_refused():
+    # each of these passed the structural checks alone: a store to C[b, j, i] and two accumulators
+    # written to each other's places would have produced a wrong C from the tensor-core kernel
+    p = irgen.SMALL["c4tc"]()
+
+    def transpose_store(st):
+        if st.get("kind") == "Write":
+            st["index"][1], st["index"][2] = st["index"][2], st["index"][1]
+    for edit in (transpose_store, _swap_first_write_values()):
+        g, k = _mutated(p, "bmm_bf16", edit)
+        assert match_bmm(g, k) is None, edit.__name__
+        assert compile_graph(g, p.meta()).kernels[0]["kind"] == "generic"
+
+
+def test_attention_near_misses_are_refused():
+    p = irgen.SMALL["c5tc"]()
+
+    def shared_kv_head(st):                       # K[b, 0, kv, d]: every head reads head 0's keys
+        if st.get("kind") == "Load" and st.get("input") == "K":
+            st["index"][1] = {"kind": "Literal", "value": 0, "dtype": "i32"}
+
+    def v_transposed(st):                         # V[b, h, d, kv]
+        if st.get("kind") == "Load" and st.get("input") == "V":
+            st["index"][2], st["index"][3] = st["index"][3], st["index"][2]
+    for edit in (shared_kv_head, v_transposed, _swap_first_write_values()):
+        g, k = _mutated(p, "attention_causal", edit)
+        assert match_attention(g, k) is None, edit.__name__
+        assert [r["kind"] for r in compile_graph(g, p.meta()).kernels] == ["generic"], edit.__name__
+
+
+def test_attention_with_another_scale_is_lowered_with_it():
+    # the softmax scale is a kernel parameter: a nest with another scale literal is still the
+    # canonical nest for that scale
+    p = irgen.SMALL["c5tc"]()
+
+    def other_scale(st):
+        if st.get("kind") == "Assign" and st.get("name") == "sc":
+            st["args"][1]["value"] = 0.1
+    g, k = _mutated(p, "attention_causal", other_scale)
+    hit = match_attention(g, k)
+    assert hit is not None and abs(hit[-1] - 0.1) < 1e-9
+
+
+def test_renamed_buffers_still_match():
+    # the equality gate compares bodies up to the buffer names
+    p = irgen.SMALL["c4tc"]()
+    d = copy.deepcopy(p.graph)
+    blob = json.dumps(d).replace('"A"', '"lhs"').replace('"B"', '"rhs"').replace('"C"', '"out"')
+    g = Graph.from_dict(json.loads(blob))
+    hit = match_bmm(g, g.kernels()[0])
+    assert hit is not None and (hit[0].name, hit[1].name, hit[2].name) == ("lhs", "rhs", "out")
