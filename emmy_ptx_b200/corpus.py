@@ -230,8 +230,9 @@ def cumsum_1d(n=128):
 
 
 def int_ops(n=1000):
-    """Integer elementwise work with a two-way and a three-way Select (first true branch wins);
-    division and remainder truncate toward zero as in C."""
+    """Integer elementwise work with a two-way and two three-way Selects, one of them with overlapping
+    predicates (x > 10 and x > 0 are both true above 10: the first true branch wins); division and
+    remainder truncate toward zero as in C."""
     body = [Tile([Axis("i", n)], [
         Load(["x"], "x", [V("i")], "i32"),
         Load(["y"], "y", [V("i")], "i32"),
@@ -241,6 +242,7 @@ def int_ops(n=1000):
         Assign("gt", "greater", ["x", 4], "bool"),
         Select("z", [(V("gt"), "a"), (None, "o3")]),
         Select("sg", [(Bin("<", V("x"), 0), -1), (Bin("==", V("x"), 0), 0), (None, 1)]),
+        Select("bd", [(Bin(">", V("x"), 10), 2), (Bin(">", V("x"), 0), 1), (None, 0)]),
         Assign("q", "divide", ["x", 3], "i32"),
         Assign("r", "modulo", ["x", 3], "i32"),
         Assign("sh", "left_shift", ["y", 2], "i32"),
@@ -249,10 +251,11 @@ def int_ops(n=1000):
         Write("z", ["z"], [V("i")], "i32"),
         Write("s", ["sg"], [V("i")], "i32"),
         Write("w", ["w"], [V("i")], "i32"),
+        Write("bd", ["bd"], [V("i")], "i32"),
     ])]
     args = [TensorSpec("x", (n,), "i32", ("randint", -20, 21)), TensorSpec("y", (n,), "i32", ("randint", 0, 9)),
             TensorSpec("z", (n,), "i32", output=True), TensorSpec("s", (n,), "i32", output=True),
-            TensorSpec("w", (n,), "i32", output=True)]
+            TensorSpec("w", (n,), "i32", output=True), TensorSpec("bd", (n,), "i32", output=True)]
     return _problem("intops", f"intops_{n}", "int_ops", args, body, (n + 127) // 128, 128, rtol=0.0, atol=0.0)
 
 

@@ -83,7 +83,8 @@ def _intops(t, p):
     x, y = t["x"].long(), t["y"].long()
     q = torch.div(x, 3, rounding_mode="trunc")
     r = x - q * 3
-    return {"z": torch.where(x > 4, x & y, (x | y) - 3), "s": torch.sign(x), "w": torch.maximum(q, r) + (y << 2)}
+    return {"z": torch.where(x > 4, x & y, (x | y) - 3), "s": torch.sign(x), "w": torch.maximum(q, r) + (y << 2),
+            "bd": torch.where(x > 10, 2, torch.where(x > 0, 1, 0))}
 
 
 def _mathzoo(t, p):
