@@ -616,6 +616,28 @@ def matmul_odd(m=33, k=65, n=17):
                     rtol=1e-4, contraction=True)
 
 
+def scan_max_and_prod(rows=4, cols=64):
+    """cm[r, c] = max of x[r, :c+1] (a running max: a thread per row, the Accum read after each step
+    of a rolled Loop) and pr[r] = prod of x[r, :] (a warp per row: Accum multiply, then a shuffle
+    whose combine is a product, which has no redux form)."""
+    body = [Tile([Axis("row", rows), Axis("t", 32)], [
+        Cond(Bin("==", V("t"), 0), [
+            Loop("c", cols, [
+                Load(["x"], "x", [V("row"), V("c")], "f32"),
+                Accum("cm", "maximum", "x"),
+                Write("cm", ["cm"], [V("row"), V("c")], "f32"),
+            ]),
+        ]),
+        StridedLoop("c2", cols, V("t"), 32, [Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+                                             Accum("pr", "multiply", "x2")], end=cols),
+        WarpShuffle(["pr"], ["pr_o"], [Assign("pr", "multiply", ["pr", "pr_o"])]),
+        Cond(Bin("==", V("t"), 0), [Write("pr", ["pr"], [V("row")], "f32")]),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("uniform", 0.5, 1.5)),
+            TensorSpec("cm", (rows, cols), "f32", output=True), TensorSpec("pr", (rows,), "f32", output=True)]
+    return _problem("scanprod", f"scanprod_{rows}x{cols}", "scan_max_prod", args, body, rows, 32)
+
+
 def special_values(n=777):
     """IEEE special values through the elementwise forms (the input holds NaN, +-inf, +0, 1e30 and a
     small negative number at fixed positions, normal values elsewhere).  The results follow the PTX
@@ -724,4 +746,5 @@ CORPUS = {
     "k_logsumexp": log_sum_exp,
     "k_matmul_odd": matmul_odd,
     "k_special": special_values,
+    "k_scanprod": scan_max_and_prod,
 }
