@@ -670,6 +670,27 @@ def special_values(n=777):
     return _problem("special", f"special_{n}", "special_values", args, body, (n + 127) // 128, 128)
 
 
+def special_values_16bit(n=640):
+    """The special values through 16-bit loads and stores: bf16 and f16 inputs holding NaN, +-inf
+    and +0 (the 1e30 of the f32 pattern is already inf in f16) are widened to f32 (bf16 by a shift of
+    the packed word, f16 by ``cvt``), go through max / multiply / isnan, and are narrowed back."""
+    body = [Tile([Axis("i8", n // 8)], [
+        Let("i", Bin("*", V("i8"), 8)),
+        Load([f"b{k}" for k in range(8)], "xb", [V("i")], "bf16"),
+        Load([f"h{k}" for k in range(8)], "xh", [V("i")], "f16"),
+        *[Assign(f"rb{k}", "maximum", [f"b{k}", Lit(0.0)], "bf16") for k in range(8)],
+        *[Assign(f"dh{k}", "multiply", [f"h{k}", Lit(2.0)], "f16") for k in range(8)],
+        *[Assign(f"nb{k}", "isnan", [f"b{k}"], "bool") for k in range(8)],
+        Write("yb", [f"rb{k}" for k in range(8)], [V("i")], "bf16"),
+        Write("yh", [f"dh{k}" for k in range(8)], [V("i")], "f16"),
+        *[Write("nanb", [f"nb{k}"], [Bin("+", V("i"), k)], "u8") for k in range(8)],
+    ])]
+    args = [TensorSpec("xb", (n,), "bf16", ("special", 1.0)), TensorSpec("xh", (n,), "f16", ("special", 1.0)),
+            TensorSpec("yb", (n,), "bf16", output=True), TensorSpec("yh", (n,), "f16", output=True),
+            TensorSpec("nanb", (n,), "u8", output=True)]
+    return _problem("special16", f"special16_{n}", "special_values_16bit", args, body, (n // 8 + 63) // 64, 64)
+
+
 def _kernel_node(entry, inputs, outputs, body):
     return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
             "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
@@ -747,4 +768,5 @@ CORPUS = {
     "k_matmul_odd": matmul_odd,
     "k_special": special_values,
     "k_scanprod": scan_max_and_prod,
+    "k_special16": special_values_16bit,
 }

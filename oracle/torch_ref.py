@@ -150,8 +150,18 @@ def _special(t, p):
             "xb": x * 2.0}
 
 
+def _special16(t, p):
+    """The 16-bit special-value kernel in float64 (max returns the non-NaN operand)."""
+    import torch
+    xb, xh = t["xb"].double(), t["xh"].double()
+    nan = torch.isnan(xb)
+    return {"yb": torch.where(nan, torch.zeros_like(xb), xb.clamp_min(0.0)), "yh": xh * 2.0,
+            "nanb": nan.to(torch.uint8)}
+
+
 CORPUS = {
     "special": _special,
+    "special16": _special16,
     "rmsnorm": _rmsnorm,
     "layernorm": _layernorm,
     "logsoftmax": lambda t, p: {"y": __import__("torch").log_softmax(t["x"].double(), -1)},
