@@ -8,3 +8,5 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); run with -m gpu")
+    config.addinivalue_line("markers", "gpu_optin: opt-in variants not yet run on a B200 (skipped without a "
+                                       "GPU); run with -m gpu_optin")

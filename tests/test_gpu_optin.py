@@ -1,0 +1,73 @@
+"""GPU tests of the opt-in variants that have not yet run on a B200 (marker ``gpu_optin``).
+
+These kernels are not on the default path: the persistent attention schedule, the other attention
+variants kept for measurement, and config 1's one-division-per-row IR with the fast-math emitter
+options.  Each is checked on the CPU by the PTX / tensor-core emulators; here it is compared with the
+oracle on a B200.  Run them with ``pytest -m gpu_optin``; a variant moves to the ``gpu`` suite once it
+has passed there.
+"""
+import pytest
+import torch
+
+from emmy_ptx_b200 import irgen, data
+from oracle.run import oracle_outputs
+from tests.checks import compare, rtol_for
+from tests.test_gpu_parity import _run_ours
+from tests.test_gpu_parity import test_full_attention_tensor_core_sampled as _full_attention
+
+pytestmark = [pytest.mark.gpu_optin,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU (B200)")]
+
+
+ATTN_VARIANTS = {
+    "persistent-2ctas": {"attn_persistent": True, "sms": 2},
+    "persistent-3ctas": {"attn_persistent": True, "sms": 3},
+    "pack-in-turn": {"attn_pack_in_turn": True},
+    "pack-after-turn": {"attn_pack_after_turn": True},
+    "defer-sum": {"attn_pack_after_turn": True, "attn_defer_sum": True},
+    "prefetch": {"attn_prefetch_next": 148},
+    "poly8": {"attn_poly": 8},
+    "f16-int4": {"attn_f16_int": 4},
+    "no-turns": {"attn_pingpong": False},
+    "bf16-pairs": {"attn_half": False},
+}
+
+
+_ORACLE_CACHE: dict = {}
+
+
+def _small_with_oracle(key):
+    """A small configuration's inputs and oracle outputs, computed once per key."""
+    if key not in _ORACLE_CACHE:
+        p = irgen.SMALL[key]()
+        t = data.make_inputs(p)
+        _ORACLE_CACHE[key] = (p, t, oracle_outputs(p, t))
+    return _ORACLE_CACHE[key]
+
+
+@pytest.mark.parametrize("key", ["c5tc", "c5tcnc"])
+@pytest.mark.parametrize("variant", sorted(ATTN_VARIANTS))
+def test_attention_variants_match_oracle(key, variant):
+    """The opt-in attention variants (measured against the default for speed) give the default's
+    results: each against the oracle on the small causal and non-causal configurations."""
+    p, t, want = _small_with_oracle(key)
+    got, ex = _run_ours(p, t, **ATTN_VARIANTS[variant])
+    assert ex.records[-1]["kind"] == "tcgen05_attention"
+    assert ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"{key} {variant}", rms_floor=True)
+
+
+def test_full_softmax_fast_math_options():
+    """Config 1 in its measured variants: one division per row in the IR, and the opt-in approx_ftz
+    and fast_div emitter options; all within the softmax tolerance at full size."""
+    p = irgen.softmax_ir(4096, 1024, "warp", recip=True)
+    t = data.make_inputs(p)
+    want = torch.softmax(t["x"].cuda().double(), dim=-1).cpu()
+    for opts in ({}, {"approx_ftz": True, "fast_div": True}):
+        got, _ = _run_ours(p, t, **opts)
+        compare(got["y"], want, "f32", 1e-5, f"c1 recip {opts}")
+
+
+def test_full_attention_persistent_sampled():
+    """Config 5 at full size through the persistent schedule; sampled heads against float64."""
+    _full_attention({"attn_persistent": True})
