@@ -111,3 +111,45 @@ def test_lowering_option():
     recs = compile_graph(Graph.from_dict(full.graph), full.meta(), {"attn_persistent": True}).kernels
     assert [r["kind"] for r in recs] == ["value_prepass", "tcgen05_attention"]
     assert recs[1]["grid"] == [148, 1, 1] and recs[1]["block"] == [384, 1, 1]
+
+
+def _schedule(P, batch, heads, seq):
+    """Each CTA's units in order, as (batch, head, 256-row tile): unit k*P + c on even rounds and
+    k*P + (P-1-c) on odd ones, the longest causal tiles first; a CTA stops at its first missing unit."""
+    nbh, nt = batch * heads, seq // 256
+    out = []
+    for c in range(P):
+        units, k = [], 0
+        while True:
+            u = k * P + (P - 1 - c if k & 1 else c)
+            if u >= nbh * nt:
+                break
+            bh = u % nbh
+            units.append((bh // heads, bh % heads, nt - 1 - u // nbh))
+            k += 1
+        out.append(units)
+    return out
+
+
+def test_schedule_model_matches_the_kernel():
+    # the units each simulated CTA loads Q for, in order, are the model's
+    txt, rec = _kernel()
+    sim = CtaSim(txt, rec)
+    model = _schedule(CTAS, B, H, S)
+    for cta in range(rec["grid"][0]):
+        seen = []
+        for _, name, cs, _ in sim.run(ctaid=cta, seed=cta, log_tma=True)["tma"]:
+            if name == "tmQ":
+                u = (cs[3], cs[2], cs[1] // 256)
+                if u not in seen:
+                    seen.append(u)
+        assert seen == model[cta], cta
+
+
+def test_config5_schedule_is_balanced():
+    # config 5 (8 x 32 x 4096, causal) over 148 CTAs: a unit's work is its 64-row key/value blocks over
+    # both row halves, 8t + 6 for tile t; the busiest CTA is within 1 % of the mean
+    sched = _schedule(148, 8, 32, 4096)
+    work = [sum(8 * t + 6 for _, _, t in units) for units in sched]
+    assert sum(len(u) for u in sched) == 8 * 32 * 16
+    assert max(work) <= 1.01 * (sum(work) / len(work))
