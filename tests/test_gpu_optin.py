@@ -13,7 +13,7 @@ from emmy_ptx_b200 import irgen, data
 from oracle.run import oracle_outputs
 from tests.checks import compare, rtol_for
 from tests.test_gpu_parity import _run_ours
-from tests.test_gpu_parity import test_full_attention_tensor_core_sampled as _full_attention
+from tests.test_gpu_parity import full_attention_check
 
 pytestmark = [pytest.mark.gpu_optin,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU (B200)")]
@@ -70,4 +70,4 @@ def test_full_softmax_fast_math_options():
 
 def test_full_attention_persistent_sampled():
     """Config 5 at full size through the persistent schedule; sampled heads against float64."""
-    _full_attention({"attn_persistent": True})
+    full_attention_check({"attn_persistent": True})

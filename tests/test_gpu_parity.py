@@ -139,16 +139,20 @@ def test_full_bmm_tensor_core_sampled():
         compare(C[b], want, "f32", 1e-4, f"c4 full batch {b}")
 
 
-def test_full_attention_tensor_core_sampled(opts=None):
-    """Config 5 at full size through the tcgen05 kernel; sampled heads against float64 attention
-    (``opts``: compile options, for the opt-in variants' tests)."""
+def test_full_attention_tensor_core_sampled():
+    """Config 5 at full size through the tcgen05 kernel; sampled heads against float64 attention."""
+    full_attention_check({})
+
+
+def full_attention_check(opts):
+    """Config 5 at full size compiled with ``opts``; heads (0,0), (3,17), (7,31) against float64."""
     import math
     p = irgen.FULL["c5"]()
     gen = torch.Generator(device="cuda").manual_seed(11)
     shape = p.spec("Q").shape
     Q, K, V = ((torch.randn(shape, generator=gen, device="cuda")).to(torch.bfloat16) for _ in range(3))
     O = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), opts or {})
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), opts)
     assert mod.kernels[-1]["kind"] == "tcgen05_attention"
     ex = Executable(mod)
     ex({"Q": Q, "K": K, "V": V, "O": O})
