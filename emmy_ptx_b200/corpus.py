@@ -691,6 +691,29 @@ def special_values_16bit(n=640):
     return _problem("special16", f"special16_{n}", "special_values_16bit", args, body, (n // 8 + 63) // 64, 64)
 
 
+def softmax_mid(a=4, b=32, c=16):
+    """softmax over the middle axis of [4, 32, 16] (torch dim=1): a thread per (i, k) column walks j
+    in three rolled loops, every load 16 elements (64 bytes) from the previous one."""
+    body = [Tile([Axis("i", a), Axis("k", c)], [
+        Loop("j", b, [Load(["x"], "x", [V("i"), V("j"), V("k")], "f32"), Accum("m", "maximum", "x")]),
+        Loop("j1", b, [
+            Load(["x1"], "x", [V("i"), V("j1"), V("k")], "f32"),
+            Assign("z", "subtract", ["x1", "m"]),
+            Assign("e", "exp", ["z"]),
+            Accum("s", "add", "e"),
+        ]),
+        Loop("j2", b, [
+            Load(["x2"], "x", [V("i"), V("j2"), V("k")], "f32"),
+            Assign("z2", "subtract", ["x2", "m"]),
+            Assign("e2", "exp", ["z2"]),
+            Assign("y", "divide", ["e2", "s"]),
+            Write("y", ["y"], [V("i"), V("j2"), V("k")], "f32"),
+        ]),
+    ])]
+    args = [TensorSpec("x", (a, b, c), "f32", ("normal", 1.0)), TensorSpec("y", (a, b, c), "f32", output=True)]
+    return _problem("softmax_mid", f"softmax_mid_{a}x{b}x{c}", "softmax_mid", args, body, 1, a * c)
+
+
 def _kernel_node(entry, inputs, outputs, body):
     return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
             "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
@@ -769,4 +792,5 @@ CORPUS = {
     "k_special": special_values,
     "k_scanprod": scan_max_and_prod,
     "k_special16": special_values_16bit,
+    "k_softmax_mid": softmax_mid,
 }

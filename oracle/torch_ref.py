@@ -191,6 +191,7 @@ CORPUS = {
     "pad": lambda t, p: {"y": __import__("torch").nn.functional.pad(t["x"].double(), (p["left"], p["right"]))},
     "logsumexp": lambda t, p: {"y": __import__("torch").logsumexp(t["x"].double(), -1)},
     "matmul": lambda t, p: {"C": t["A"].double() @ t["B"].double()},
+    "softmax_mid": lambda t, p: {"y": __import__("torch").softmax(t["x"].double(), 1)},
     "scanprod": lambda t, p: {"cm": __import__("torch").cummax(t["x"].double(), -1).values,
                               "pr": t["x"].double().prod(-1)},
 }
