@@ -498,6 +498,26 @@ def bmm_ir(batch: int = 16, m: int = 4096, n: int = 4096, k: int = 4096) -> Prob
                    params={"batch": batch, "m": m, "n": n, "k": k})
 
 
+def bmm_naive_ir(batch: int, m: int, n: int, k: int, threads: int = 256) -> Problem:
+    """The same batched matmul in its unscheduled form: a thread per output element, a rolled Loop
+    over k accumulating bf16 products in f32 (what a lowering emits before any tiling)."""
+    body = [Tile([Axis("b", batch), Axis("i", m), Axis("j", n)], [
+        Loop("kk", k, [
+            Load(["a"], "A", [V("b"), V("i"), V("kk")], "bf16"),
+            Load(["w"], "B", [V("b"), V("kk"), V("j")], "bf16"),
+            Assign("p", "multiply", ["a", "w"]),
+            Accum("acc", "add", "p"),
+        ]),
+        Write("C", ["acc"], [V("b"), V("i"), V("j")], "f32"),
+    ])]
+    args = [TensorSpec("A", (batch, m, k), "bf16", ("normal", 0.02)),
+            TensorSpec("B", (batch, k, n), "bf16", ("normal", 0.02)),
+            TensorSpec("C", (batch, m, n), "f32", output=True)]
+    return Problem(f"bmm_naive_{batch}x{m}x{n}x{k}", "bmm", "bmm_naive", _graph("bmm_naive", args, body), args,
+                   grid=(batch * m * n + threads - 1) // threads, block=threads, rtol=1e-4, atol=1e-6,
+                   params={"batch": batch, "m": m, "n": n, "k": k})
+
+
 # ---- config 5: causal attention -------------------------------------------------------------
 
 

@@ -47,7 +47,13 @@ def _body_data(node, rename=None) -> list:
 
 def is_canonical(node, template, rename: dict) -> bool:
     """True when ``node``'s body, its buffers renamed by ``rename``, equals the body of the single
-    kernel of ``template`` (a problem from :mod:`.irgen`)."""
+    kernel of ``template`` (a problem from :mod:`.irgen`, or a callable making one: a generator that
+    has no form for these parameters raises ValueError, and then nothing matches)."""
+    if callable(template):
+        try:
+            template = template()
+        except ValueError:
+            return False
     tnode = Graph.from_dict(template.graph).kernels()[0]
     return _body_data(node, rename) == _body_data(tnode)
 
@@ -108,6 +114,10 @@ def match_bmm(graph, node):
     if X is None or Y is None or X.shape[2] != Y.shape[1]:
         return None
     k = X.shape[2]
+    rename = {X.name: "A", Y.name: "B", C.name: "C"}
+    from .irgen import bmm_ir, bmm_naive_ir
+    if is_canonical(node, lambda: bmm_naive_ir(bt, m, n, k), rename):
+        return X, Y, C, bt, m, n, k              # the unscheduled nest: one thread per element
 
     stmts = []
     walk(op.body, stmts.append)
@@ -185,8 +195,7 @@ def match_bmm(graph, node):
                 return None
         if cls == "ZeroPrologue":
             return None
-    from .irgen import bmm_ir
-    if not is_canonical(node, bmm_ir(bt, m, n, k), {X.name: "A", Y.name: "B", C.name: "C"}):
+    if not is_canonical(node, lambda: bmm_ir(bt, m, n, k), rename):
         return None
     return X, Y, C, bt, m, n, k
 
@@ -336,7 +345,7 @@ def match_attention(graph, node):
     K = vals[kname]
     V = vals[vname]
     from .irgen import attention_ir
-    if not is_canonical(node, attention_ir(bt, hd, seq, dim, causal, scale=scale),
+    if not is_canonical(node, lambda: attention_ir(bt, hd, seq, dim, causal, scale=scale),
                         {Q.name: "Q", K.name: "K", V.name: "V", O.name: "O"}):
         return None
     return Q, K, V, O, bt, hd, seq, dim, causal, scale

@@ -71,3 +71,13 @@ def test_full_softmax_fast_math_options():
 def test_full_attention_persistent_sampled():
     """Config 5 at full size through the persistent schedule; sampled heads against float64."""
     full_attention_check({"attn_persistent": True})
+
+
+def test_gemm_from_the_unscheduled_matmul():
+    """The thread-per-element matmul nest, lowered to the tcgen05 GEMM, against the oracle."""
+    p = irgen.bmm_naive_ir(2, 256, 512, 256)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[0]["kind"] == "tcgen05_gemm" and ex.error_code() == 0
+    compare(got["C"], want["C"], "f32", rtol_for(p), "bmm naive")

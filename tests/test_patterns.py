@@ -194,3 +194,21 @@ def test_renamed_buffers_still_match():
     g = Graph.from_dict(json.loads(blob))
     hit = match_bmm(g, g.kernels()[0])
     assert hit is not None and (hit[0].name, hit[1].name, hit[2].name) == ("lhs", "rhs", "out")
+
+
+def test_unscheduled_matmul_reaches_the_tensor_cores():
+    # a thread per output element with a rolled k loop is the same contraction: at tile multiples it
+    # takes the tcgen05 GEMM; at other shapes, or with a transposed store, it stays on the CUDA cores
+    p = irgen.bmm_naive_ir(1, 128, 256, 64)
+    g, k = _kernel(p)
+    assert match_bmm(g, k) is not None
+    assert compile_graph(g, p.meta()).kernels[0]["kind"] == "tcgen05_gemm"
+    odd = irgen.bmm_naive_ir(1, 100, 256, 64)
+    g2, k2 = _kernel(odd)
+    assert compile_graph(g2, odd.meta()).kernels[0]["kind"] == "generic"
+
+    def transpose_store(st):
+        if st.get("kind") == "Write":
+            st["index"][1], st["index"][2] = st["index"][2], st["index"][1]
+    g3, k3 = _mutated(p, "bmm_naive", transpose_store)
+    assert match_bmm(g3, k3) is None

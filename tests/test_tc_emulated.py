@@ -145,3 +145,9 @@ def test_late_completions_expose_a_planted_early_release():
     _check(p, t, {}, "tcgen05_attention", defer=True)            # the real kernel passes
     with pytest.raises((AssertionError, RuntimeError)):
         _check(p, t, {}, "tcgen05_attention", defer=True, mod=CompiledModule(bad, mod.kernels))
+
+
+def test_gemm_from_the_unscheduled_matmul_emulated():
+    # the thread-per-element matmul nest lowered to the tcgen05 GEMM; the oracle interprets the nest
+    p = irgen.bmm_naive_ir(1, 128, 256, 64)
+    _check(p, data.make_inputs(p), {"sms": 1}, "tcgen05_gemm")
