@@ -39,6 +39,7 @@ struct Driver {
   CUresult (*PrimaryCtxRetain)(CUcontext*, CUdevice);
   CUresult (*CtxSetCurrent)(CUcontext);
   CUresult (*CtxGetCurrent)(CUcontext*);
+  CUresult (*CtxGetId)(CUcontext, unsigned long long*);  // optional (CUDA 12.0+)
   CUresult (*CtxSynchronize)(void);
   CUresult (*ModuleLoadDataEx)(CUmodule*, const void*, unsigned int, CUjit_option*, void**);
   CUresult (*ModuleLoadData)(CUmodule*, const void*);
@@ -121,6 +122,7 @@ int load_driver() {
             sym(lib, d.TensorMapEncodeTiled, "cuTensorMapEncodeTiled") &&
             sym(lib, d.GetErrorString, "cuGetErrorString");
   if (!ok) return fail(EMMY_ERR_NO_DRIVER, "libcuda.so.1 lacks a required symbol: %s", dlerror());
+  if (!sym(lib, d.CtxGetId, "cuCtxGetId")) d.CtxGetId = nullptr;
   g_drv = d;
   g_loaded = true;
   return 0;
@@ -183,6 +185,20 @@ int nc(int rc, const char* what) {
 }
 
 }  // namespace
+
+int emmy_internal_ready(unsigned long long* context_id) {
+  if (int rc = ready()) return rc;
+  if (context_id) {
+    // A context's id is unique for the process's lifetime: a primary context that was reset and
+    // created again gets a new one, so a cache keyed on it never serves a stale device address.
+    unsigned long long id = 0;
+    if (g_drv.CtxGetId && g_drv.CtxGetId(g_ctx, &id) == CUDA_SUCCESS)
+      *context_id = id;
+    else
+      *context_id = static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(g_ctx));
+  }
+  return 0;
+}
 
 int emmy_internal_fail(int code, const char* fmt, ...) {
   char buf[1024];

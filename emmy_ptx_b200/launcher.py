@@ -61,6 +61,7 @@ SIGNATURES = {
     "emmy_nccl_destroy": [],
     "emmy_bmm_bf16_noalloc": [vp, vp, vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
                               ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, vp],
+    "emmy_bmm_bf16_noalloc_status": [ctypes.POINTER(ctypes.c_uint32), vp],
 }
 
 # CUfunction_attribute values used by the runtime
@@ -313,6 +314,15 @@ class Device:
                                              int(block), int(dyn_smem), int(scratch_bytes), vp(stream or 0)),
               "emmy_bmm_bf16_noalloc")
         self.launches += 1
+
+    def bmm_noalloc_status(self, stream: int) -> int:
+        """The status word of the last no-allocation bmm queued on ``stream`` (0 = every bounded wait
+        completed); waits for the stream."""
+        self._use()
+        word = ctypes.c_uint32(0)
+        check(self.lib.emmy_bmm_bf16_noalloc_status(ctypes.byref(word), vp(stream or 0)),
+              "emmy_bmm_bf16_noalloc_status")
+        return int(word.value)
 
     def nccl_destroy(self) -> None:
         self._use()

@@ -8,7 +8,8 @@
  *
  * Conventions
  *  - Every function returns 0 on success.  Non-zero values are the CUresult of the failing
- *    driver call, EMMY_ERR_NCCL_BASE + ncclResult_t for NCCL, or one of the EMMY_ERR_* codes.
+ *    driver call, EMMY_ERR_NCCL_BASE + ncclResult_t for NCCL, EMMY_ERR_RUNTIME_BASE + cudaError_t
+ *    for the CUDA runtime calls of the no-allocation entry points, or one of the EMMY_ERR_* codes.
  *    emmy_last_error() returns a description of the last failure on the calling thread.
  *    Nothing in this library calls exit() or abort().
  *  - Device pointers are CUdeviceptr values (uint64_t) owned by the caller; module, function,
@@ -34,6 +35,7 @@ extern "C" {
 #define EMMY_ERR_BAD_ARG 10003     /* null handle, zero size, misaligned pointer, ... */
 #define EMMY_ERR_NO_NCCL 10004     /* libnccl.so.2 could not be opened or lacks a symbol */
 #define EMMY_ERR_NCCL_BASE 20000   /* + ncclResult_t */
+#define EMMY_ERR_RUNTIME_BASE 30000 /* + cudaError_t (CUDA runtime calls) */
 
 /* ABI version of this header (bumped on incompatible change). */
 int emmy_version(void);
@@ -156,10 +158,20 @@ int emmy_nccl_destroy(void);
  *  - The scratch is a fixed 256-byte array in this library's device memory, held on every GPU that loads
  *    the library until the process exits.  The first call on a device looks up its address (with that
  *    device current); make that first call before any stream capture.
- *  - Every call uses the same array and clears it first; calls that overlap on the GPU race on it. */
+ *  - Every call uses the same array and clears it first; calls that overlap on the GPU race on it.
+ *  - Needs emmy_init() on the calling thread first (EMMY_ERR_NOT_INIT otherwise).
+ *  - A kernel whose bounded pipeline wait timed out returns early with C incomplete and a non-zero
+ *    status word; read it with emmy_bmm_bf16_noalloc_status. */
 int emmy_bmm_bf16_noalloc(void* function, const void* tmap_a, const void* tmap_b, uint64_t a, uint64_t b,
                           uint64_t c, uint32_t grid, uint32_t block, uint32_t dyn_smem,
                           uint32_t scratch_bytes, void* stream);
+
+/* Reads the status word of the last emmy_bmm_bf16_noalloc call queued on `stream` into *word
+ * (0 = every wait completed; otherwise the code of the wait that timed out).  It queues one 4-byte
+ * device-to-host copy from the fixed array on `stream` and waits for that stream, so the word is
+ * valid on return; it allocates nothing.  With calls in flight on other streams the word may be
+ * theirs (the array is shared).  No counterpart in the reference. */
+int emmy_bmm_bf16_noalloc_status(uint32_t* word, void* stream);
 
 #ifdef __cplusplus
 }
