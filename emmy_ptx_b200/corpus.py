@@ -714,6 +714,117 @@ def softmax_mid(a=4, b=32, c=16):
     return _problem("softmax_mid", f"softmax_mid_{a}x{b}x{c}", "softmax_mid", args, body, 1, a * c)
 
 
+FLT_MAX = 3.4028234663852886e38
+
+
+def nan_to_num(n=777):
+    """y = nan_to_num(x): NaN -> 0, +inf -> the largest f32, -inf -> its negative, other values
+    unchanged (torch's defaults).  NaN is found with ``isnan`` (``testp.notanumber``): an ordered
+    comparison such as x != x is false on NaN in the instructions the IR lowers to."""
+    body = [Tile([Axis("i", n)], [
+        Load(["x"], "x", [V("i")], "f32"),
+        Assign("isn", "isnan", ["x"], "bool"),
+        Assign("isi", "isinf", ["x"], "bool"),
+        Assign("pos", "greater", ["x", Lit(0.0)], "bool"),
+        Select("y", [(V("isn"), Lit(0.0)),
+                     (Bin("&&", V("isi"), V("pos")), Lit(FLT_MAX)),
+                     (V("isi"), Lit(-FLT_MAX)),
+                     (None, "x")]),
+        Write("y", ["y"], [V("i")], "f32"),
+    ])]
+    args = [TensorSpec("x", (n,), "f32", ("special", 1.0)), TensorSpec("y", (n,), "f32", output=True)]
+    return _problem("nan_to_num", f"nan_to_num_{n}", "nan_to_num", args, body, (n + 127) // 128, 128)
+
+
+def log_add_exp(n=1000):
+    """y = logaddexp(a, b) = max(a, b) + log1p(exp(-|a - b|)), the overflow-free form."""
+    body = [Tile([Axis("i", n)], [
+        Load(["a"], "a", [V("i")], "f32"), Load(["b"], "b", [V("i")], "f32"),
+        Assign("m", "maximum", ["a", "b"]),
+        Assign("d", "subtract", ["a", "b"]),
+        Assign("ad", "absolute", ["d"]),
+        Assign("nd", "negative", ["ad"]),
+        Assign("e", "exp", ["nd"]),
+        Assign("l", "log1p", ["e"]),
+        Assign("y", "add", ["m", "l"]),
+        Write("y", ["y"], [V("i")], "f32"),
+    ])]
+    args = [TensorSpec("a", (n,), "f32", ("normal", 3.0)), TensorSpec("b", (n,), "f32", ("normal", 3.0)),
+            TensorSpec("y", (n,), "f32", output=True)]
+    return _problem("logaddexp", f"logaddexp_{n}", "log_add_exp", args, body, (n + 127) // 128, 128)
+
+
+SELU_ALPHA = 1.6732632423543772
+SELU_SCALE = 1.0507009873554805
+
+
+def elu_selu(rows=2, cols=320):
+    """elu(x) = x if x > 0 else expm1(x) (alpha 1) and selu(x) = scale * (x if x > 0 else
+    alpha * expm1(x)), four elements a thread through 16-byte vector loads and stores."""
+    n = rows * cols
+    body = [Tile([Axis("i4", n // 4)], [
+        Let("i", Bin("*", V("i4"), 4)),
+        Load([f"x{k}" for k in range(4)], "x", [V("i")], "f32"),
+        *[st for k in range(4) for st in (
+            Assign(f"p{k}", "greater", [f"x{k}", Lit(0.0)], "bool"),
+            Assign(f"m{k}", "expm1", [f"x{k}"]),
+            Assign(f"e{k}", "where", [f"p{k}", f"x{k}", f"m{k}"]),
+            Assign(f"am{k}", "multiply", [f"m{k}", Lit(SELU_ALPHA)]),
+            Assign(f"sv{k}", "where", [f"p{k}", f"x{k}", f"am{k}"]),
+            Assign(f"s{k}", "multiply", [f"sv{k}", Lit(SELU_SCALE)]))],
+        Write("elu", [f"e{k}" for k in range(4)], [V("i")], "f32"),
+        Write("selu", [f"s{k}" for k in range(4)], [V("i")], "f32"),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("elu", (rows, cols), "f32", output=True),
+            TensorSpec("selu", (rows, cols), "f32", output=True)]
+    return _problem("elu_selu", f"elu_selu_{rows}x{cols}", "elu_selu", args, body, (n // 4 + 63) // 64, 64)
+
+
+def row_any(rows=64, cols=96, thresh=2.5):
+    """out[r] = any(x[r, :] > thresh) as a byte, a warp per row: each lane folds its columns' tests
+    into an i32 flag with a maximum Accum, one shuffle takes the warp's maximum."""
+    body = [Tile([Axis("row", rows), Axis("t", 32)], [
+        StridedLoop("c", cols, V("t"), 32, [
+            Load(["x"], "x", [V("row"), V("c")], "f32"),
+            Assign("hi", "greater", ["x", Lit(thresh)], "bool"),
+            Select("one", [(V("hi"), 1), (None, 0)]),
+            {**Accum("f", "maximum", "one", "i32"), "op": _int_op("maximum", 0)},
+        ], end=cols),
+        WarpShuffle(["f"], ["f_o"], [Assign("f", "maximum", ["f", "f_o"], "i32")]),
+        Assign("any", "greater", ["f", 0], "bool"),
+        Cond(Bin("==", V("t"), 0), [Write("out", ["any"], [V("row")], "u8")]),
+    ])]
+    args = [TensorSpec("x", (rows, cols), "f32", ("normal", 1.0)), TensorSpec("out", (rows,), "u8", output=True)]
+    return _problem("any", f"any_{rows}x{cols}", "row_any", args, body, rows, 32, rtol=0.0, atol=0.0,
+                    thresh=thresh)
+
+
+def l2_normalize(rows=64, cols=256, eps=1e-12, threads=64):
+    """y = x / max(||x||_2, eps) along the last axis of [2, 32, 256] (torch.nn.functional.normalize),
+    a block per row: block-strided sum of squares, block reduction, one division per element."""
+    nw = threads // 32
+    body = [
+        Smem("red", [nw], "f32", 16),
+        Tile([Axis("row", rows), Axis("t", threads)], [
+            StridedLoop("c", cols, V("t"), threads, [
+                Load(["x"], "x", [V("row"), V("c")], "f32"),
+                Assign("sq", "multiply", ["x", "x"]),
+                Accum("ss", "add", "sq"),
+            ], end=cols),
+            *_block_reduce(["ss"], ["red"], {"ss": "add"}, nw),
+            Assign("nrm", "sqrt", ["ss"]),
+            Assign("den", "maximum", ["nrm", Lit(eps)]),
+            StridedLoop("c2", cols, V("t"), threads, [
+                Load(["x2"], "x", [V("row"), V("c2")], "f32"),
+                Assign("y", "divide", ["x2", "den"]),
+                Write("y", ["y"], [V("row"), V("c2")], "f32"),
+            ], end=cols),
+        ]),
+    ]
+    args = [TensorSpec("x", (2, 32, cols), "f32", ("normal", 1.0)), TensorSpec("y", (2, 32, cols), "f32", output=True)]
+    return _problem("l2norm", f"l2norm_{rows}x{cols}", "l2_normalize", args, body, rows, threads, eps=eps)
+
+
 def _kernel_node(entry, inputs, outputs, body):
     return {"op": "KernelOp", "op_fields": {"name": entry, "body": body}, "inputs": list(inputs),
             "outputs": [{"name": o.name, "shape": list(o.shape), "dtype": o.dtype} for o in outputs]}
@@ -793,4 +904,9 @@ CORPUS = {
     "k_scanprod": scan_max_and_prod,
     "k_special16": special_values_16bit,
     "k_softmax_mid": softmax_mid,
+    "k_nan_to_num": nan_to_num,
+    "k_logaddexp": log_add_exp,
+    "k_elu_selu": elu_selu,
+    "k_any": row_any,
+    "k_l2norm": l2_normalize,
 }

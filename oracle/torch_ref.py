@@ -194,4 +194,12 @@ CORPUS = {
     "softmax_mid": lambda t, p: {"y": __import__("torch").softmax(t["x"].double(), 1)},
     "scanprod": lambda t, p: {"cm": __import__("torch").cummax(t["x"].double(), -1).values,
                               "pr": t["x"].double().prod(-1)},
+    # torch's posinf / neginf defaults for a float32 tensor: the largest finite f32 and its negative
+    "nan_to_num": lambda t, p: {"y": __import__("torch").nan_to_num(t["x"]).double()},
+    "logaddexp": lambda t, p: {"y": __import__("torch").logaddexp(t["a"].double(), t["b"].double())},
+    "elu_selu": lambda t, p: {"elu": __import__("torch").nn.functional.elu(t["x"].double()),
+                              "selu": __import__("torch").nn.functional.selu(t["x"].double())},
+    "any": lambda t, p: {"out": (t["x"].double() > p["thresh"]).any(-1).to(__import__("torch").uint8)},
+    "l2norm": lambda t, p: {"y": __import__("torch").nn.functional.normalize(t["x"].double(), dim=-1,
+                                                                             eps=p["eps"])},
 }

@@ -1,6 +1,9 @@
 """Regenerate the golden fixtures under tests/golden (run where the reference checkout exists).
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH [--only small|full|all]
+    EMMY_REFERENCE=PATH python tests/golden/make_golden.py
+
+PATH is a checkout of fanjialin8-create/emmy-ptx (the directory holding its ``compile.py``).
 
 For every small configuration in ``emmy_ptx_b200.irgen.SMALL`` and every coverage kernel in
 ``emmy_ptx_b200.corpus.CORPUS`` it writes
@@ -15,6 +18,11 @@ For every small configuration in ``emmy_ptx_b200.irgen.SMALL`` and every coverag
 * ``vectors/<key>.npz`` — the float64 source-expression result (``oracle/torch_ref.py``) on the
   seeded inputs, stored as float64, and an input checksum.
 * ``manifest.json`` — a hash of each IR, so a fixture made from a different IR is detected.
+
+For every BASELINE configuration at full size (``irgen.FULL``) it writes ``ref_ptx_full/<key>.ptx``:
+the reference emitter's PTX for the full-size IR, which ``bench.py`` launches with the same
+geometry and buffers as this backend's kernel to time the reference's own kernels on the GPU
+(``ref_ptx_full/manifest.json`` holds the IR hashes).
 """
 from __future__ import annotations
 
@@ -61,10 +69,56 @@ def _ptxas_error(ptx: str) -> str:
     return lines[0] if lines else f"exit status {r.returncode}"
 
 
+def reference_ptx(compile_py: Path, env: dict, p) -> tuple[str | None, str]:
+    """The reference emitter's PTX for problem ``p`` (its IR and meta.json in a scratch directory),
+    or (None, why) when the reference rejects the IR or writes PTX that must not run."""
+    from emmy_ptx_b200.codegen.ptxcheck import undefined_uses
+    with tempfile.TemporaryDirectory() as td:
+        ir = Path(td) / f"{p.entry}.ir.json"
+        ir.write_text(json.dumps(p.graph))
+        (Path(td) / "meta.json").write_text(json.dumps(p.meta()))
+        r = subprocess.run([sys.executable, str(compile_py), str(ir)], capture_output=True, text=True, env=env)
+    if r.returncode != 0:
+        return None, (r.stderr.strip().splitlines() or ["exit status %d" % r.returncode])[-1]
+    if _ptxas_error(r.stdout):
+        return None, "ptxas: " + _ptxas_error(r.stdout)
+    if undefined_uses(r.stdout):
+        entry, _, reg, text = undefined_uses(r.stdout)[0]
+        return None, f"unsafe: {entry}: {reg} read before any write on some path: {text.strip()}"
+    return r.stdout, ""
+
+
+def write_full(compile_py: Path, env: dict) -> int:
+    """``ref_ptx_full/<key>.ptx`` for every full-size BASELINE configuration."""
+    from emmy_ptx_b200 import irgen
+    out = HERE / "ref_ptx_full"
+    out.mkdir(exist_ok=True)
+    manifest = {}
+    for key, mk in irgen.FULL.items():
+        p = mk()
+        ptx, why = reference_ptx(compile_py, env, p)
+        rec = {"ir": ir_hash(p.graph, p.meta()), "entry": p.entry}
+        if ptx is None:
+            rec["ref_error"] = why
+            print(f"full {key}: no reference PTX: {why}")
+        else:
+            (out / f"{key}.ptx").write_text(ptx)
+            rec["ref_ptx_lines"] = ptx.count("\n")
+            print(f"full {key}: {p.name} ref PTX {rec['ref_ptx_lines']} lines")
+        manifest[key] = rec
+    (out / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("EMMY_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("EMMY_REFERENCE"),
+                    help="checkout of the reference (the directory holding compile.py); or set EMMY_REFERENCE")
+    ap.add_argument("--only", default="all", choices=["all", "small", "full"])
     args = ap.parse_args()
+    if not args.reference:
+        print("give the reference checkout with --reference PATH or EMMY_REFERENCE", file=sys.stderr)
+        return 2
     import numpy as np
     from emmy_ptx_b200 import irgen, corpus, data
     from emmy_ptx_b200.codegen.ptxcheck import undefined_uses
@@ -74,9 +128,13 @@ def main() -> int:
     if not compile_py.exists():
         print(f"reference compile.py not found at {compile_py}", file=sys.stderr)
         return 2
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE / "emmy_shim"), str(ROOT)]))
+    if args.only in ("all", "full"):
+        write_full(compile_py, env)
+    if args.only == "full":
+        return 0
     (HERE / "ref_ptx").mkdir(exist_ok=True)
     (HERE / "vectors").mkdir(exist_ok=True)
-    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE / "emmy_shim"), str(ROOT)]))
     manifest = {}
     for key, mk in {**irgen.SMALL, **corpus.CORPUS}.items():
         p = mk()

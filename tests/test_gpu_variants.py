@@ -1,10 +1,9 @@
-"""GPU tests of the opt-in variants that have not yet run on a B200 (marker ``gpu_optin``).
+"""GPU tests of the variants kept beside the default lowerings.
 
-These kernels are not on the default path: the persistent attention schedule, the other attention
-variants kept for measurement, and config 1's one-division-per-row IR with the fast-math emitter
-options.  Each is checked on the CPU by the PTX / tensor-core emulators; here it is compared with the
-oracle on a B200.  Run them with ``pytest -m gpu_optin``; a variant moves to the ``gpu`` suite once it
-has passed there.
+The persistent attention schedule and the other attention variants kept for measurement, config 1's
+one-division-per-row IR with the fast-math emitter options, and the unscheduled matmul nest lowered
+to the tcgen05 GEMM.  Each is also checked on the CPU by the PTX / tensor-core emulators; here it is
+compared with the oracle (or float64) on a B200.
 """
 import pytest
 import torch
@@ -15,8 +14,7 @@ from tests.checks import compare, rtol_for
 from tests.test_gpu_parity import _run_ours
 from tests.test_gpu_parity import full_attention_check
 
-pytestmark = [pytest.mark.gpu_optin,
-              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU (B200)")]
+pytestmark = pytest.mark.gpu
 
 
 ATTN_VARIANTS = {

@@ -102,19 +102,19 @@ def test_shards_cover_every_unit_once(n, world):
 def test_nccl_steps_are_never_captured_in_a_graph():
     """The sum's multi-GPU step holds an ncclAllReduce; bench.py times it with host launches, since a
     live CUDA graph that holds an NCCL call keeps the communicator's teardown waiting.  Steps without
-    a collective are graph-replayed unless graphs are switched off."""
+    a collective are graph-replayed, at any number of ranks, unless graphs are switched off."""
     import importlib.util
     from pathlib import Path
     spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parents[1] / "bench.py")
     bench = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(bench)
     assert bench.capture_steps(collective=True, no_graph=False) is False
+    assert bench.capture_steps(collective=True, no_graph=False, world=8) is False
     assert bench.capture_steps(collective=False, no_graph=False) is True
     assert bench.capture_steps(collective=False, no_graph=True) is False
-    # several ranks: no graph capture at all (host launches, the measured multi-GPU path)
-    assert bench.use_graphs(world=2, no_graph=False) is False
-    assert bench.capture_steps(collective=False, no_graph=False, world=8) is False
-    assert bench.use_graphs(world=1, no_graph=False) is True
+    assert bench.capture_steps(collective=False, no_graph=False, world=8) is True
+    assert bench.use_graphs(world=2, no_graph=False) is True
+    assert bench.use_graphs(world=1, no_graph=True) is False
 
 
 def test_bench_compile_options_parse():
