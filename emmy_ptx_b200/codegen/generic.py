@@ -748,6 +748,8 @@ class KernelEmitter:
             return
         esize = dt_bytes(t)
         space = "shared" if shared else ("global.nc" if buf not in self.written else "global")
+        if not shared and buf not in self.written:
+            space += self._load_hint()
         if not shared:
             self.palign[buf] = max(self.palign.get(buf, 16), 16)
         for first, cnt in self._vec_plan(lin, len(names), esize, buf, shared):
@@ -781,6 +783,30 @@ class KernelEmitter:
                     self.syms[hi_nm] = Sym("f32", op=self._unpack(w, t, 1))
             else:
                 raise Unsupported(f"unsupported load element size {esize}")
+
+    def _load_hint(self) -> str:
+        """Cache qualifiers for read-only global vector loads (opt-in): ``ld_no_l1`` adds
+        ``.L1::no_allocate`` (streamed data never re-read through L1), ``ld_prefetch`` adds
+        ``.L2::64B`` / ``.L2::128B`` / ``.L2::256B`` (the L2 fetches that many bytes per miss)."""
+        hint = ""
+        if self.opts.get("ld_no_l1"):
+            hint += ".L1::no_allocate"
+        pf = self.opts.get("ld_prefetch")
+        if pf:
+            if int(pf) not in (64, 128, 256):
+                raise Unsupported(f"ld_prefetch must be 64, 128 or 256, not {pf!r}")
+            hint += f".L2::{int(pf)}B"
+        return hint
+
+    def _store_hint(self) -> str:
+        """A cache operator for global stores (opt-in ``st_cop``: ``cs`` streams the line past the
+        caches, ``wt`` writes through)."""
+        cop = self.opts.get("st_cop")
+        if not cop:
+            return ""
+        if cop not in ("cs", "wt", "wb", "cg"):
+            raise Unsupported(f"st_cop must be one of cs, wt, wb, cg, not {cop!r}")
+        return "." + cop
 
     def _unpack(self, word: str, t: str, half: int) -> str:
         """One 16-bit float of a packed word, widened to f32 (exact)."""
@@ -831,6 +857,8 @@ class KernelEmitter:
                 self.b.emit(f"st.{space}.f64 {self.addr(base, imm)}, {d};")
             return
         esize = dt_bytes(t)
+        if not shared:
+            space += self._store_hint()
         for first, cnt in self._vec_plan(lin, len(values), esize, out, shared):
             base, imm = addr_fn(out, lin + first, esize)
             if not shared and cnt * esize == 32:

@@ -20,19 +20,24 @@ F16_MAX_BF16_BITS = 0x477F
 
 
 def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16", "__vflag"),
-                bh_range: tuple[int, int] | None = None, ctas: int | None = None) -> dict:
+                bh_range: tuple[int, int] | None = None, ctas: int | None = None,
+                block_rows: int = BLOCK_ROWS) -> dict:
     """The pre-pass entry; ``bh_range`` = (first, count) converts only those flattened (batch, head)
     pairs (their blocks and flags sit at the same places as in a whole-tensor launch).  ``ctas``
     caps the grid: each CTA then strides over the blocks, which keeps the launch to one CTA per SM
-    when it shares the GPU with a concurrent kernel."""
-    if seq % BLOCK_ROWS:
-        raise ValueError("the value pre-pass needs S % 64 == 0")
+    when it shares the GPU with a concurrent kernel.  ``block_rows`` is the attention kernel's key /
+    value block (64, or 128 for the 128-row kernel): one CTA and one flag per block."""
+    if block_rows not in (64, 128):
+        raise ValueError("the value pre-pass converts 64- or 128-row blocks")
+    if seq % block_rows:
+        raise ValueError(f"the value pre-pass needs S % {block_rows} == 0")
+    block_bytes = block_rows * D * 2
     bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
     if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):
         raise ValueError(f"bh_range {bh_range} outside the {batch * heads} (batch, head) pairs")
-    blocks = nbh * (seq // BLOCK_ROWS)
-    first = bh0 * (seq // BLOCK_ROWS)
-    vec = BLOCK_BYTES // 16 // THREADS      # 16-byte vectors per thread
+    blocks = nbh * (seq // block_rows)
+    first = bh0 * (seq // block_rows)
+    vec = block_bytes // 16 // THREADS      # 16-byte vectors per thread
     grid = blocks if not ctas else min(blocks, int(ctas))
     a = Asm()
     tid, blk = a.r(), a.r()
@@ -51,7 +56,7 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
         a(f"setp.ge.u32 {pend}, {blk}, {first + blocks};")
         a(f"@{pend} bra {l_done};")
     off = a.r("rd")
-    a(f"mul.wide.u32 {off}, {blk}, {BLOCK_BYTES};")
+    a(f"mul.wide.u32 {off}, {blk}, {block_bytes};")
     t16 = a.r("rd")
     a(f"mul.wide.u32 {t16}, {tid}, 16;")
     a(f"add.s64 {off}, {off}, {t16};")
@@ -103,5 +108,5 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
         "grid": [grid, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": 0,
         "align": {vn: 16, v16n: 16, fn: 4}, "zero_outputs": [],
         "scratch": [{"name": v16n, "dtype": "f16", "shape": [batch, heads, seq, D]},
-                    {"name": fn, "dtype": "i32", "shape": [batch * heads * (seq // BLOCK_ROWS)]}],
+                    {"name": fn, "dtype": "i32", "shape": [batch * heads * (seq // block_rows)]}],
     }

@@ -388,6 +388,20 @@ def try_lower(graph, node, kmeta, prefix, options):
                   defer_sum=bool(options.get("attn_defer_sum", False)),
                   prefetch_next=int(options.get("attn_prefetch_next", 0)),
                   pack_in_turn=bool(options.get("attn_pack_in_turn", False)))
+        if options.get("attn_kv128", False):
+            # 128-row key/value blocks: QK^T bound by the tensor core instead of shared memory
+            from .kernels import tc_attention_kv128 as t128, vconv
+            scratch = (f"{prefix}{name}__v16", f"{prefix}{name}__vflag")
+            att = t128.attention_kv128_entry(name, bt, hd, seq, causal, scale,
+                                             names=(Q.name, K.name, V.name, O.name), prefix=prefix,
+                                             half=half, pingpong=bool(options.get("attn_pingpong", True)),
+                                             ordered=bool(options.get("attn_ordered", False)),
+                                             pack_in_turn=bool(options.get("attn_pack_in_turn", False)),
+                                             scratch_names=scratch if half else None)
+            if not half:
+                return att
+            return [vconv.vconv_entry(f"{name}_vconv", bt, hd, seq, names=(V.name,) + scratch,
+                                      block_rows=t128.BKV), att]
         if options.get("attn_persistent", False):
             # opt-in persistent schedule (one CTA per SM, alternating row halves; see the module)
             from .kernels import tc_attention_persistent as tap, vconv

@@ -423,7 +423,7 @@ class Emulator:
                 smem[dst:dst + size] = mem.load(src, size)
                 continue
             if op.startswith(("cp.async.commit", "cp.async.wait", "fence", "membar", "griddepcontrol",
-                              "prefetch")):
+                              "prefetch", "setmaxnreg")):
                 continue
             r = self._extra(th, x, op, ops, regs, val, addr, smem, mem)
             if r is not None:

@@ -28,6 +28,10 @@ ATTN_VARIANTS = {
     "f16-int4": {"attn_f16_int": 4},
     "no-turns": {"attn_pingpong": False},
     "bf16-pairs": {"attn_half": False},
+    "kv128": {"attn_kv128": True},
+    "kv128-ordered": {"attn_kv128": True, "attn_ordered": True},
+    "kv128-bf16-pairs": {"attn_kv128": True, "attn_half": False},
+    "kv128-pack-in-turn": {"attn_kv128": True, "attn_pack_in_turn": True},
 }
 
 
@@ -64,6 +68,12 @@ def test_full_softmax_fast_math_options():
     for opts in ({}, {"approx_ftz": True, "fast_div": True}):
         got, _ = _run_ours(p, t, **opts)
         compare(got["y"], want, "f32", 1e-5, f"c1 recip {opts}")
+
+
+@pytest.mark.parametrize("opts", [{"attn_kv128": True}, {"attn_kv128": True, "attn_ordered": True}])
+def test_full_attention_kv128_sampled(opts):
+    """Config 5 at full size through the 128-row key/value block kernel; sampled heads against float64."""
+    full_attention_check(opts)
 
 
 def test_full_attention_persistent_sampled():
