@@ -75,7 +75,7 @@ def build_problem(key: str, units: int | None = None, **kw):
     if units is None:
         return irgen.FULL[key](**kw)
     return {
-        "c1": lambda: irgen.softmax_ir(units, 1024, **kw),
+        "c1": lambda: irgen.softmax_ir(units, 1024, **{"recip": True, **kw}),
         "c2": lambda: irgen.sum_ir(units, "f32", **kw),
         "c2i": lambda: irgen.sum_ir(units, "i32", **kw),
         "c3": lambda: irgen.fused_ir(units, 8192, **kw),
@@ -87,7 +87,7 @@ def build_problem(key: str, units: int | None = None, **kw):
 def _small_for_profile():
     from emmy_ptx_b200 import irgen
     return {
-        "c1": lambda **kw: irgen.softmax_ir(4096, 1024, **kw),
+        "c1": lambda **kw: irgen.softmax_ir(4096, 1024, **{"recip": True, **kw}),
         "c2": lambda **kw: irgen.sum_ir(1 << 26, "f32", **kw),
         "c2i": lambda **kw: irgen.sum_ir(1 << 26, "i32", **kw),
         "c3": lambda **kw: irgen.fused_ir(4096, 8192, **kw),
