@@ -598,9 +598,9 @@ def log_sum_exp(a=2, b=32, c=64):
 
 
 def matmul_odd(m=33, k=65, n=17):
-    """C = A @ B for odd sizes, a thread per output cell with a rolled Loop over k: the shape the
-    tensor-core lowering declines (no dimension is a multiple of its tile), so it stays on the CUDA
-    cores.  Held to the matmul tolerance."""
+    """C = A @ B for odd sizes, a thread per output cell with a rolled Loop over k: f32 operands and
+    a K of 65 (not a multiple of 8, so A's rows are no whole number of 16-byte TMA units), which the
+    tensor-core lowering declines, so it stays on the CUDA cores.  Held to the matmul tolerance."""
     body = [Tile([Axis("i", m), Axis("j", n)], [
         Loop("kk", k, [
             Load(["a"], "A", [V("i"), V("kk")], "f32"),
@@ -614,6 +614,20 @@ def matmul_odd(m=33, k=65, n=17):
             TensorSpec("C", (m, n), "f32", output=True)]
     return _problem("matmul", f"matmul_{m}x{k}x{n}", "matmul_odd", args, body, (m * n + 127) // 128, 128,
                     rtol=1e-4, contraction=True)
+
+
+def bmm_small(batch=2, m=32, n=32, k=64):
+    """C = A @ B for [2, 32, 64] x [2, 64, 32] bf16 (the small batched matmul of the reference's
+    cases): the unscheduled nest, a thread per output element.  Far below one 128 x 256 tile, it
+    runs on the tensor cores as a single edge tile (TMA zero-fills the box past M, N and the store
+    keeps rows below M and columns below N)."""
+    from .irgen import bmm_naive_ir
+    base = bmm_naive_ir(batch, m, n, k)
+    args = [TensorSpec("A", (batch, m, k), "bf16", ("normal", 1.0)),
+            TensorSpec("B", (batch, k, n), "bf16", ("normal", 1.0)),
+            TensorSpec("C", (batch, m, n), "f32", output=True)]
+    return Problem(f"bmm_small_{batch}x{m}x{n}x{k}", "corpus", base.entry, base.graph, args, grid=base.grid,
+                   block=base.block, rtol=1e-4, atol=1e-6, params={"expr": "matmul", "contraction": True})
 
 
 def scan_max_and_prod(rows=4, cols=64):
@@ -909,4 +923,5 @@ CORPUS = {
     "k_elu_selu": elu_selu,
     "k_any": row_any,
     "k_l2norm": l2_normalize,
+    "k_bmm_small": bmm_small,
 }

@@ -47,13 +47,25 @@ ERR_DRAIN = 5
 from .ptxasm import Asm, idesc_f16, smem_desc_hi, wait_bar as _wait, wait_bar_warp as _wait_warp
 
 
+def supported(m: int, n: int, k: int) -> bool:
+    """Whether the tcgen05 GEMM takes these shapes: any M; N and K multiples of 8, so that the
+    row strides of A (K bf16) and B (N bf16) are whole 16-byte units as TMA requires, and C's f32
+    rows split into whole 32-byte stores."""
+    return m >= 1 and n >= 8 and k >= 8 and n % 8 == 0 and k % 8 == 0
+
+
 def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
                names=("A", "B", "C"), prefix: str = "") -> dict:
     """The build record (module writer format) of the tcgen05 GEMM for these shapes; ``names`` are
-    the IR buffer names of X, Y and the output (the kernel's parameters, in that order)."""
-    if m % BM or n % BN or k % BK:
-        raise ValueError("tcgen05 GEMM needs M % 128, N % 256, K % 64 == 0")
-    mt, nt, nk = m // BM, n // BN, k // BK
+    the IR buffer names of X, Y and the output (the kernel's parameters, in that order).
+
+    Shapes that are not tile multiples run as edge tiles: TMA fills the parts of an A or B box past
+    the tensor's end with zeros (their products add nothing, in K too), and the epilogue stores only
+    the rows below M and the 8-column groups below N."""
+    if not supported(m, n, k):
+        raise ValueError("tcgen05 GEMM needs N % 8 == 0 and K % 8 == 0")
+    mt, nt, nk = -(-m // BM), -(-n // BN), -(-k // BK)
+    edge_m, edge_n = m % BM != 0, n % BN != 0
     tiles = batch * mt * nt
     grid = min(tiles, sms)
     a = Asm()
@@ -311,9 +323,14 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
     a("tcgen05.fence::after_thread_sync;")
     # this thread's output row: C + ((b*M + m0 + 32q + lane) * N + n0) * 4
     row, rowaddr = a.r(), a.r("rd")
-    a(f"mad.lo.u32 {row}, {ebb}, {m}, {emm};")
-    a(f"mad.lo.u32 {row}, {q}, 32, {row};")
-    a(f"add.u32 {row}, {row}, {lane};")
+    rin = a.r()
+    a(f"mad.lo.u32 {rin}, {q}, 32, {emm};")
+    a(f"add.u32 {rin}, {rin}, {lane};")                # row within the batch
+    prow = None
+    if edge_m:
+        prow = a.r("p")
+        a(f"setp.lt.u32 {prow}, {rin}, {m};")          # rows past M belong to no output
+    a(f"mad.lo.u32 {row}, {ebb}, {m}, {rin};")
     tmp64 = a.r("rd")
     a(f"mul.wide.u32 {rowaddr}, {row}, {n * 4};")
     a(f"mul.wide.u32 {tmp64}, {enn}, 4;")
@@ -328,7 +345,20 @@ def gemm_entry(name: str, batch: int, m: int, n: int, k: int, sms: int = 148,
         a(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{src}];")
         a("tcgen05.wait::ld.sync.aligned;")
         for v in range(4):
-            a(f"st.global.v8.f32 [{rowaddr}+{128 * ch + 32 * v}], {{{', '.join(regs[8 * v:8 * v + 8])}}};")
+            guard = prow
+            if edge_n:
+                # the 8 columns n0 + 32ch + 8v .. +7 are all below N or all past it (N % 8 == 0);
+                # a group past N in the first tile is past N in every tile
+                lim = n - (32 * ch + 8 * v)
+                if lim <= 0:
+                    continue
+                pc = a.r("p")
+                a(f"setp.lt.u32 {pc}, {enn}, {lim};")
+                if prow is not None:
+                    a(f"and.pred {pc}, {pc}, {prow};")
+                guard = pc
+            g = f"@{guard} " if guard else ""
+            a(f"{g}st.global.v8.f32 [{rowaddr}+{128 * ch + 32 * v}], {{{', '.join(regs[8 * v:8 * v + 8])}}};")
     a("tcgen05.fence::before_thread_sync;")
     a("bar.warp.sync -1;")
     pl = a.r("p")

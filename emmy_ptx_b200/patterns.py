@@ -365,7 +365,7 @@ def try_lower(graph, node, kmeta, prefix, options):
     if hit is not None:
         X, Y, C, bt, m, n, k = hit
         from .kernels import tc_gemm
-        if m % tc_gemm.BM or n % tc_gemm.BN or k % tc_gemm.BK:
+        if not tc_gemm.supported(m, n, k):
             return None
         b = tc_gemm.gemm_entry(node.op.name, bt, m, n, k, sms=int(options.get("sms", 148)),
                                names=(X.name, Y.name, C.name), prefix=prefix)

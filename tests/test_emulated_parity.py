@@ -85,9 +85,21 @@ def _problem(key):
     return irgen.SMALL[key]() if key in irgen.SMALL else corpus.CORPUS[key]()
 
 
+def _tensor_core(p) -> bool:
+    return any(r["kind"] != "generic" for r in compile_graph(Graph.from_dict(p.graph), p.meta()).kernels)
+
+
 @pytest.mark.parametrize("key", SMALL_KEYS + CORPUS_KEYS)
 def test_emitted_ptx_matches_oracle(key):
     p = _problem(key)
+    if _tensor_core(p):
+        # a corpus kernel the tensor-core lowering takes runs in the tensor-core emulator
+        from tests.test_tc_emulated import run_emulated
+        t = data.make_inputs(p)
+        got, code, _ = run_emulated(p, t, {})
+        assert code == 0
+        _check(p, t, got, f"tc-emu:{key}")
+        return
     t, got = _run_ours(p)
     _check(p, t, got, f"emu:{key}")
 
@@ -96,7 +108,10 @@ def test_emitted_ptx_matches_oracle(key):
 def test_emitted_ptx_without_shortcuts_matches_oracle(key):
     # per-level tree barriers, no redux, no unrolling: the CUDA-core emitter's plain forms
     p = _problem(key)
-    t, got = _run_ours(p, {"tree_barriers": True, "no_redux": True, "no_unroll": True})
+    opts = {"tree_barriers": True, "no_redux": True, "no_unroll": True}
+    if _tensor_core(p):
+        opts["patterns"] = False             # the CUDA-core form of a tensor-core corpus kernel
+    t, got = _run_ours(p, opts)
     _check(p, t, got, f"emu-plain:{key}")
 
 

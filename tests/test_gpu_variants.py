@@ -9,6 +9,9 @@ import pytest
 import torch
 
 from emmy_ptx_b200 import irgen, data
+from emmy_ptx_b200.compiler import compile_graph
+from emmy_ptx_b200.ir import Graph
+from emmy_ptx_b200.runtime import Executable
 from oracle.run import oracle_outputs
 from tests.checks import compare, rtol_for
 from tests.test_gpu_parity import _run_ours
@@ -89,3 +92,25 @@ def test_gemm_from_the_unscheduled_matmul():
     got, ex = _run_ours(p, t)
     assert ex.records[0]["kind"] == "tcgen05_gemm" and ex.error_code() == 0
     compare(got["C"], want["C"], "f32", rtol_for(p), "bmm naive")
+
+
+@pytest.mark.parametrize("shape", [(2, 200, 264, 72), (1, 130, 8, 16), (3, 1000, 1000, 1000)])
+def test_gemm_edge_tiles(shape):
+    """The tcgen05 GEMM on shapes that are not tile multiples (edge tiles in M, N and K), against
+    float64 with the matmul tolerance; the output is pre-filled with NaN so a row or column the
+    kernel skips, or one it writes past, shows."""
+    p = irgen.bmm_naive_ir(*shape)
+    t = data.make_inputs(p)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    assert mod.kernels[0]["kind"] == "tcgen05_gemm"
+    ex = Executable(mod)
+    td = {k: v.cuda() for k, v in t.items()}
+    b, m, n, _ = shape
+    guard = torch.full((b * m * n + 4096,), float("nan"), dtype=torch.float32, device="cuda")
+    td["C"] = guard[: b * m * n].view(b, m, n)
+    ex(td)
+    torch.cuda.synchronize()
+    assert ex.error_code() == 0
+    assert torch.isnan(guard[b * m * n:]).all(), "the kernel wrote past the output"
+    want = t["A"].double() @ t["B"].double()
+    compare(td["C"].cpu(), want, "f32", 1e-4, f"gemm edge {shape}")

@@ -33,8 +33,12 @@ def test_tile_multiples_select_the_tensor_core_kernel():
                 "cp.async.bulk.tensor.3d", "tcgen05.ld.sync.aligned.32x32b.x32", "mbarrier.try_wait.parity"):
         assert ins in mod.ptx
     assert "multicast" not in mod.ptx
-    small = irgen.SMALL["c4"]()          # N = 128 is not a multiple of the 256-wide tile
-    assert compile_graph(Graph.from_dict(small.graph), small.meta()).kernels[0]["kind"] == "generic"
+    small = irgen.SMALL["c4"]()          # N = 128, half of the 256-wide tile: one edge tile in N
+    assert compile_graph(Graph.from_dict(small.graph), small.meta()).kernels[0]["kind"] == "tcgen05_gemm"
+    odd_k = irgen.bmm_naive_ir(1, 64, 64, 36)     # K % 8 != 0: A's rows are no whole 16-byte TMA units
+    assert compile_graph(Graph.from_dict(odd_k.graph), odd_k.meta()).kernels[0]["kind"] == "generic"
+    odd_n = irgen.bmm_naive_ir(1, 64, 20, 64)     # N % 8 != 0: B's rows likewise
+    assert compile_graph(Graph.from_dict(odd_n.graph), odd_n.meta()).kernels[0]["kind"] == "generic"
 
 
 def test_swapped_contraction_axis_is_refused():
@@ -197,13 +201,17 @@ def test_renamed_buffers_still_match():
 
 
 def test_unscheduled_matmul_reaches_the_tensor_cores():
-    # a thread per output element with a rolled k loop is the same contraction: at tile multiples it
-    # takes the tcgen05 GEMM; at other shapes, or with a transposed store, it stays on the CUDA cores
+    # a thread per output element with a rolled k loop is the same contraction: it takes the tcgen05
+    # GEMM (edge tiles where M or N is not a tile multiple); with K % 8 != 0, or a transposed store,
+    # it stays on the CUDA cores
     p = irgen.bmm_naive_ir(1, 128, 256, 64)
     g, k = _kernel(p)
     assert match_bmm(g, k) is not None
     assert compile_graph(g, p.meta()).kernels[0]["kind"] == "tcgen05_gemm"
-    odd = irgen.bmm_naive_ir(1, 100, 256, 64)
+    edge = irgen.bmm_naive_ir(1, 100, 256, 64)
+    g1, _ = _kernel(edge)
+    assert compile_graph(g1, edge.meta()).kernels[0]["kind"] == "tcgen05_gemm"
+    odd = irgen.bmm_naive_ir(1, 100, 256, 60)
     g2, k2 = _kernel(odd)
     assert compile_graph(g2, odd.meta()).kernels[0]["kind"] == "generic"
 

@@ -147,6 +147,14 @@ def test_late_completions_expose_a_planted_early_release():
         _check(p, t, {}, "tcgen05_attention", defer=True, mod=CompiledModule(bad, mod.kernels))
 
 
+@pytest.mark.parametrize("shape", [(2, 32, 32, 64), (1, 200, 264, 72), (1, 130, 8, 16), (2, 128, 128, 96)])
+def test_gemm_edge_tiles_emulated(shape):
+    """Shapes that are not tile multiples: TMA zero-fills past M, N and K, the epilogue stores rows
+    below M and 8-column groups below N (a store past the output would raise in the emulator)."""
+    p = irgen.bmm_naive_ir(*shape)
+    _check(p, data.make_inputs(p), {}, "tcgen05_gemm")
+
+
 def test_gemm_from_the_unscheduled_matmul_emulated():
     # the thread-per-element matmul nest lowered to the tcgen05 GEMM; the oracle interprets the nest
     p = irgen.bmm_naive_ir(1, 128, 256, 64)
