@@ -36,6 +36,17 @@ class Unsupported(IRError):
     """The IR uses a construct this backend refuses (the reference raises SystemExit too)."""
 
 
+class TmaNotProvable(Exception):
+    """A promoted stripe's TMA alignment could not be proved: the kernel is built again with
+    ``cp.async`` (``tma_stripes=False``)."""
+
+
+TMA_BARS = "__tmabar"                # the shared mbarriers of the promoted commit groups
+TMA_WAIT_LIMIT = 40000               # bounded try_wait polls with a 0.1 ms hint: < ~4 s
+TMA_WAIT_HINT_NS = 100000
+ERR_TMA_WAIT = 41                    # status word: a commit group's TMA loads never completed
+
+
 class Sym:
     """A bound IR value: ``f32`` (operand string), ``pred`` (register) or ``s32`` (Affine)."""
 
@@ -100,6 +111,13 @@ class KernelEmitter:
         self.G = int(grid[0]) if grid else None
         if grid and len(grid) > 1 and any(int(x) != 1 for x in grid[1:]):
             self.G = None
+        self.tma = None
+        if self.opts.get("tma_stripes", True) is not False and self.T:
+            from . import tma_stripes
+            self.tma = tma_stripes.plan(self.op.body, self.T, self.shapes, self.dtypes, self.smem)
+            if self.tma is not None:
+                # one 8-byte mbarrier per commit group that can be in flight
+                self.smem[TMA_BARS] = ((2 * self.tma["nbar"],), "i32", 16)
         self._plan_smem()
 
     def _scan(self, body) -> None:
@@ -185,6 +203,8 @@ class KernelEmitter:
             else:
                 b.emit(f"mov.u32 {r}, {self.sym_name(name)};")
             self.sbase[name] = r
+        if self.tma is not None:
+            self._tma_prologue(tid)
 
     # ---- integers -------------------------------------------------------------------------
     def mat(self, aff) -> str:
@@ -1022,8 +1042,81 @@ class KernelEmitter:
         else:
             self.b.emit(f"bar.sync {int(getattr(st, 'barrier_id', 0) or 0)};")
 
+    # ---- CpAsyncCopy stripes promoted to TMA (codegen/tma_stripes.py) ------------------------
+    def _tma_prologue(self, tid: str) -> None:
+        """Tensor-map parameter addresses, the status word, the commit groups' mbarriers (thread 0
+        initialises them; one block barrier publishes the initialisation) and the group counter."""
+        b = self.b
+        self.tma_regs = []
+        for spec in self.tma["tmaps"]:
+            r = b.reg("b64")
+            b.emit(f"mov.u64 {r}, p_{spec['name']};")
+            b.emit(f"cvta.param.u64 {r}, {r};")
+            self.tma_regs.append(r)
+        self.err = b.reg("b64")
+        b.emit(f"ld.param.u64 {self.err}, [p_err];")
+        b.emit(f"cvta.to.global.u64 {self.err}, {self.err};")
+        self.t0 = b.reg("pred")
+        b.emit(f"setp.eq.u32 {self.t0}, {tid}, 0;")
+        skip = b.label("_tmainit")
+        b.emit(f"@!{self.t0} bra {skip};")
+        bars = self.sbase[TMA_BARS]
+        for i in range(self.tma["nbar"]):
+            b.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * i}], 1;")
+        b.emit("fence.mbarrier_init.release.cluster;")
+        b.place(skip)
+        b.emit("bar.sync 0;")
+        self.grp = b.reg("b32")
+        b.emit(f"mov.u32 {self.grp}, 0;")
+
+    def _tma_bar(self, group: str) -> str:
+        """The shared address of the mbarrier of commit group ``group`` (a register)."""
+        b = self.b
+        slot, bar = b.reg("b32"), b.reg("b32")
+        b.emit(f"rem.u32 {slot}, {group}, {self.tma['nbar']};")
+        b.emit(f"mad.lo.u32 {bar}, {slot}, 8, {self.sbase[TMA_BARS]};")
+        return bar
+
+    def _reg32(self, aff) -> str:
+        m = self.mat(aff)
+        if m.startswith("%"):
+            return m
+        r = self.b.reg("b32")
+        self.b.emit(f"mov.b32 {r}, {m};")
+        return r
+
+    def _tma_copy(self, st, sp) -> None:
+        """One TMA tile load of the whole stripe, issued by thread 0 into the current group's
+        mbarrier: the box origin is the source index less the lane's (row, col), the destination
+        the stripe's shared base.  TMA wants the origin's innermost coordinate and the shared
+        address on 16-byte boundaries; both are proved here or the kernel is built without TMA."""
+        b = self.b
+        es = sp.elem_bytes
+        unit = 16 // es
+        lin = self.linear(st.smem, st.smem_index)
+        idx = [self.ival(x) for x in st.src_index]
+        idx[-2] = recombine(idx[-2] - self.ival(st.lane_index[0]))
+        idx[-1] = recombine(idx[-1] - self.ival(st.lane_index[1]))
+        if not lin.divisible_by(unit) or not idx[-1].divisible_by(unit) or self.smem_off[st.smem] % 16:
+            raise TmaNotProvable(f"cannot prove the 16-byte alignment of the {st.src!r} stripe")
+        coords = [self._reg32(c) for c in reversed(idx)]
+        base, imm = self.shared_addr(st.smem, lin, es)
+        dst = b.reg("b32")
+        b.emit(f"add.u32 {dst}, {base}, {imm};")
+        bar = self._tma_bar(self.grp)
+        rank = len(idx)
+        t0 = self.t0
+        b.emit(f"@{t0} fence.proxy.async.shared::cta;")
+        b.emit(f"@{t0} mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [{bar}], {sp.box_bytes};")
+        b.emit(f"@{t0} cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+               f"[{dst}], [{self.tma_regs[sp.tmap]}, {{{', '.join(coords)}}}], [{bar}];")
+
     def st_CpAsyncCopy(self, st) -> None:
-        """compile.py:1449-1471: stripe base plus the lane's (row, col); 16 B ``.cg``, 4/8 B ``.ca``."""
+        """compile.py:1449-1471: stripe base plus the lane's (row, col); 16 B ``.cg``, 4/8 B ``.ca``.
+        A kernel whose stripes each form one dense box issues them as TMA tile loads instead."""
+        if self.tma is not None:
+            self._tma_copy(st, self.tma["copies"][id(st)])
+            return
         if str(getattr(st, "swizzle", "NONE") or "NONE").upper() != "NONE":
             raise Unsupported(f"unsupported cp.async swizzle {st.swizzle}")
         if getattr(st, "valid", None) is not None:
@@ -1045,10 +1138,40 @@ class KernelEmitter:
             raise Unsupported(f"unsupported cp.async size {nbytes}")
 
     def st_CpAsyncCommit(self, st) -> None:
+        if self.tma is not None:
+            # thread 0's arrival closes the group: its mbarrier phase completes once every TMA byte
+            # of the group has landed (at once for a group that issued no copy)
+            bar = self._tma_bar(self.grp)
+            self.b.emit(f"@{self.t0} mbarrier.arrive.shared::cta.b64 _, [{bar}];")
+            self.b.emit(f"add.u32 {self.grp}, {self.grp}, 1;")
+            return
         self.b.emit("cp.async.commit_group;")
 
     def st_CpAsyncWait(self, st) -> None:
-        self.b.emit(f"cp.async.wait_group {int(getattr(st, 'group', 0) or 0)};")
+        n = int(getattr(st, "group", 0) or 0)
+        if self.tma is None:
+            self.b.emit(f"cp.async.wait_group {n};")
+            return
+        # every thread waits (bounded) for group g = committed - 1 - n: its mbarrier's phase g / nbar
+        b = self.b
+        g, ph, cnt = b.reg("b32"), b.reg("b32"), b.reg("b32")
+        pz, pw, pq = b.reg("pred"), b.reg("pred"), b.reg("pred")
+        done, top = b.label("_tmaw"), b.label("_tmawl")
+        b.emit(f"sub.s32 {g}, {self.grp}, {n + 1};")
+        b.emit(f"setp.lt.s32 {pz}, {g}, 0;")
+        b.emit(f"@{pz} bra {done};")
+        bar = self._tma_bar(g)
+        b.emit(f"div.u32 {ph}, {g}, {self.tma['nbar']};")
+        b.emit(f"and.b32 {ph}, {ph}, 1;")
+        b.emit(f"mov.u32 {cnt}, 0;")
+        b.place(top)
+        b.emit(f"mbarrier.try_wait.parity.shared::cta.b64 {pw}, [{bar}], {ph}, {TMA_WAIT_HINT_NS};")
+        b.emit(f"@{pw} bra {done};")
+        b.emit(f"add.u32 {cnt}, {cnt}, 1;")
+        b.emit(f"setp.lt.u32 {pq}, {cnt}, {TMA_WAIT_LIMIT};")
+        b.emit(f"@{pq} bra {top};")
+        b.emit(f"st.global.u32 [{self.err}], {ERR_TMA_WAIT};")
+        b.place(done)
 
     def st_ZeroPrologue(self, st) -> None:
         """compile.py:1401-1447: the whole grid zeroes ``words`` 32-bit words, grid stride."""
@@ -1376,4 +1499,6 @@ class KernelEmitter:
             "align": dict(self.palign),
             "zero_outputs": list(self.kmeta.get("zero_outputs") or []),
             "pdl": self.pdl,
+            **({"tmaps": self.tma["tmaps"], "extra": [{"name": "__err", "kind": "errword"}]}
+               if self.tma is not None else {}),
         }

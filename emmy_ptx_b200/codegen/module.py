@@ -58,6 +58,10 @@ def entry_text(b: dict) -> list[str]:
     if b.get("raw_entry"):
         return [MARK + json.dumps(launch_record(b), sort_keys=True)] + b["raw_entry"]
     params = [f"\t.param .u64 p_{n}" for n in b["params"]]
+    # extension of the reference's ABI for promoted stripes: the TMA descriptors after arg_order, then
+    # the status word the bounded waits write
+    params += [f"\t.param .align 64 .b8 p_{spec['name']}[128]" for spec in b.get("tmaps") or []]
+    params += ["\t.param .u64 p_err" for spec in b.get("extra") or [] if spec.get("kind") == "errword"]
     out = [MARK + json.dumps(launch_record(b), sort_keys=True)]
     out.append(f".visible .entry {b['name']}(\n" + ",\n".join(params) + "\n)")
     if b.get("reqntid"):

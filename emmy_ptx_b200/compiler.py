@@ -14,7 +14,7 @@ from dataclasses import dataclass, field
 from pathlib import Path
 
 from .ir import Graph, IRError, load_graph, read_meta, kernel_meta
-from .codegen.generic import KernelEmitter, Unsupported
+from .codegen.generic import KernelEmitter, TmaNotProvable, Unsupported
 from .codegen import module as modwriter
 
 
@@ -55,7 +55,11 @@ def compile_graph(graph: Graph, meta: dict | None = None, options: dict | None =
             from . import patterns
             b = patterns.try_lower(graph, node, km, prefix, options)
         if b is None:
-            b = KernelEmitter(graph, node, km, prefix, options).build()
+            try:
+                b = KernelEmitter(graph, node, km, prefix, options).build()
+            except TmaNotProvable:
+                # the stripes' TMA alignment is not provable: the same kernel with cp.async
+                b = KernelEmitter(graph, node, km, prefix, {**options, "tma_stripes": False}).build()
         # a lowering may emit several entries for one KernelOp (a pre-pass before the main kernel)
         built.extend(b if isinstance(b, list) else [b])
     text = modwriter.module_text(built)

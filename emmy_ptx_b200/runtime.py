@@ -19,7 +19,7 @@ from .compiler import CompiledModule, compile_ir
 from .launcher import Device
 from .data import torch_dtype
 
-_TMAP_DTYPE = {"u8": 0, "f16": 6, "f32": 7, "bf16": 9}   # CUtensorMapDataType (cuda.h)
+_TMAP_DTYPE = {"u8": 0, "u32": 2, "i32": 3, "f16": 6, "f32": 7, "f64": 8, "bf16": 9}   # CUtensorMapDataType (cuda.h)
 _SWIZZLE = {"none": 0, "32B": 1, "64B": 2, "128B": 3}
 
 

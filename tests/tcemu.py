@@ -129,6 +129,10 @@ class TcEmulator(Emulator):
             th.state = "mbar"
             self.mbar_waiters.setdefault(a, []).append(th)
             return "block"
+        if op.startswith("mbarrier.expect_tx"):
+            a = addr(ops[0]) & _M32
+            self.mbars[a].tx += val(ops[1])
+            return "cont"
         if op.startswith("mbarrier.arrive.expect_tx"):
             a = addr(ops[1]) & _M32
             self.mbars[a].tx += val(ops[2])

@@ -17,6 +17,7 @@ from emmy_ptx_b200.ir import Graph
 from oracle.run import oracle_outputs
 from tests.checks import atol_for, compare, rms_floor_for, rtol_for
 from tests.ptxemu import Emulator, Memory
+from tests.tcemu import TcEmulator
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 SMALL_KEYS = ["c1", "c1b", "c1w", "c2", "c2i", "c2odd", "c3"]
@@ -60,8 +61,19 @@ def _run_ours(p, opts=None):
     t, mem, addr = _setup(p)
     for rec in mod.kernels:
         _zero(mem, addr, rec.get("zero_outputs", []))
-        Emulator(mod.ptx, rec["entry"]).run(rec["grid"][0], rec["block"][0],
-                                            {f"p_{n}": addr[n] for n in rec["params"]}, mem, rec.get("dyn_smem", 0))
+        args = {f"p_{n}": addr[n] for n in rec["params"]}
+        if rec.get("tmaps"):
+            # CpAsyncCopy stripes promoted to TMA: the tensor-core emulator runs the TMA loads and
+            # the commit groups' mbarriers
+            tm = {f"p_{spec['name']}": (addr[spec["tensor"]], spec) for spec in rec["tmaps"]}
+            emu = TcEmulator(mod.ptx, rec["entry"], tm)
+            args.update(emu.tmap_args())
+            err = mem.alloc(np.zeros(16, np.uint8))
+            args["p_err"] = err
+            emu.run(rec["grid"][0], rec["block"][0], args, mem, rec.get("dyn_smem", 0))
+            assert int(mem.array(err, np.int32, (4,))[0]) == 0, "a commit group's wait timed out"
+        else:
+            Emulator(mod.ptx, rec["entry"]).run(rec["grid"][0], rec["block"][0], args, mem, rec.get("dyn_smem", 0))
     return t, _outputs(p, t, mem, addr)
 
 

@@ -114,3 +114,20 @@ def test_gemm_edge_tiles(shape):
     assert torch.isnan(guard[b * m * n:]).all(), "the kernel wrote past the output"
     want = t["A"].double() @ t["B"].double()
     compare(td["C"].cpu(), want, "f32", 1e-4, f"gemm edge {shape}")
+
+
+@pytest.mark.parametrize("tma", [True, False])
+def test_cuda_core_bmm_stripes(tma):
+    """The CUDA-core batched matmul (tensor-core lowering off) with its operand stripes as TMA tile
+    loads on mbarriers, and with the per-thread cp.async they replace, against float64."""
+    p = irgen.bmm_ir(2, 512, 256, 384)
+    t = data.make_inputs(p)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"patterns": False, "tma_stripes": tma})
+    assert ("cp.async.bulk.tensor" in mod.ptx) == tma
+    ex = Executable(mod)
+    td = {k: v.cuda() for k, v in t.items()}
+    td["C"].fill_(float("nan"))
+    ex(td)
+    torch.cuda.synchronize()
+    assert ex.error_code() == 0
+    compare(td["C"].cpu(), t["A"].double() @ t["B"].double(), "f32", 1e-4, f"cuda-core bmm tma={tma}")
