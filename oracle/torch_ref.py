@@ -195,6 +195,7 @@ CORPUS = {
     "scanprod": lambda t, p: {"cm": __import__("torch").cummax(t["x"].double(), -1).values,
                               "pr": t["x"].double().prod(-1)},
     # torch's posinf / neginf defaults for a float32 tensor: the largest finite f32 and its negative
+    "sdpa": lambda t, p: {"O": attention(t["Q"], t["K"], t["V"], p["causal"], p["scale"])},
     "nan_to_num": lambda t, p: {"y": __import__("torch").nan_to_num(t["x"]).double()},
     "logaddexp": lambda t, p: {"y": __import__("torch").logaddexp(t["a"].double(), t["b"].double())},
     "elu_selu": lambda t, p: {"elu": __import__("torch").nn.functional.elu(t["x"].double()),

@@ -39,7 +39,7 @@ def rtol_for(problem) -> float:
 
 
 def rms_floor_for(problem) -> bool:
-    return problem.family == "attention"
+    return problem.family == "attention" or bool(problem.params.get("attention"))
 
 
 def compare(got: torch.Tensor, ref: torch.Tensor, dtype: str, rtol: float, what: str = "",
