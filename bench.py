@@ -5,7 +5,8 @@
                     [--impl ours|reference] [--scaling strong|weak]
 
 A *step* is one pass of the hot path over one batch of synthetic input: the compiled kernel(s) of a
-configuration (plus, for the full-array sum at N > 1, the ncclAllReduce of the per-GPU partial).
+configuration (plus, for the full-array sum at N > 1, the exchange of the per-GPU partials: the
+peer-exchange kernel over NVLink by default, or one ncclAllReduce with ``--exchange nccl``).
 By default one run measures all six configurations one after another in one process and prints
 ONE JSON line (rank 0): the headline fields are config 2's — the f32 sum of 2**28 elements, metric
 HBM GB/s — and ``per_config`` holds every configuration's own record.
@@ -421,6 +422,9 @@ def parse(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="strong: the ranks share one global problem; weak: every rank runs a full-size one")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="how the sum's partials combine at N>1: the peer-exchange kernel over NVLink (falls back "
+                         "to NCCL when the ranks cannot map each other's memory) or one ncclAllReduce")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-emitter", action="store_true")
@@ -741,7 +745,18 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
     sets = make_sets(key, p, p_global, rotate, world, rank, "strong" if strong else "weak", lo, hi)
 
     collective = p.family == "sum" and world > 1
-    allreduce = edist.AllReducePartials(dev, dist, rank, world) if collective else None
+    allreduce, exchange = None, None
+    if collective:
+        if args.exchange == "peer":
+            try:
+                allreduce = edist.PeerAllReduce(dev, dist, rank, world, p.params["dtype"])
+                exchange = "peer (NVLink exchange kernel)"
+            except RuntimeError as exc:         # the same on every rank (the set-up agrees)
+                exchange = f"nccl (peer exchange unavailable: {exc})"
+        if allreduce is None:
+            allreduce = edist.AllReducePartials(dev, dist, rank, world)
+            exchange = exchange or "nccl"
+    nccl_in_step = collective and isinstance(allreduce, edist.AllReducePartials)
     try:
         def step(t, s=None):
             s = stream if s is None else s
@@ -758,7 +773,7 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
         reps = args.steps if units * 1.0 > 1e11 or kind == "FLOP" else max(args.steps, 200)
         graphs = use_graphs(world, args.no_graph)
         step_graph = graph_of(lambda s: [step(sets[i % rotate], s) for i in range(args.steps)],
-                              capture=capture_steps(collective, args.no_graph, world))
+                              capture=capture_steps(nccl_in_step, args.no_graph, world))
         kern_graph = graph_of(lambda s: [ex.run(sets[i % rotate], s, zero=False) for i in range(reps)],
                               capture=graphs)
         t_timed0 = time.time()
@@ -786,7 +801,8 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
         check["tolerance"] = tol
         check["ok"] = ok
         bad = int(max_over_ranks(dist, 0.0 if ok else 1.0))
-        code = int(max_over_ranks(dist, float(ex.error_code())))
+        code = int(max_over_ranks(dist, float(max(ex.error_code(),
+                                                  allreduce.error_code() if hasattr(allreduce, "error_code") else 0))))
         if code:
             raise KernelTimedOut(f"{key}: kernel status word {code}: a pipeline wait timed out")
         if bad:
@@ -876,20 +892,21 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
         "metric": f"{desc} {metric}", "value": value, "unit": unit, "ms_per_step": ms_step, "dtype": p.args[0].dtype,
         "config": {"workload": key, "description": desc, "per_rank_units": units, "global_units": g_units,
                    "unit_kind": kind,
-                   "parallelism": f"dp{world} ({'sharded + ncclAllReduce of the partial' if collective else 'sharded, no collective'})",
+                   "parallelism": f"dp{world} ({'sharded + ' + exchange + ' of the partial' if collective else 'sharded, no collective'})",
                    "shard": ([lo, hi] if strong else None),
                    "l2": ("inputs exceed L2 (126 MB)" if rotate == 1 else f"{rotate} rotating buffer sets exceed 2x L2"),
                    "grid": p.grid, "block": p.block, **({"compile_options": options} if options else {}),
                    **({"ir_options": ir_kw} if ir_kw else {})},
         "gpu_launches": args.steps * len(mod.kernels),
-        "timing": ("CUDA graph replay of the K steps" if capture_steps(collective, args.no_graph, world)
-                   else "host launches (kernel + ncclAllReduce per step)" if collective else "host launches"),
+        "timing": ("CUDA graph replay of the K steps" if capture_steps(nccl_in_step, args.no_graph, world)
+                   else "host launches (kernel + ncclAllReduce per step)" if nccl_in_step else "host launches"),
         "roofline": roof, "ref_emitter": ref, "cpu_baseline": cpu, "cpu_port": port, "e2e": e2e,
         "check": check, "kernel_kind": mod.kernels[-1].get("kind"),
         "clocks_window": [t_timed0, t_timed1], "wall_s": t_end - t_start,
     }
     if allreduce_ms is not None:
-        rec["allreduce_ms"] = allreduce_ms
+        rec["exchange"] = exchange
+        rec["exchange_ms"] = allreduce_ms
         rec["kernel_ms"] = kern_ms
     return rec
 

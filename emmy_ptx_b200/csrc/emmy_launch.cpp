@@ -67,6 +67,9 @@ struct Driver {
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
   CUresult (*GetErrorString)(CUresult, const char**);
+  CUresult (*IpcGetMemHandle)(CUipcMemHandle*, CUdeviceptr);
+  CUresult (*IpcOpenMemHandle)(CUdeviceptr*, CUipcMemHandle, unsigned int);
+  CUresult (*IpcCloseMemHandle)(CUdeviceptr);
 };
 
 Driver g_drv;
@@ -120,7 +123,10 @@ int load_driver() {
             sym(lib, d.MemcpyHtoDAsync, "cuMemcpyHtoDAsync_v2") &&
             sym(lib, d.MemcpyDtoHAsync, "cuMemcpyDtoHAsync_v2") &&
             sym(lib, d.TensorMapEncodeTiled, "cuTensorMapEncodeTiled") &&
-            sym(lib, d.GetErrorString, "cuGetErrorString");
+            sym(lib, d.GetErrorString, "cuGetErrorString") &&
+            sym(lib, d.IpcGetMemHandle, "cuIpcGetMemHandle") &&
+            sym(lib, d.IpcOpenMemHandle, "cuIpcOpenMemHandle_v2") &&
+            sym(lib, d.IpcCloseMemHandle, "cuIpcCloseMemHandle");
   if (!ok) return fail(EMMY_ERR_NO_DRIVER, "libcuda.so.1 lacks a required symbol: %s", dlerror());
   if (!sym(lib, d.CtxGetId, "cuCtxGetId")) d.CtxGetId = nullptr;
   g_drv = d;
@@ -494,6 +500,34 @@ int emmy_mem_alloc(uint64_t* dptr, size_t bytes) {
 int emmy_mem_free(uint64_t dptr) {
   if (int rc = ready()) return rc;
   return cu(g_drv.MemFree(static_cast<CUdeviceptr>(dptr)), "cuMemFree");
+}
+
+int emmy_ipc_get_handle(uint64_t dptr, char handle[64]) {
+  if (!dptr || !handle) return fail(EMMY_ERR_BAD_ARG, "null device pointer or handle buffer");
+  if (int rc = ready()) return rc;
+  CUipcMemHandle h;
+  if (int rc = cu(g_drv.IpcGetMemHandle(&h, static_cast<CUdeviceptr>(dptr)), "cuIpcGetMemHandle")) return rc;
+  std::memcpy(handle, h.reserved, sizeof(h.reserved));
+  return 0;
+}
+
+int emmy_ipc_open(const char handle[64], uint64_t* dptr) {
+  if (!handle || !dptr) return fail(EMMY_ERR_BAD_ARG, "null handle or result pointer");
+  if (int rc = ready()) return rc;
+  CUipcMemHandle h;
+  std::memcpy(h.reserved, handle, sizeof(h.reserved));
+  CUdeviceptr p = 0;
+  // peer access to the exporting device is enabled on first use of the mapping
+  if (int rc = cu(g_drv.IpcOpenMemHandle(&p, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS), "cuIpcOpenMemHandle"))
+    return rc;
+  *dptr = p;
+  return 0;
+}
+
+int emmy_ipc_close(uint64_t dptr) {
+  if (!dptr) return fail(EMMY_ERR_BAD_ARG, "null device pointer");
+  if (int rc = ready()) return rc;
+  return cu(g_drv.IpcCloseMemHandle(static_cast<CUdeviceptr>(dptr)), "cuIpcCloseMemHandle");
 }
 
 int emmy_memset_d32_async(uint64_t dptr, uint32_t value, size_t count, void* stream) {

@@ -1,10 +1,11 @@
 """Multi-GPU plumbing: one process per GPU, units sharded by rank, the sum's partials combined once.
 
 Every benchmark configuration partitions into independent units (rows, batches, (b,h) pairs), so each
-rank owns a full-size shard of a weak-scaled global problem and runs the same kernel on it with no
-data-path collective.  The full-array sum is the one exchange: each rank reduces its shard to one
-partial, then one ``ncclAllReduce`` (through the C ABI) adds the partials.  ``torch.distributed``
-carries only control traffic: the NCCL unique id, barriers and the max-over-ranks of timings.
+rank owns a shard (``shard``) and runs the same kernel on it with no data-path collective.  The
+full-array sum is the one exchange: each rank reduces its shard to one partial, then either one
+``ncclAllReduce`` through the C ABI (``AllReducePartials``) or the peer-exchange kernel over NVLink
+(``PeerAllReduce``, :mod:`.kernels.peer_sum`) adds the partials.  ``torch.distributed`` carries only
+control traffic: the NCCL unique id and IPC handles, barriers and the max-over-ranks of timings.
 """
 from __future__ import annotations
 
@@ -82,3 +83,101 @@ class AllReducePartials:
         if self.active:
             self.dev.nccl_destroy()
             self.active = False
+
+
+def agree(dist, ok: bool) -> bool:
+    """True only if ``ok`` holds on every rank (so that all ranks take the same path)."""
+    if dist is None:
+        return ok
+    import torch
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def exchange_handles(dist, rank: int, world: int, handle: bytes) -> list:
+    """Every rank's 64-byte IPC handle, in rank order."""
+    if dist is None:
+        return [handle]
+    out = [None] * world
+    dist.all_gather_object(out, handle)
+    if any(not isinstance(h, (bytes, bytearray)) or len(h) != 64 for h in out):
+        raise RuntimeError("an IPC handle is missing or malformed")
+    return [bytes(h) for h in out]
+
+
+class PeerAllReduce:
+    """The sum's exchange step as the peer-exchange kernel (:mod:`.kernels.peer_sum`).
+
+    Set-up: each rank allocates a 2 KiB exchange buffer (``cuMemAlloc``, zeroed), exports its IPC
+    handle, receives every rank's handle, maps the others' buffers into this process and writes the
+    table of the ``world`` buffer addresses to the device.  Every rank must then launch the kernel the
+    same number of times (each launch is one step); the kernel's bounded wait writes status code 51
+    if a peer never arrives.  ``close`` unmaps the peers' buffers and frees this rank's."""
+
+    def __init__(self, device, dist, rank: int, world: int, dtype: str):
+        import torch
+        from .codegen.module import module_text
+        from .kernels import peer_sum
+        self.dev, self.rank, self.world, self.dtype = device, rank, world, dtype
+        self.opened: list[int] = []
+        self.xch = 0
+        self.module = None
+        # each stage ends with an agreement, so a failure on any rank fails the set-up on every rank
+        # (and no rank is left waiting in a collective the others skipped)
+        handle, why = None, ""
+        try:
+            self.xch = device.mem_alloc(peer_sum.BUF_BYTES)
+            device.memset_d32(self.xch, 0, peer_sum.BUF_BYTES // 4, 0)
+            device.sync()
+            handle = device.ipc_handle(self.xch)
+        except Exception as exc:           # noqa: BLE001 - reported on every rank below
+            why = f"{type(exc).__name__}: {exc}"
+        if not agree(dist, handle is not None):
+            self.close()
+            raise RuntimeError(f"peer exchange set-up failed on some rank ({why or 'another rank'})")
+        handles = exchange_handles(dist, rank, world, handle)
+        ok = True
+        try:
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == rank:
+                    ptrs.append(self.xch)
+                else:
+                    q = device.ipc_open(h)
+                    self.opened.append(q)
+                    ptrs.append(q)
+            self.table = torch.tensor(ptrs, dtype=torch.int64, device=f"cuda:{device.index}")
+            self.err = torch.zeros(4, dtype=torch.int32, device=f"cuda:{device.index}")
+            rec = peer_sum.peer_sum_entry(f"peer_sum_{dtype}", rank, world, dtype)
+            self.module = device.load_ptx(module_text([rec]))
+            self.fn = device.function(self.module, rec["name"])
+        except Exception as exc:           # noqa: BLE001
+            ok, why = False, f"{type(exc).__name__}: {exc}"
+        if not agree(dist, ok):
+            self.close()
+            raise RuntimeError(f"peer exchange mapping failed on some rank ({why or 'another rank'})")
+
+    def __call__(self, tensor, dtype: str, stream: int) -> None:
+        if dtype != self.dtype or tensor.numel() != 1:
+            raise ValueError("the peer exchange adds one partial of the dtype it was built for")
+        self.dev.launch_u64(self.fn, [1, 1, 1], [32, 1, 1], 0, stream,
+                            [tensor.data_ptr(), self.xch, self.table.data_ptr(), self.err.data_ptr()])
+
+    def error_code(self) -> int:
+        return int(self.err[0].item())
+
+    def close(self) -> None:
+        for q in self.opened:
+            try:
+                self.dev.ipc_close(q)
+            except Exception:
+                pass
+        self.opened = []
+        if getattr(self, "module", None) is not None:
+            self.dev.unload(self.module)
+            self.module = None
+        if self.xch:
+            self.dev.mem_free(self.xch)
+            self.xch = 0

@@ -51,6 +51,9 @@ SIGNATURES = {
     "emmy_ctx_synchronize": [],
     "emmy_mem_alloc": [c_u64p, ctypes.c_size_t],
     "emmy_mem_free": [ctypes.c_uint64],
+    "emmy_ipc_get_handle": [ctypes.c_uint64, ctypes.c_char_p],
+    "emmy_ipc_open": [ctypes.c_char_p, c_u64p],
+    "emmy_ipc_close": [ctypes.c_uint64],
     "emmy_memset_d32_async": [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_size_t, vp],
     "emmy_memcpy_htod_async": [ctypes.c_uint64, vp, ctypes.c_size_t, vp],
     "emmy_memcpy_dtoh_async": [vp, ctypes.c_uint64, ctypes.c_size_t, vp],
@@ -228,6 +231,37 @@ class Device:
         self._use()
         check(self.lib.emmy_memset_d32_async(int(dptr), value & 0xFFFFFFFF, int(count), vp(stream or 0)),
               "emmy_memset_d32_async")
+
+    def mem_alloc(self, nbytes: int) -> int:
+        """A device allocation of its own (cuMemAlloc), e.g. memory to export to other processes."""
+        self._use()
+        p = ctypes.c_uint64(0)
+        check(self.lib.emmy_mem_alloc(ctypes.byref(p), int(nbytes)), "emmy_mem_alloc")
+        return int(p.value)
+
+    def mem_free(self, dptr: int) -> None:
+        self._use()
+        check(self.lib.emmy_mem_free(int(dptr)), "emmy_mem_free")
+
+    def ipc_handle(self, dptr: int) -> bytes:
+        """The 64-byte inter-process handle of an allocation from :meth:`mem_alloc`."""
+        self._use()
+        buf = ctypes.create_string_buffer(64)
+        check(self.lib.emmy_ipc_get_handle(int(dptr), buf), "emmy_ipc_get_handle")
+        return buf.raw[:64]
+
+    def ipc_open(self, handle: bytes) -> int:
+        """Map another process's exported allocation (over NVLink peer access); its device address."""
+        self._use()
+        if len(handle) != 64:
+            raise ValueError("an IPC handle is 64 bytes")
+        p = ctypes.c_uint64(0)
+        check(self.lib.emmy_ipc_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(p)), "emmy_ipc_open")
+        return int(p.value)
+
+    def ipc_close(self, dptr: int) -> None:
+        self._use()
+        check(self.lib.emmy_ipc_close(int(dptr)), "emmy_ipc_close")
 
     def htod(self, dst: int, src_ptr: int, nbytes: int, stream: int) -> None:
         self._use()

@@ -135,6 +135,16 @@ int emmy_stream_wait_event(void* stream, void* event);
 /* Memory (caller-owned device pointers). */
 int emmy_mem_alloc(uint64_t* dptr, size_t bytes);
 int emmy_mem_free(uint64_t dptr);
+
+/* Cross-process device memory for the peer exchange of the multi-GPU sum (one process per GPU):
+ * emmy_ipc_get_handle exports an allocation made by emmy_mem_alloc as a 64-byte handle, which the
+ * caller passes to the other ranks; emmy_ipc_open maps a peer's allocation into this process
+ * (cuIpcOpenMemHandle with lazy peer access over NVLink) and emmy_ipc_close unmaps it.  No
+ * counterpart in the reference, which runs on one GPU (the replacement for its role here is one
+ * ncclAllReduce). */
+int emmy_ipc_get_handle(uint64_t dptr, char handle[64]);
+int emmy_ipc_open(const char handle[64], uint64_t* dptr);
+int emmy_ipc_close(uint64_t dptr);
 int emmy_memset_d32_async(uint64_t dptr, uint32_t value, size_t count, void* stream);
 int emmy_memcpy_htod_async(uint64_t dst, const void* src, size_t bytes, void* stream);
 int emmy_memcpy_dtoh_async(void* dst, uint64_t src, size_t bytes, void* stream);

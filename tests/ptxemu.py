@@ -407,11 +407,15 @@ class Emulator:
             if op.startswith("ld.param"):
                 regs[ops[0]] = args[ops[1].strip()[1:-1]]
                 continue
-            if op.startswith(("ld.global", "ld.shared", "ldu.global", "ld.volatile")):
+            if op.startswith(("ld.global", "ld.shared", "ldu.global", "ld.volatile", "ld.acquire", "ld.relaxed")):
                 self._load(op, ops, regs, addr, smem, mem)
                 continue
-            if op.startswith(("st.global", "st.shared")):
+            if op.startswith(("st.global", "st.shared", "st.release", "st.relaxed")):
                 self._store(op, ops, regs, addr, val, smem, mem)
+                continue
+            if op.startswith("mov.u64") and ops[1].strip() == "%globaltimer":
+                # a nanosecond clock: the emulator's step count, so bounded waits end in emulated time
+                regs[ops[0]] = 1000 * n
                 continue
             if op.startswith("red.global") or op.startswith("atom.global"):
                 self._red(op, ops, regs, addr, val, mem)
@@ -481,7 +485,7 @@ class Emulator:
                          "neg", "not", "selp") and parts[-1] in ("s32", "u32", "b32", "s64", "u64", "b64", "pred")
                 and not x.ops[0].startswith("{")) or (parts[0] == "setp" and parts[-1][0] in "sub") or (
                 op in ("mov.u32", "mov.b32", "mov.u64", "mov.b64", "mov.s32")
-                and not x.ops[0].startswith("{") and not x.ops[1].strip().startswith(("{", "0f", "0d"))):
+                and not x.ops[0].startswith("{") and not x.ops[1].strip().startswith(("{", "0f", "0d", "%globaltimer"))):
             return (2,)
         if parts[-1] != "f32" or parts[0] not in _F32 or x.ops[0].startswith("{"):
             return (0,)
