@@ -159,8 +159,12 @@ def check_verdict(key: str, check: dict) -> tuple[bool, str]:
         ok = check["abs_err"] == 0 and check.get("global_abs_err", 0) == 0
         return ok, "bit-exact"
     if key == "c2":
-        ok = check["rel_err"] <= 1e-5 and check.get("global_rel_err", 0.0) <= 1e-5
-        return ok, "1e-5 relative"
+        # the configuration's output is the global scalar: at N > 1 the bound applies to the exchanged
+        # total; a rank's partial is an intermediate whose shard may cancel to near zero, where a
+        # relative bound on it says nothing about the kernel (its error is reported all the same)
+        if "global_rel_err" in check:
+            return check["global_rel_err"] <= 1e-5, "1e-5 relative on the global total"
+        return check["rel_err"] <= 1e-5, "1e-5 relative"
     if key == "c1":
         return check["max_err_over_bound"] <= 1.0, "1e-5 relative (floor 1e-5 of the largest |y|)"
     if key == "c3":
@@ -806,7 +810,12 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
         if code:
             raise KernelTimedOut(f"{key}: kernel status word {code}: a pipeline wait timed out")
         if bad:
-            raise CheckFailed(f"{key}: result outside the tolerance ({tol}) on some rank: {json.dumps(check)}")
+            per_rank = [check]
+            if dist:
+                per_rank = [None] * world
+                dist.all_gather_object(per_rank, check)
+            raise CheckFailed(f"{key}: result outside the tolerance ({tol}) on some rank; checks by rank: "
+                              f"{json.dumps(per_rank)}")
 
         # e2e: pinned host buffers, copies inside the timed region, through the C ABI
         e2e = None
