@@ -630,17 +630,17 @@ def bmm_small(batch=2, m=32, n=32, k=64):
                    block=base.block, rtol=1e-4, atol=1e-6, params={"expr": "matmul", "contraction": True})
 
 
-def sdpa(batch, heads, seq, dim, causal, scale=None):
+def sdpa(batch, heads, seq, dim, causal, scale=None, mask=False):
     """scaled_dot_product_attention of bf16 Q, K, V [batch, heads, seq, dim] (optionally causal, with
     an explicit scale): the online-softmax nest of the attention IR at the small shapes of the
     reference's attention cases.  Sequences that are not a multiple of the tensor-core kernel's
     256-row query tiles run on the CUDA cores."""
     from .irgen import attention_ir
-    base = attention_ir(batch, heads, seq, dim, causal, scale=scale)
-    return Problem(f"sdpa_{batch}x{heads}x{seq}x{dim}{'_causal' if causal else ''}", "corpus", base.entry,
-                   base.graph, base.args, grid=base.grid, block=base.block, rtol=1e-4, atol=1e-6,
-                   params={"expr": "sdpa", "contraction": True, "attention": True, "causal": causal,
-                           "scale": base.params["scale"]})
+    base = attention_ir(batch, heads, seq, dim, causal, scale=scale, mask=mask)
+    return Problem(f"sdpa_{batch}x{heads}x{seq}x{dim}{'_causal' if causal else ''}{'_mask' if mask else ''}",
+                   "corpus", base.entry, base.graph, base.args, grid=base.grid, block=base.block, rtol=1e-4,
+                   atol=1e-6, params={"expr": "sdpa", "contraction": True, "attention": True, "causal": causal,
+                                      "scale": base.params["scale"], "mask": mask})
 
 
 def scan_max_and_prod(rows=4, cols=64):
@@ -943,4 +943,6 @@ CORPUS = {
     # a_sdpa_causal and a_sdpa_scale: causal at head dim 64, and an explicit scale at 48 rows, dim 32
     "k_sdpa_causal": lambda: sdpa(1, 2, 64, 64, True),
     "k_sdpa_scale": lambda: sdpa(1, 4, 48, 32, False, scale=0.2),
+    # a_mask: an explicit boolean attention mask (random here, so some rows start with masked keys)
+    "k_sdpa_mask": lambda: sdpa(1, 2, 16, 32, False, mask=True),
 }

@@ -526,12 +526,17 @@ def bmm_naive_ir(batch: int, m: int, n: int, k: int, threads: int = 256) -> Prob
 
 
 def attention_ir(batch: int = 8, heads: int = 32, seq: int = 4096, dim: int = 128,
-                 causal: bool = True, scale: float | None = None) -> Problem:
+                 causal: bool = True, scale: float | None = None, mask: bool = False) -> Problem:
     """O = softmax(Q K^T / sqrt(D) + causal mask) V, bf16 in and out, f32 math.
 
     One warp per query row; each lane holds D/32 contiguous dims.  Scores come from a lane dot
     plus a WarpShuffle sum, the causal mask is a Select, and the online softmax keeps the running
     max / sum / output as Accums whose ``base`` is the rescaled previous value.
+
+    ``mask`` adds an explicit boolean mask M [seq, seq] (u8; nonzero = the key takes part, torch's
+    ``attn_mask`` convention): a masked score is -inf.  Since any key may then be masked, the
+    exponents use a safe maximum (0 while every key so far is masked), so a masked first key cannot
+    turn the running sum into NaN; a row with every key masked ends as 0 / 0 = NaN, as in torch.
     """
     if dim % 32 or dim // 32 not in (1, 2, 4, 8):
         raise ValueError("attention_ir needs dim in {32, 64, 128, 256}")
@@ -556,17 +561,23 @@ def attention_ir(batch: int = 8, heads: int = 32, seq: int = 4096, dim: int = 12
                 dot.append(Assign(nm, "add", [terms[j], terms[j + 1]]))
                 nxt.append(nm)
             terms, lvl = nxt, lvl + 1
-    mask = [(Bin(">", V("kv"), V("qi")), Lit(-math.inf))] if causal else []
+    sel = [(Bin(">", V("kv"), V("qi")), Lit(-math.inf))] if causal else []
+    if mask:
+        sel.append((Bin("==", V("mk"), 0), Lit(-math.inf)))
+    safe = "mu" if mask else "mn"
     body_k = [
         Load(ks, "K", [V("b"), V("h"), V("kv"), V("d0")], "bf16"),
+        *([Load(["mk"], "M", [V("qi"), V("kv")], "u8")] if mask else []),
         *dot,
         WarpShuffle(["dp"], ["dp_o"], _combine("dp", "dp_o", "add", "f32")),
         Assign("sc", "multiply", ["dp", Lit(scale)]),
-        Select("sm", [*mask, (None, "sc")]),
+        Select("sm", [*sel, (None, "sc")]),
         Assign("mn", "maximum", ["m", "sm"]),
-        Assign("dm", "subtract", ["m", "mn"]),
+        *([Assign("allm", "equal", ["mn", Lit(-math.inf)], "bool"),
+           Select("mu", [(V("allm"), Lit(0.0)), (None, "mn")])] if mask else []),
+        Assign("dm", "subtract", ["m", safe]),
         Assign("alpha", "exp", ["dm"]),
-        Assign("ds", "subtract", ["sm", "mn"]),
+        Assign("ds", "subtract", ["sm", safe]),
         Assign("pe", "exp", ["ds"]),
         Assign("ls", "multiply", ["l", "alpha"]),
         Accum("l", "add", "pe", base="ls"),
@@ -589,15 +600,17 @@ def attention_ir(batch: int = 8, heads: int = 32, seq: int = 4096, dim: int = 12
     shape = (batch, heads, seq, dim)
     args = [TensorSpec("Q", shape, "bf16", ("normal", 1.0)),
             TensorSpec("K", shape, "bf16", ("normal", 1.0)),
-            TensorSpec("V", shape, "bf16", ("normal", 1.0)),
-            TensorSpec("O", shape, "bf16", output=True)]
+            TensorSpec("V", shape, "bf16", ("normal", 1.0))]
+    if mask:
+        args.append(TensorSpec("M", (seq, seq), "u8", ("randint", 0, 2)))
+    args.append(TensorSpec("O", shape, "bf16", output=True))
     threads = 128
     grid = batch * heads * seq * 32 // threads
     return Problem(f"attn_{batch}x{heads}x{seq}x{dim}", "attention", "attention_causal" if causal else "attention",
                    _graph("attention_causal" if causal else "attention", args, body), args,
                    grid=grid, block=threads, rtol=1e-4, atol=1e-6,
                    params={"batch": batch, "heads": heads, "seq": seq, "dim": dim, "causal": causal,
-                           "scale": scale})
+                           "scale": scale, **({"mask": True} if mask else {})})
 
 
 #: The five BASELINE configurations at full size.

@@ -32,15 +32,17 @@ def bmm(A, B):
     return torch.bmm(A.double(), B.double())
 
 
-def attention(Q, K, V, causal=True, scale=None):
+def attention(Q, K, V, causal=True, scale=None, mask=None):
+    """SDPA in float64; ``mask`` is a boolean [S, S] tensor, True where the key takes part."""
     import torch
     q, k, v = Q.double(), K.double(), V.double()
     d = q.shape[-1]
     s = (q @ k.transpose(-1, -2)) * (scale if scale is not None else 1.0 / math.sqrt(d))
     if causal:
         n = s.shape[-1]
-        mask = torch.ones(n, n, dtype=torch.bool).triu(1)
-        s = s.masked_fill(mask, float("-inf"))
+        s = s.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
+    if mask is not None:
+        s = s.masked_fill(~mask.bool(), float("-inf"))
     return torch.softmax(s, dim=-1) @ v
 
 
@@ -195,7 +197,8 @@ CORPUS = {
     "scanprod": lambda t, p: {"cm": __import__("torch").cummax(t["x"].double(), -1).values,
                               "pr": t["x"].double().prod(-1)},
     # torch's posinf / neginf defaults for a float32 tensor: the largest finite f32 and its negative
-    "sdpa": lambda t, p: {"O": attention(t["Q"], t["K"], t["V"], p["causal"], p["scale"])},
+    "sdpa": lambda t, p: {"O": attention(t["Q"], t["K"], t["V"], p["causal"], p["scale"],
+                                         t["M"] if p.get("mask") else None)},
     "nan_to_num": lambda t, p: {"y": __import__("torch").nan_to_num(t["x"]).double()},
     "logaddexp": lambda t, p: {"y": __import__("torch").logaddexp(t["a"].double(), t["b"].double())},
     "elu_selu": lambda t, p: {"elu": __import__("torch").nn.functional.elu(t["x"].double()),
