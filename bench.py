@@ -178,18 +178,21 @@ def check_verdict(key: str, check: dict) -> tuple[bool, str]:
 
 # ---- clocks -------------------------------------------------------------------------------------
 
-CLOCK_FIELDS = ["timestamp", "index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+CLOCK_FIELDS = ["timestamp", "index", "uuid", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
                 "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
                 "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
 
 
 class ClockSampler:
-    """nvidia-smi sampling every 200 ms for the whole run; ``summary(t0, t1)`` reads a time window."""
+    """nvidia-smi sampling every 200 ms for the whole run; ``summary(t0, t1)`` reads a time window.
+    ``uuids`` (set by the caller) restricts the summary to the GPUs the job's ranks run on, so a job on
+    4 GPUs of an 8-GPU box reports its own clocks, not the idle GPUs'."""
 
     def __init__(self):
         self.proc = None
         self.file = None
         self.rows = None
+        self.uuids: set | None = None
 
     def start(self):
         try:
@@ -240,6 +243,9 @@ class ClockSampler:
             except ValueError:
                 return None
 
+        if self.uuids:
+            mine = [r for r in rows if r["uuid"].removeprefix("GPU-").lower() in self.uuids]
+            rows = mine or rows
         by_gpu = {}
         for r in rows:
             by_gpu.setdefault(r["index"], []).append(r)
@@ -930,7 +936,14 @@ def main(argv=None) -> int:
     dist = edist.init(world, local)
     peaks, peak_src = load_peaks()
     clocks = ClockSampler() if local == 0 else None
+    # the GPUs this job runs on (every rank's), for the clock summary
+    uuid = str(torch.cuda.get_device_properties(local).uuid).removeprefix("GPU-").lower()
+    uuids = [uuid]
+    if dist:
+        uuids = [None] * world
+        dist.all_gather_object(uuids, uuid)
     if clocks:
+        clocks.uuids = set(uuids)
         clocks.start()
         time.sleep(0.3)
     per = {}

@@ -145,3 +145,22 @@ def test_bench_reference_arm_runs_on_the_host():
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300,
                        env={**env, "RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert r.returncode == 0 and not r.stdout.strip()
+
+
+def test_clock_summary_reads_only_the_jobs_gpus():
+    """A job on some GPUs of a larger box summarises the clocks of its own GPUs (matched by UUID), not
+    those of idle GPUs beside it."""
+    import bench
+    rows = []
+    for idx, uu, mhz, pw in [("0", "GPU-AAAA-1", "1900", "700"), ("1", "GPU-BBBB-2", "300", "90"),
+                             ("0", "GPU-AAAA-1", "1950", "710"), ("2", "GPU-CCCC-3", "345", "95")]:
+        r = dict(zip(bench.CLOCK_FIELDS, ["2026/12/02 06:00:00.000", idx, uu, mhz, "1965", pw] + ["Not Active"] * 5))
+        r["t"] = None
+        rows.append(r)
+    c = bench.ClockSampler()
+    c.rows = rows
+    c.uuids = {"aaaa-1"}
+    s = c.summary()
+    assert s["gpus"] == ["0"] and s["sm_mhz"] == 1925.0
+    c.uuids = {"bbbb-2", "cccc-3"}
+    assert c.summary()["gpus"] == ["1", "2"]
