@@ -577,7 +577,7 @@ def make_sets(key, p, p_global, rotate, world, rank, scaling, shard_lo, shard_hi
     return sets
 
 
-def correctness(key, p, t, ex, step, dist, collective, stream) -> dict:
+def correctness(key, p, t, ex, step, dist, collective, stream, fused: bool = False) -> dict:
     """The timed output (rank-local shard) against float64, as the tolerance measures it."""
     import torch
     ex(t, stream)
@@ -586,6 +586,14 @@ def correctness(key, p, t, ex, step, dist, collective, stream) -> dict:
     if fam == "sum":
         want = t["x"].double().sum().item() if p.params["dtype"] == "f32" else int(t["x"].long().sum().item())
         got = t["out"].item()
+        if fused:
+            # the kernel's output is already the exchanged total of every rank's partial
+            tot = torch.tensor([float(want)], dtype=torch.float64, device="cuda")
+            dist.all_reduce(tot)
+            e = abs(got - tot.item())
+            r = e / max(abs(tot.item()), 1e-30)
+            return {"abs_err": e, "rel_err": r, "global_abs_err": e, "global_rel_err": r,
+                    "partial": "exchanged inside the kernel (no rank-local partial to check)"}
         check = {"abs_err": abs(got - want), "rel_err": abs(got - want) / max(abs(want), 1e-30)}
         if collective:
             # the exchange step too: kernel + ncclAllReduce against the all-reduced float64 shard sums
@@ -744,34 +752,41 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
     desc, metric, unit = CONFIGS[key]
     scale = 1e9 if unit == "GB/s" else 1e12
 
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), options)
+    from emmy_ptx_b200.launcher import Device
+    dev = Device.get(local)
+    collective = p.family == "sum" and world > 1
+    allreduce, exchange, fused = None, None, False
+    if collective:
+        if args.exchange == "peer":
+            try:
+                allreduce = edist.PeerAllReduce(dev, dist, rank, world, p.params["dtype"])
+                exchange, fused = "peer (NVLink exchange fused into the reduction kernel)", True
+            except RuntimeError as exc:         # the same on every rank (the set-up agrees)
+                exchange = f"nccl (peer exchange unavailable: {exc})"
+        if allreduce is None:
+            allreduce = edist.AllReducePartials(dev, dist, rank, world)
+            exchange = exchange or "nccl"
+    nccl_in_step = collective and not fused
+    build_opts = dict(options)
+    if fused:
+        # the last block of the reduction publishes the partial and adds every rank's (kernels/peer_sum.py)
+        build_opts["exchange"] = {"rank": rank, "world": world, "partial": "out", "dtype": p.params["dtype"]}
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), build_opts)
     ex = Executable(mod, device=local)
-    dev = ex.dev
     stream = torch.cuda.current_stream().cuda_stream
 
     rotate = 1
     if units < 2 * 126e6 and kind == "B":      # L2-resident working set: rotate buffer sets past 2x L2
         rotate = int(max(2, (2 * 126e6 * 2) // units + 1))
     sets = make_sets(key, p, p_global, rotate, world, rank, "strong" if strong else "weak", lo, hi)
-
-    collective = p.family == "sum" and world > 1
-    allreduce, exchange = None, None
-    if collective:
-        if args.exchange == "peer":
-            try:
-                allreduce = edist.PeerAllReduce(dev, dist, rank, world, p.params["dtype"])
-                exchange = "peer (NVLink exchange kernel)"
-            except RuntimeError as exc:         # the same on every rank (the set-up agrees)
-                exchange = f"nccl (peer exchange unavailable: {exc})"
-        if allreduce is None:
-            allreduce = edist.AllReducePartials(dev, dist, rank, world)
-            exchange = exchange or "nccl"
-    nccl_in_step = collective and isinstance(allreduce, edist.AllReducePartials)
+    if fused:
+        for t_ in sets:
+            t_["__xch"], t_["__peers"] = allreduce.xch, allreduce.table
     try:
         def step(t, s=None):
             s = stream if s is None else s
             ex(t, s)
-            if collective:
+            if nccl_in_step:
                 allreduce(t["out"], p.params["dtype"], s)
 
         for i in range(max(args.warmup, 3)):
@@ -798,15 +813,26 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
             kern_ms = timed(lambda: [ex.run(sets[i % rotate], stream, zero=False) for i in range(reps)], dist,
                             max_over_ranks, reps)
         allreduce_ms = None
-        if collective:
+        if nccl_in_step:
             n_ar = 50
             allreduce_ms = timed(lambda: [allreduce(sets[0]["out"], p.params["dtype"], stream) for _ in range(n_ar)],
                                  dist, max_over_ranks, n_ar)
+        elif fused:
+            # the exchange's cost: the fused kernel against the same reduction without its epilogue
+            plain = Executable(compile_graph(Graph.from_dict(p.graph), p.meta(), options), device=local)
+            g_plain = graph_of(lambda s: [plain.run(sets[i % rotate], s, zero=False) for i in range(reps)],
+                               capture=graphs)
+            plain_ms = timed(g_plain.replay if g_plain is not None else
+                             (lambda: [plain.run(sets[i % rotate], stream, zero=False) for i in range(reps)]),
+                             dist, max_over_ranks, reps)
+            allreduce_ms = kern_ms - plain_ms
+            g_plain = None
+            plain.close()
         t_timed1 = time.time()
         step_graph = kern_graph = None
         value = g_units / (ms_step / 1000.0) / scale
 
-        check = correctness(key, p, sets[0], ex, step, dist, collective, stream)
+        check = correctness(key, p, sets[0], ex, step, dist, collective, stream, fused)
         ok, tol = check_verdict(key, check)
         check["tolerance"] = tol
         check["ok"] = ok
@@ -898,6 +924,8 @@ def run_config(key, args, world, rank, local, dist, peaks, peak_src, clocks) -> 
     finally:
         torch.cuda.synchronize()
         if collective:
+            if dist:
+                dist.barrier()               # every rank is done with the peers' exchange buffers
             allreduce.close()
         ex.close()
         del sets

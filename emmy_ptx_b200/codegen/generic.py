@@ -111,6 +111,18 @@ class KernelEmitter:
         self.G = int(grid[0]) if grid else None
         if grid and len(grid) > 1 and any(int(x) != 1 for x in grid[1:]):
             self.G = None
+        self.exchange = self.opts.get("exchange")
+        if self.exchange:
+            # the multi-GPU sum's exchange as this kernel's epilogue (kernels/peer_sum.py): it needs the
+            # grid size (the block that finishes last runs it) and the one-element partial to publish
+            x = self.exchange
+            if not self.G or not self.T:
+                raise Unsupported("the fused exchange needs a 1-D grid and block from the launch meta")
+            if x.get("partial") not in self.params or self.shapes.get(x["partial"], (0,)) not in ((1,), ()):
+                raise Unsupported(f"the fused exchange needs a one-element output, not {x.get('partial')!r}")
+            if x.get("dtype") not in ("f32", "i32") or dt_name(self.dtypes[x["partial"]]) != x["dtype"]:
+                raise Unsupported("the fused exchange adds an f32 or i32 partial of the output's type")
+        self.err = None
         self.tma = None
         if self.opts.get("tma_stripes", True) is not False and self.T:
             from . import tma_stripes
@@ -205,6 +217,16 @@ class KernelEmitter:
             self.sbase[name] = r
         if self.tma is not None:
             self._tma_prologue(tid)
+        if self.exchange:
+            self.xch, self.peers = b.reg("b64"), b.reg("b64")
+            for r, nm in ((self.xch, "p_xch"), (self.peers, "p_peers")):
+                b.emit(f"ld.param.u64 {r}, [{nm}];")
+                b.emit(f"cvta.to.global.u64 {r}, {r};")
+            if self.err is None:
+                self.err = b.reg("b64")
+                b.emit(f"ld.param.u64 {self.err}, [p_err];")
+                b.emit(f"cvta.to.global.u64 {self.err}, {self.err};")
+            self.tid_reg = tid
 
     # ---- integers -------------------------------------------------------------------------
     def mat(self, aff) -> str:
@@ -1069,6 +1091,37 @@ class KernelEmitter:
         self.grp = b.reg("b32")
         b.emit(f"mov.u32 {self.grp}, 0;")
 
+    def _exchange_epilogue(self) -> None:
+        """The multi-GPU sum's exchange, fused after the reduction: every block meets at a barrier (its
+        atomic adds to the partial are issued), thread 0 releases them and takes a ticket from the
+        exchange buffer; in the block whose ticket is the last, warp 0 resets the ticket, acquires
+        the other blocks' adds and runs the peer exchange (kernels/peer_sum.py), which leaves the
+        rank-ordered total of every rank's partial in the output."""
+        from ..kernels import peer_sum
+        b, x = self.b, self.exchange
+        end = b.label("_xend")
+        lane, w, tk = b.reg("b32"), b.reg("b32"), b.reg("b32")
+        pw, p0, plast = b.reg("pred"), b.reg("pred"), b.reg("pred")
+        b.emit("bar.sync 0;")
+        b.emit(f"and.b32 {lane}, {self.tid_reg}, 31;")
+        b.emit(f"shr.u32 {w}, {self.tid_reg}, 5;")
+        b.emit(f"setp.ne.u32 {pw}, {w}, 0;")
+        b.emit(f"@{pw} bra {end};")
+        b.emit(f"setp.eq.u32 {p0}, {lane}, 0;")
+        b.emit(f"mov.u32 {tk}, 0;")
+        b.emit(f"@{p0} fence.acq_rel.gpu;")
+        b.emit(f"@{p0} atom.global.add.u32 {tk}, [{self.xch}+{peer_sum.TICKET}], 1;")
+        b.emit(f"shfl.sync.idx.b32 {tk}, {tk}, 0, 31, -1;")
+        b.emit(f"setp.ne.u32 {plast}, {tk}, {self.G - 1};")
+        b.emit(f"@{plast} bra {end};")
+        b.emit(f"@{p0} st.global.u32 [{self.xch}+{peer_sum.TICKET}], 0;")
+        b.emit(f"@{p0} fence.acq_rel.gpu;")
+        out = self.preg[x["partial"]]
+        peer_sum.emit_exchange(lambda line: b.place(line[:-1]) if line.endswith(":") else b.emit(line),
+                               b.reg, lambda tag: b.label("_" + tag), lane, out, self.xch, self.peers,
+                               self.err, int(x["rank"]), int(x["world"]), x["dtype"])
+        b.place(end)
+
     def _tma_bar(self, group: str) -> str:
         """The shared address of the mbarrier of commit group ``group`` (a register)."""
         b = self.b
@@ -1476,6 +1529,8 @@ class KernelEmitter:
         self.prepare()
         self.prologue()
         self.stmts(self.op.body)
+        if self.exchange:
+            self._exchange_epilogue()
         body, decls = self.b.lines(), self.b.reg_decls()
         if self.opts.get("regalloc", os.environ.get("EMMY_B200_REGALLOC", "1") != "0"):
             from .regalloc import allocate
@@ -1499,6 +1554,10 @@ class KernelEmitter:
             "align": dict(self.palign),
             "zero_outputs": list(self.kmeta.get("zero_outputs") or []),
             "pdl": self.pdl,
-            **({"tmaps": self.tma["tmaps"], "extra": [{"name": "__err", "kind": "errword"}]}
-               if self.tma is not None else {}),
+            **({"tmaps": self.tma["tmaps"]} if self.tma is not None else {}),
+            **({"extra": ([{"name": "__xch", "kind": "buffer", "param": "p_xch"},
+                           {"name": "__peers", "kind": "buffer", "param": "p_peers"}] if self.exchange else [])
+                + [{"name": "__err", "kind": "errword"}]}
+               if self.tma is not None or self.exchange else {}),
+            **({"exchange": dict(self.exchange)} if self.exchange else {}),
         }

@@ -46,7 +46,7 @@ def launch_record(b: dict) -> dict:
         "zero_outputs": b.get("zero_outputs", []),
         "kind": b.get("kind", "generic"),
     }
-    for k in ("tmaps", "cluster", "extra", "pdl", "scratch", "stream", "after"):
+    for k in ("tmaps", "cluster", "extra", "pdl", "scratch", "stream", "after", "exchange"):
         if b.get(k):
             rec[k] = b[k]
     if b.get("carveout") is not None:
@@ -61,7 +61,8 @@ def entry_text(b: dict) -> list[str]:
     # extension of the reference's ABI for promoted stripes: the TMA descriptors after arg_order, then
     # the status word the bounded waits write
     params += [f"\t.param .align 64 .b8 p_{spec['name']}[128]" for spec in b.get("tmaps") or []]
-    params += ["\t.param .u64 p_err" for spec in b.get("extra") or [] if spec.get("kind") == "errword"]
+    params += [f"\t.param .u64 {'p_err' if spec.get('kind') == 'errword' else spec['param']}"
+               for spec in b.get("extra") or []]
     out = [MARK + json.dumps(launch_record(b), sort_keys=True)]
     out.append(f".visible .entry {b['name']}(\n" + ",\n".join(params) + "\n)")
     if b.get("reqntid"):

@@ -151,7 +151,12 @@ class Executable:
                 if spec.get("kind") == "errword":
                     v = ctypes.c_uint64(self.err.data_ptr())
                 else:
-                    v = ctypes.c_uint64(int(spec["value"]) if "value" in spec else tensors[spec["name"]].data_ptr())
+                    if "value" in spec:
+                        ptr = int(spec["value"])
+                    else:
+                        t = tensors[spec["name"]]
+                        ptr = int(t) if isinstance(t, int) else t.data_ptr()   # a raw device address, or a tensor
+                    v = ctypes.c_uint64(ptr)
                 keep.append(v)
                 args.append(ctypes.cast(ctypes.byref(v), ctypes.c_void_p).value)
             self.dev.launch(fn, g, rec["block"], rec.get("dyn_smem", 0), stream, args,

@@ -189,3 +189,156 @@ def test_two_rank_exchange_over_nvlink():
     want = [np.float32(np.float32(0.5 + 10 * s) + np.float32(1.5 + 10 * s)) for s in range(4)]
     for rank, got, code in res:
         assert code == 0 and got == [float(w) for w in want], (rank, got)
+
+
+def _emulate_fused(world, rank, dtype, peers_by_step, launches=2):
+    """The reduction kernel with the exchange fused as its epilogue, run ``launches`` times for rank
+    ``rank``; before launch e the other ranks have published ``peers_by_step[e-1]``."""
+    from emmy_ptx_b200 import data, irgen
+    from emmy_ptx_b200.compiler import compile_graph
+    from emmy_ptx_b200.ir import Graph
+    p = irgen.sum_ir(1 << 12, dtype, blocks=4, threads=128)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(),
+                        {"exchange": {"rank": rank, "world": world, "partial": "out", "dtype": dtype}})
+    rec = mod.kernels[0]
+    assert [s["name"] for s in rec["extra"]] == ["__xch", "__peers", "__err"]
+    t = data.make_inputs(p)
+    npdt = np.float32 if dtype == "f32" else np.int32
+    mem = Memory()
+    x = mem.alloc(t["x"].numpy().copy())
+    bufs = [mem.alloc(np.zeros(peer_sum.BUF_BYTES, np.uint8)) for _ in range(world)]
+    table = mem.alloc(np.array(bufs, np.uint64))
+    err = mem.alloc(np.zeros(4, np.int32))
+    own = mem.array(bufs[rank], np.uint8, (-1,))
+    got = []
+    for e in range(1, launches + 1):
+        for k, v in peers_by_step[e - 1].items():
+            _publish(own, world, e, k, v, dtype)
+        out = mem.alloc(np.zeros(1, npdt))                      # the runtime zeroes the output
+        Emulator(mod.ptx, rec["entry"]).run(rec["grid"][0], rec["block"][0],
+                                            {"p_x": x, "p_out": out, "p_xch": bufs[rank], "p_peers": table,
+                                             "p_err": err}, mem, rec.get("dyn_smem", 0))
+        got.append(mem.array(out, npdt, (1,))[0])
+    assert struct.unpack("<I", bytes(own[peer_sum.TICKET:peer_sum.TICKET + 4]))[0] == 0   # reset each launch
+    return t, got, int(mem.array(err, np.int32, (4,))[0])
+
+
+def test_fused_reduction_and_exchange_f32():
+    peers = [{0: 10.5, 1: -3.25}, {0: 1.0, 1: 2.0}]
+    t, got, code = _emulate_fused(3, 2, "f32", peers)
+    assert code == 0
+    local = t["x"].double().sum().item()
+    for g, pe in zip(got, peers):
+        assert abs(g - (local + sum(pe.values()))) <= 1e-5 * abs(local + sum(pe.values()))
+
+
+def test_fused_reduction_and_exchange_i32_is_exact():
+    peers = [{1: 123456}, {1: -98765}]
+    t, got, code = _emulate_fused(2, 0, "i32", peers)
+    assert code == 0
+    local = int(t["x"].long().sum().item())
+    assert [int(g) for g in got] == [local + 123456, local - 98765]
+
+
+def test_fused_kernel_assembles():
+    import shutil
+    import subprocess
+    import tempfile
+    from pathlib import Path
+    from emmy_ptx_b200 import irgen
+    from emmy_ptx_b200.codegen.ptxcheck import undefined_uses
+    from emmy_ptx_b200.compiler import compile_graph
+    from emmy_ptx_b200.ir import Graph
+    ptxas = shutil.which("ptxas") or "/usr/local/cuda/bin/ptxas"
+    for dtype in ("f32", "i32"):
+        p = irgen.FULL["c2" if dtype == "f32" else "c2i"]()
+        mod = compile_graph(Graph.from_dict(p.graph), p.meta(),
+                            {"exchange": {"rank": 5, "world": 8, "partial": "out", "dtype": dtype}})
+        assert not undefined_uses(mod.ptx)
+        with tempfile.TemporaryDirectory() as td:
+            f = Path(td) / "k.ptx"
+            f.write_text(mod.ptx)
+            r = subprocess.run([ptxas, "-arch=sm_100a", str(f), "-o", str(Path(td) / "k.cubin")],
+                               capture_output=True, text=True)
+            assert r.returncode == 0, r.stderr
+
+
+def _fused_executable(dev, rank, world, dtype, n=1 << 20):
+    from emmy_ptx_b200 import irgen
+    from emmy_ptx_b200.compiler import compile_graph
+    from emmy_ptx_b200.ir import Graph
+    from emmy_ptx_b200.runtime import Executable
+    p = irgen.sum_ir(n, dtype, blocks=148, threads=256)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(),
+                        {"exchange": {"rank": rank, "world": world, "partial": "out", "dtype": dtype}})
+    return p, Executable(mod, device=dev.index)
+
+
+@pytest.mark.gpu
+def test_fused_reduction_and_exchange_one_rank_on_the_gpu():
+    """The reduction with its exchange epilogue (world 1): the output is the block sum, launch after
+    launch (the ticket counter resets itself), for f32 and i32."""
+    from emmy_ptx_b200 import data
+    from emmy_ptx_b200.launcher import Device
+    dev = Device.get(torch.cuda.current_device())
+    for dtype in ("f32", "i32"):
+        xr = edist.PeerAllReduce(dev, None, 0, 1, dtype)
+        try:
+            p, ex = _fused_executable(dev, 0, 1, dtype)
+            t = {k: v.cuda() for k, v in data.make_inputs(p).items()}
+            t["__xch"], t["__peers"] = xr.xch, xr.table
+            want = t["x"].double().sum().item() if dtype == "f32" else int(t["x"].long().sum().item())
+            for _ in range(3):
+                ex(t)
+                torch.cuda.synchronize()
+                assert ex.error_code() == 0
+                got = t["out"].item()
+                assert (got == want) if dtype == "i32" else abs(got - want) <= 1e-5 * abs(want)
+            ex.close()
+        finally:
+            xr.close()
+
+
+def _worker_fused(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    d = edist.init(world, rank, backend="nccl", timeout_s=60.0)
+    from emmy_ptx_b200 import data
+    from emmy_ptx_b200.launcher import Device
+    dev = Device.get(rank)
+    xr = edist.PeerAllReduce(dev, d, rank, world, "i32")
+    try:
+        p, ex = _fused_executable(dev, rank, world, "i32")
+        t = {k: v.cuda() for k, v in data.make_inputs(p, seed_offset=rank).items()}
+        t["__xch"], t["__peers"] = xr.xch, xr.table
+        local = torch.tensor([int(t["x"].long().sum().item())], dtype=torch.int64, device="cuda")
+        total = local.clone()
+        d.all_reduce(total)
+        got = []
+        for _ in range(3):
+            ex(t)
+            torch.cuda.synchronize()
+            got.append(int(t["out"].item()))
+        q.put((rank, got, int(total.item()), ex.error_code()))
+        ex.close()
+    finally:
+        d.barrier()
+        xr.close()
+        d.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_reduction_and_exchange_over_nvlink():
+    world, port = 2, _port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_fused, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    for rank, got, total, code in res:
+        assert code == 0 and got == [total] * 3, (rank, got, total)
