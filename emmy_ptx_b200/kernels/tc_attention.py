@@ -91,14 +91,21 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                     pingpong: bool = True, f16_int: int = 0, pack_after_turn: bool = False,
                     defer_sum: bool = False, bh_range: tuple[int, int] | None = None,
                     scratch_names: tuple[str, str] | None = None, prefetch_next: int = 0,
-                    pack_in_turn: bool = False) -> dict:
+                    pack_in_turn: bool = False, pair_poly: int = 0) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
     ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps.
     ``bh_range`` = (first, count) restricts the launch to those flattened (batch, head) pairs.
     ``prefetch_next`` = n > 0 makes the producer prefetch into L2, after its last load, the Q tiles and
     first K / V block of CTA index + n (the one likely to start when this one ends).  ``pack_in_turn``
-    keeps all of a block's f16 packing inside its MUFU turn."""
+    keeps all of a block's f16 packing inside its MUFU turn.  ``pair_poly`` = n (0-4) takes n of every
+    4 score pairs of the f16 path off the MUFU: a cubic exp2 on the FMA pipe, two scores per f32x2
+    instruction (the MUFU ``ex2`` and the f16 ``cvt`` packing share the XU pipe, which bounds the exp
+    phase)."""
+    if not 0 <= pair_poly <= 4:
+        raise ValueError("pair_poly takes 0-4 of every 4 score pairs")
+    if pair_poly and poly_every:
+        raise ValueError("pair_poly and poly_every are alternatives")
     if seq % (BQ * TILES):
         raise ValueError("tcgen05 attention needs S % 256 == 0")
     if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
@@ -802,7 +809,44 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"mov.b64 {{{parts[0]}, {parts[1]}}}, {acc[0]};")
         a(f"mov.b64 {{{parts[2]}, {parts[3]}}}, {acc[1]};")
 
-    def exp_block(poly_every, cols=range(BKV), sums=True):
+    pconst = {}
+
+    def pair_const(name, bits32):
+        """A 64-bit register holding the f32 constant ``bits32`` in both halves (made once)."""
+        if name not in pconst:
+            r = a.r("rd")
+            a(f"mov.b64 {r}, 0x{bits32:08X}{bits32:08X};")
+            pconst[name] = r
+        return pconst[name]
+
+    def poly_pair(xp, x0, x1):
+        """(x0, x1) = 2^x for the pair in ``xp`` on the FMA and integer pipes, two lanes per f32x2
+        instruction: clamp at -120, split x = n + f with f in [-1/2, 1/2] by adding and taking away
+        1.5 * 2^23, 2^f by the cubic ``EXP2_C`` (7.8e-5 relative, below the f16 rounding of P) in
+        Horner form, then n added to the exponent field."""
+        magic = pair_const("magic", 0x4B400000)
+        cs = [pair_const(f"c{i}", int(EXP2_C[i][2:], 16)) for i in range(4)]
+        a(f"max.f32 {x0}, {x0}, 0fC2F00000;")
+        a(f"max.f32 {x1}, {x1}, 0fC2F00000;")
+        tp, jp, fp, rp = a.r("rd"), a.r("rd"), a.r("rd"), a.r("rd")
+        a(f"mov.b64 {xp}, {{{x0}, {x1}}};")
+        a(f"add.rn.f32x2 {tp}, {xp}, {magic};")
+        a(f"sub.rn.f32x2 {jp}, {tp}, {magic};")
+        a(f"sub.rn.f32x2 {fp}, {xp}, {jp};")
+        a(f"fma.rn.f32x2 {rp}, {fp}, {cs[3]}, {cs[2]};")
+        a(f"fma.rn.f32x2 {rp}, {rp}, {fp}, {cs[1]};")
+        a(f"fma.rn.f32x2 {rp}, {rp}, {fp}, {cs[0]};")
+        t0, t1, r0, r1 = a.r(), a.r(), a.r(), a.r()
+        a(f"mov.b64 {{{t0}, {t1}}}, {tp};")
+        a(f"mov.b64 {{{r0}, {r1}}}, {rp};")
+        a(f"shl.b32 {t0}, {t0}, 23;")
+        a(f"shl.b32 {t1}, {t1}, 23;")
+        a(f"add.s32 {r0}, {r0}, {t0};")
+        a(f"add.s32 {r1}, {r1}, {t1};")
+        a(f"mov.b32 {x0}, {r0};")
+        a(f"mov.b32 {x1}, {r1};")
+
+    def exp_block(poly_every, cols=range(BKV), sums=True, pairs_poly=0):
         """p = 2^(s*c - m) for the row's BKV scores, summed into ``parts``.  With ``poly_every`` = n,
         every n-th value is taken on the FMA pipe instead of the MUFU (the softmax's bottleneck):
         x is clamped at -120, split as n + f with f in [-1/2, 1/2] by the 1.5*2^23 rounding trick,
@@ -824,8 +868,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                 a(f"mov.b64 {xp}, {{{x0}, {x1}}};")
                 a(f"fma.rn.f32x2 {xp}, {xp}, {cp2}, {np2};")
                 a(f"mov.b64 {{{x0}, {x1}}}, {xp};")
-                a(f"ex2.approx.ftz.f32 {x0}, {x0};")
-                a(f"ex2.approx.ftz.f32 {x1}, {x1};")
+                if (idx // 2) % 4 < pairs_poly:
+                    poly_pair(xp, x0, x1)           # pairs_poly of every 4 pairs off the MUFU
+                else:
+                    a(f"ex2.approx.ftz.f32 {x0}, {x0};")
+                    a(f"ex2.approx.ftz.f32 {x1}, {x1};")
                 if sums:
                     ep = a.r("rd")
                     a(f"mov.b64 {ep}, {{{x0}, {x1}}};")
@@ -901,7 +948,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         if pack_after_turn:
             # only the exps hold the MUFU turn; the f16 packing and the TMEM store of P overlap the
             # other tile's exps
-            exp_block(poly_every, sums=not defer_sum)
+            exp_block(poly_every, sums=not defer_sum, pairs_poly=pair_poly)
             sstamp(4)
             turn_pass()
             if defer_sum:
@@ -912,7 +959,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                 # each half of the row is packed and stored as soon as its exps are done; with
                 # pack_in_turn the second half's packing stays inside the MUFU turn too, so no f16
                 # conversion of this tile runs during the other tile's exps
-                exp_block(poly_every, range(half_n * h, half_n * (h + 1)))
+                exp_block(poly_every, range(half_n * h, half_n * (h + 1)), pairs_poly=pair_poly)
                 if h == 1:
                     sstamp(4)
                     if not pack_in_turn:

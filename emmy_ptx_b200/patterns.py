@@ -387,7 +387,8 @@ def try_lower(graph, node, kmeta, prefix, options):
                   pack_after_turn=bool(options.get("attn_pack_after_turn", False)),
                   defer_sum=bool(options.get("attn_defer_sum", False)),
                   prefetch_next=int(options.get("attn_prefetch_next", 0)),
-                  pack_in_turn=bool(options.get("attn_pack_in_turn", False)))
+                  pack_in_turn=bool(options.get("attn_pack_in_turn", False)),
+                  pair_poly=int(options.get("attn_pair_poly", 0)))
         if options.get("attn_kv128", False):
             # 128-row key/value blocks: QK^T bound by the tensor core instead of shared memory
             from .kernels import tc_attention_kv128 as t128, vconv

@@ -31,6 +31,8 @@ ATTN_VARIANTS = {
     "f16-int4": {"attn_f16_int": 4},
     "no-turns": {"attn_pingpong": False},
     "bf16-pairs": {"attn_half": False},
+    "pair-poly-2": {"attn_pair_poly": 2},
+    "pair-poly-4": {"attn_pair_poly": 4},
     "kv128": {"attn_kv128": True},
     "kv128-ordered": {"attn_kv128": True, "attn_ordered": True},
     "kv128-bf16-pairs": {"attn_kv128": True, "attn_half": False},
