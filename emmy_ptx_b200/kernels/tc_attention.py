@@ -91,7 +91,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                     pingpong: bool = True, f16_int: int = 0, pack_after_turn: bool = False,
                     defer_sum: bool = False, bh_range: tuple[int, int] | None = None,
                     scratch_names: tuple[str, str] | None = None, prefetch_next: int = 0,
-                    pack_in_turn: bool = False, pair_poly: int = 0) -> dict:
+                    pack_in_turn: bool = False, pair_poly: int = 0, dim: int = 128) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
     ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps.
@@ -102,6 +102,15 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     4 score pairs of the f16 path off the MUFU: a cubic exp2 on the FMA pipe, two scores per f32x2
     instruction (the MUFU ``ex2`` and the f16 ``cvt`` packing share the XU pipe, which bounds the exp
     phase)."""
+    if dim not in (64, 128):
+        raise ValueError("tcgen05 attention takes head dim 64 or 128")
+    # the head dim sets the tile sizes: a Q tile or K/V block is dim / 64 TMA boxes of 64 columns
+    D = dim
+    Q_BYTES = BQ * D * 2
+    Q_HALF = BQ * 64 * 2
+    KV_BYTES = BKV * D * 2
+    KV_HALF = BKV * 64 * 2
+    S_COL0 = TILES * D
     if not 0 <= pair_poly <= 4:
         raise ValueError("pair_poly takes 0-4 of every 4 score pairs")
     if pair_poly and poly_every:
@@ -288,7 +297,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     for i in range(TILES):
         r_i = a.r()
         a(f"add.u32 {r_i}, {row0}, {BQ * i};")
-        for hb in range(2):
+        for hb in range(D // 64):
             d_ = a.r()
             a(f"add.u32 {d_}, {sQ}, {Q_BYTES * i + Q_HALF * hb};")
             tma4(d_, tq, 64 * hb, r_i, qb)
@@ -338,9 +347,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     else:
         a(f"selp.b64 {tsel}, {tv}, {tk}, {isv};")
     tma4(dst, tsel, 0, kvrow, fb)
-    dst2 = a.r()
-    a(f"add.u32 {dst2}, {dst}, {KV_HALF};")
-    tma4(dst2, tsel, 64, kvrow, fb)
+    if D == 128:
+        dst2 = a.r()
+        a(f"add.u32 {dst2}, {dst}, {KV_HALF};")
+        tma4(dst2, tsel, 64, kvrow, fb)
     pw = a.r("p")
     a(f"add.u32 {stage}, {stage}, 1;")
     a(f"setp.eq.u32 {pw}, {stage}, {STAGES};")
@@ -370,10 +380,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         for i in range(TILES):
             r_i = a.r()
             a(f"add.u32 {r_i}, {rown}, {BQ * i};")
-            for hb in range(2):
+            for hb in range(D // 64):
                 a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tq}, {{{64 * hb}, {r_i}, {hhn}, {bbn}}}];")
         for tmn in (tk, tv16 if half else tv):
-            for hb in range(2):
+            for hb in range(D // 64):
                 a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tmn}, {{{64 * hb}, 0, {hhn}, {bbn}}}];")
         a.label(l_nopf)
     for s in range(STAGES):

@@ -21,7 +21,7 @@ F16_MAX_BF16_BITS = 0x477F
 
 def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16", "__vflag"),
                 bh_range: tuple[int, int] | None = None, ctas: int | None = None,
-                block_rows: int = BLOCK_ROWS) -> dict:
+                block_rows: int = BLOCK_ROWS, dim: int = D) -> dict:
     """The pre-pass entry; ``bh_range`` = (first, count) converts only those flattened (batch, head)
     pairs (their blocks and flags sit at the same places as in a whole-tensor launch).  ``ctas``
     caps the grid: each CTA then strides over the blocks, which keeps the launch to one CTA per SM
@@ -31,7 +31,9 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
         raise ValueError("the value pre-pass converts 64- or 128-row blocks")
     if seq % block_rows:
         raise ValueError(f"the value pre-pass needs S % {block_rows} == 0")
-    block_bytes = block_rows * D * 2
+    if dim not in (64, 128):
+        raise ValueError("the value pre-pass converts head dim 64 or 128")
+    block_bytes = block_rows * dim * 2
     bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
     if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):
         raise ValueError(f"bh_range {bh_range} outside the {batch * heads} (batch, head) pairs")
@@ -107,6 +109,6 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
         "name": name, "kind": "value_prepass", "params": [vn, v16n, fn], "raw_entry": entry,
         "grid": [grid, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": 0,
         "align": {vn: 16, v16n: 16, fn: 4}, "zero_outputs": [],
-        "scratch": [{"name": v16n, "dtype": "f16", "shape": [batch, heads, seq, D]},
+        "scratch": [{"name": v16n, "dtype": "f16", "shape": [batch, heads, seq, dim]},
                     {"name": fn, "dtype": "i32", "shape": [batch * heads * (seq // block_rows)]}],
     }

@@ -374,8 +374,12 @@ def try_lower(graph, node, kmeta, prefix, options):
     if hit is not None:
         Q, K, V, O, bt, hd, seq, dim, causal, scale = hit
         from .kernels import tc_attention
-        if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES):
+        if dim not in (64, 128) or seq % (tc_attention.BQ * tc_attention.TILES):
             return None
+        if dim != tc_attention.D:
+            # head dim 64: the default schedule only (the other forms are built for 128)
+            options = {k: v for k, v in options.items()
+                       if k not in ("attn_persistent", "attn_kv128", "attn_overlap")}
         precise = bool(options.get("attn_precise", True))
         half = bool(options.get("attn_half", True)) and precise
         name = node.op.name
@@ -388,7 +392,7 @@ def try_lower(graph, node, kmeta, prefix, options):
                   defer_sum=bool(options.get("attn_defer_sum", False)),
                   prefetch_next=int(options.get("attn_prefetch_next", 0)),
                   pack_in_turn=bool(options.get("attn_pack_in_turn", False)),
-                  pair_poly=int(options.get("attn_pair_poly", 0)))
+                  pair_poly=int(options.get("attn_pair_poly", 0)), dim=dim)
         if options.get("attn_kv128", False):
             # 128-row key/value blocks: QK^T bound by the tensor core instead of shared memory
             from .kernels import tc_attention_kv128 as t128, vconv
@@ -424,7 +428,7 @@ def try_lower(graph, node, kmeta, prefix, options):
         head = pairs // int(options.get("attn_overlap_split", 8)) if options.get("attn_overlap", False) else 0
         if head < 1 or head >= pairs:
             attn = tc_attention.attention_entry(name, bt, hd, seq, causal, scale, scratch_names=scratch, **kw)
-            pre = vconv.vconv_entry(f"{name}_vconv", bt, hd, seq, names=(V.name,) + scratch)
+            pre = vconv.vconv_entry(f"{name}_vconv", bt, hd, seq, names=(V.name,) + scratch, dim=dim)
             return [pre, attn]
         # The value pre-pass of all but the first `head` (batch, head) pairs runs on a side stream while
         # the attention of those first pairs runs: the pre-pass is bound by HBM bandwidth, which the

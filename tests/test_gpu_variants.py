@@ -133,3 +133,26 @@ def test_cuda_core_bmm_stripes(tma):
     torch.cuda.synchronize()
     assert ex.error_code() == 0
     compare(td["C"].cpu(), t["A"].double() @ t["B"].double(), "f32", 1e-4, f"cuda-core bmm tma={tma}")
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_head_dim_64(causal):
+    """Head dim 64 on the tensor cores: the small case against the oracle, and [2, 8, 2048, 64] against
+    float64 on a few heads (first, middle and last)."""
+    import math
+    p = irgen.attention_ir(1, 2, 512, 64, causal)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"d64 causal={causal}", rms_floor=True)
+    p = irgen.attention_ir(2, 8, 2048, 64, causal)
+    t = data.make_inputs(p)
+    got, ex = _run_ours(p, t)
+    assert ex.error_code() == 0
+    for b, h in ((0, 0), (1, 3), (1, 7)):
+        q, k, v = (t[n][b, h].double() for n in ("Q", "K", "V"))
+        s_ = (q @ k.T) / math.sqrt(64)
+        if causal:
+            s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
+        compare(got["O"][b, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"d64 ({b},{h})", rms_floor=True)

@@ -44,6 +44,11 @@ def test_attention_pipeline_completes(variant):
     _run_all(txt, rec)
 
 
+def test_attention_head_dim_64_pipeline_completes():
+    txt, rec = _attention(dim=64)
+    _run_all(txt, rec)
+
+
 def test_attention_flagged_blocks_take_the_bf16_path():
     # every value block flagged as not fitting f16: the producer loads V itself and the MMA issuers
     # and softmax take the two-part P path; the hand-overs are the same

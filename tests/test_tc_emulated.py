@@ -147,6 +147,15 @@ def test_late_completions_expose_a_planted_early_release():
         _check(p, t, {}, "tcgen05_attention", defer=True, mod=CompiledModule(bad, mod.kernels))
 
 
+@pytest.mark.parametrize("causal,opts", [(True, {}), (False, {}), (True, {"attn_pingpong": False}),
+                                         (True, {"attn_half": False})])
+def test_attention_head_dim_64_emulated(causal, opts):
+    """Head dim 64: a Q tile and a K/V block are one 64-column TMA box, PV has N=64 and O takes 64
+    TMEM columns per tile."""
+    p = irgen.attention_ir(1, 2, 512, 64, causal)
+    _check(p, data.make_inputs(p), opts, "tcgen05_attention")
+
+
 @pytest.mark.parametrize("shape", [(2, 32, 32, 64), (1, 200, 264, 72), (1, 130, 8, 16), (2, 128, 128, 96)])
 def test_gemm_edge_tiles_emulated(shape):
     """Shapes that are not tile multiples: TMA zero-fills past M, N and K, the epilogue stores rows
