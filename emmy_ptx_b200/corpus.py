@@ -20,7 +20,9 @@ Each builder returns a :class:`~.irgen.Problem` whose ``params["expr"]`` names t
 """
 from __future__ import annotations
 
-from .irgen import (Problem, TensorSpec, Tile, Axis, Load, Write, Assign, Let, Accum, Select, Cond, Loop,
+import math
+
+from .irgen import (Problem, TensorSpec, Tile, Axis, Load, Write, Assign, Let, Init, Accum, Select, Cond, Loop,
                     StridedLoop, WarpShuffle, TreeHalve, Smem, Sync, Lit, V, Bin, _graph)
 
 
@@ -643,6 +645,66 @@ def sdpa(batch, heads, seq, dim, causal, scale=None, mask=False):
                                       "scale": base.params["scale"], "mask": mask})
 
 
+def sdpa_rows(batch, heads, seq, dim, dv, causal, scale=None, threads=64):
+    """scaled_dot_product_attention with a value head dim ``dv`` that may differ from the query/key
+    head dim ``dim``, and head dims that are no multiple of 32 (40, 16): one thread per query row.
+    The thread loads its query row once (``dim`` lanes of one Load), and for each key row loads it,
+    forms the dot product as a pairwise sum, masks it (causal: a Select to -inf), and runs the online
+    softmax with ``dv`` output accumulators whose ``base`` is the rescaled previous value."""
+    scale = 1.0 / math.sqrt(dim) if scale is None else float(scale)
+    qs = [f"q{i}" for i in range(dim)]
+    ks = [f"k{i}" for i in range(dim)]
+    vs = [f"v{i}" for i in range(dv)]
+    os_ = [f"o{i}" for i in range(dv)]
+    dot = [Assign(f"pp{i}", "multiply", [qs[i], ks[i]]) for i in range(dim)]
+    terms, lvl = [f"pp{i}" for i in range(dim)], 0
+    while len(terms) > 1:
+        nxt = []
+        for j in range(0, len(terms) - 1, 2):
+            nm = "dp" if len(terms) == 2 else f"ds{lvl}_{j // 2}"
+            dot.append(Assign(nm, "add", [terms[j], terms[j + 1]]))
+            nxt.append(nm)
+        if len(terms) % 2:
+            nxt.append(terms[-1])                  # an odd term carries to the next level
+        terms, lvl = nxt, lvl + 1
+    sel = [(Bin(">", V("kv"), V("qi")), Lit(-math.inf))] if causal else []
+    body_k = [
+        Load(ks, "K", [V("b"), V("h"), V("kv"), 0], "bf16"),
+        *dot,
+        Assign("sc", "multiply", ["dp", Lit(scale)]),
+        Select("sm", [*sel, (None, "sc")]),
+        Assign("mn", "maximum", ["m", "sm"]),
+        Assign("dm", "subtract", ["m", "mn"]),
+        Assign("alpha", "exp", ["dm"]),
+        Assign("ds", "subtract", ["sm", "mn"]),
+        Assign("pe", "exp", ["ds"]),
+        Assign("ls", "multiply", ["l", "alpha"]),
+        Accum("l", "add", "pe", base="ls"),
+        Load(vs, "V", [V("b"), V("h"), V("kv"), 0], "bf16"),
+        *[Assign(f"os{i}", "multiply", [os_[i], "alpha"]) for i in range(dv)],
+        *[Assign(f"pv{i}", "multiply", ["pe", vs[i]]) for i in range(dv)],
+        *[Accum(os_[i], "add", f"pv{i}", base=f"os{i}") for i in range(dv)],
+        Accum("m", "maximum", "sm"),
+    ]
+    body = [Tile([Axis("b", batch), Axis("h", heads), Axis("qi", seq)], [
+        Load(qs, "Q", [V("b"), V("h"), V("qi"), 0], "bf16"),
+        Init("m", "f32", -math.inf),
+        Init("l", "f32", 0.0),
+        *[Init(o, "f32", 0.0) for o in os_],
+        Loop("kv", seq, body_k),
+        *[Assign(f"y{i}", "divide", [os_[i], "l"], "bf16") for i in range(dv)],
+        Write("O", [f"y{i}" for i in range(dv)], [V("b"), V("h"), V("qi"), 0], "bf16"),
+    ])]
+    args = [TensorSpec("Q", (batch, heads, seq, dim), "bf16", ("normal", 1.0)),
+            TensorSpec("K", (batch, heads, seq, dim), "bf16", ("normal", 1.0)),
+            TensorSpec("V", (batch, heads, seq, dv), "bf16", ("normal", 1.0)),
+            TensorSpec("O", (batch, heads, seq, dv), "bf16", output=True)]
+    rows = batch * heads * seq
+    return _problem("sdpa", f"sdpa_rows_{batch}x{heads}x{seq}x{dim}x{dv}{'_causal' if causal else ''}",
+                    "attention_rows", args, body, (rows + threads - 1) // threads, threads, rtol=1e-4,
+                    contraction=True, attention=True, causal=causal, scale=scale, mask=False)
+
+
 def scan_max_and_prod(rows=4, cols=64):
     """cm[r, c] = max of x[r, :c+1] (a running max: a thread per row, the Accum read after each step
     of a rolled Loop) and pr[r] = prod of x[r, :] (a warp per row: Accum multiply, then a shuffle
@@ -945,4 +1007,8 @@ CORPUS = {
     "k_sdpa_scale": lambda: sdpa(1, 4, 48, 32, False, scale=0.2),
     # a_mask: an explicit boolean attention mask (random here, so some rows start with masked keys)
     "k_sdpa_mask": lambda: sdpa(1, 2, 16, 32, False, mask=True),
+    # a_sdpa_odd and a_sdpa_causal2: a query/key head dim of 40 with 32-wide values, and a causal
+    # case with 32-wide queries and keys but 16-wide values
+    "k_sdpa_odd": lambda: sdpa_rows(1, 3, 48, 40, 32, False),
+    "k_sdpa_causal2": lambda: sdpa_rows(2, 4, 64, 32, 16, True),
 }
