@@ -635,8 +635,8 @@ def bmm_small(batch=2, m=32, n=32, k=64):
 def sdpa(batch, heads, seq, dim, causal, scale=None, mask=False):
     """scaled_dot_product_attention of bf16 Q, K, V [batch, heads, seq, dim] (optionally causal, with
     an explicit scale): the online-softmax nest of the attention IR at the small shapes of the
-    reference's attention cases.  Sequences that are not a multiple of the tensor-core kernel's
-    256-row query tiles run on the CUDA cores."""
+    reference's attention cases.  Head dim 64 or 128 with at least 128 rows (one whole query tile)
+    runs on the tensor cores; shorter sequences and other head dims run on the CUDA cores."""
     from .irgen import attention_ir
     base = attention_ir(batch, heads, seq, dim, causal, scale=scale, mask=mask)
     return Problem(f"sdpa_{batch}x{heads}x{seq}x{dim}{'_causal' if causal else ''}{'_mask' if mask else ''}",
@@ -1010,5 +1010,8 @@ CORPUS = {
     # a_sdpa_odd and a_sdpa_causal2: a query/key head dim of 40 with 32-wide values, and a causal
     # case with 32-wide queries and keys but 16-wide values
     "k_sdpa_odd": lambda: sdpa_rows(1, 3, 48, 40, 32, False),
+    # a_sdpa_big: 128 rows at head dim 64, on the tensor cores (one CTA per head, its second query
+    # tile entirely past S)
+    "k_sdpa_big": lambda: sdpa(1, 4, 128, 64, False),
     "k_sdpa_causal2": lambda: sdpa_rows(2, 4, 64, 32, 16, True),
 }

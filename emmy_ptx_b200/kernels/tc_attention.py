@@ -115,11 +115,18 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         raise ValueError("pair_poly takes 0-4 of every 4 score pairs")
     if pair_poly and poly_every:
         raise ValueError("pair_poly and poly_every are alternatives")
-    if seq % (BQ * TILES):
-        raise ValueError("tcgen05 attention needs S % 256 == 0")
-    if half and precise and seq // BKV > (BAR_BYTES - VFLAGS) // 4:
+    if seq < BQ:
+        raise ValueError(f"tcgen05 attention needs S >= {BQ} (one whole Q tile box inside the tensor)")
+    # a sequence that is no multiple of the CTA's 256 query rows: the last CTA's rows past S (and the
+    # key rows past S of its blocks) are zero-filled by TMA; their results are not stored, and a full
+    # (non-causal) launch masks the keys past S in the last block
+    nt = -(-seq // (BQ * TILES))
+    spad = nt * BQ * TILES
+    nblk = -(-seq // BKV)                        # key/value blocks holding data (value flags)
+    ragged = seq != spad
+    if half and precise and spad // BKV > (BAR_BYTES - VFLAGS) // 4:
         raise ValueError("the f16 path keeps one flag per kv block in shared memory: S <= 4096")
-    if trace and seq // BKV + 1 >= TRACE_SLOTS:
+    if trace and spad // BKV + 1 >= TRACE_SLOTS:
         raise ValueError("trace supports at most 64 key/value blocks")
     half = half and precise
     if pack_in_turn and (pack_after_turn or not pingpong):
@@ -127,8 +134,6 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     if defer_sum and (poly_every or not pack_after_turn):
         raise ValueError("defer_sum goes with the MUFU-only exps packed after the turn")
     threads = THREADS
-    nblk = seq // BKV
-    nt = seq // (BQ * TILES)
     bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
     if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):
         raise ValueError(f"bh_range {bh_range} outside the {batch * heads} (batch, head) pairs")
@@ -200,7 +205,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         a(f"shl.b32 {nb}, {t}, 2;")
         a(f"add.u32 {nb}, {nb}, 4;")                    # tile 1 sees kv blocks 0..4t+3, tile 0 0..4t+1
     else:
-        a(f"mov.u32 {nb}, {seq // BKV};")
+        a(f"mov.u32 {nb}, {nblk};")
     a(f"shl.b32 {row0}, {t}, 8;")                        # first query row of this CTA
 
     raw, base = a.r(), a.r()
@@ -283,7 +288,16 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"add.u32 {fk}, {vbase}, {bk};")
             a(f"mul.wide.u32 {ga}, {fk}, 4;")
             a(f"add.s64 {ga}, {ga}, {vfp};")
-            a(f"@{pk} ld.global.nc.u32 {fk}, [{ga}];")
+            if ragged and causal:
+                # the causal diagonal's blocks past S hold no data (zero-filled by TMA from the f16
+                # copy): flag 0, and no load past this (batch, head)'s flags
+                pd = a.r("p")
+                a(f"setp.lt.u32 {pd}, {bk}, {nblk};")
+                a(f"and.pred {pd}, {pd}, {pk};")
+                a(f"mov.u32 {fk}, 0;")
+                a(f"@{pd} ld.global.nc.u32 {fk}, [{ga}];")
+            else:
+                a(f"@{pk} ld.global.nc.u32 {fk}, [{ga}];")
             a(f"mad.lo.u32 {sa}, {bk}, 4, {bars};")
             a(f"@{pk} st.shared.u32 [{sa}+{VFLAGS}], {fk};")
         a("fence.acq_rel.cta;")
@@ -755,6 +769,18 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"setp.lt.s32 {pm}, {lim}, {c};")
             a(f"@{pm} mov.b32 {s_[c]}, 0fFF800000;")
         a.label(l_nomask)
+    elif seq % BKV:
+        # kv = 64*jj + c past the sequence is masked: c > S - 1 - 64*jj, in the last block only
+        l_nokey = a.L("nokey")
+        klim, kv0k = a.r(), a.r()
+        a(f"shl.b32 {kv0k}, {jj}, 6;")
+        a(f"sub.s32 {klim}, {seq - 1}, {kv0k};")
+        pkm = a.r("p")
+        a(f"setp.ge.s32 {pkm}, {klim}, {BKV - 1};")
+        a(f"@{pkm} bra {l_nokey};")                        # the same for every thread of the CTA
+        for c in range(seq % BKV, BKV):
+            a(f"mov.b32 {s_[c]}, 0fFF800000;")
+        a.label(l_nokey)
     # row max in the scaled log2 domain: 8 independent chains of three-input maxima (columns k,
     # k+8, ...), then 8 -> 3 -> 1
     lvl = [a.r("f") for _ in range(8)]
@@ -1068,6 +1094,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"mad.lo.u32 {grow}, {bh}, {seq}, {grow0};")         # row of O in [batch*heads*S, D]
     a(f"mul.wide.u32 {oaddr}, {grow}, {D * 2};")
     a(f"add.s64 {oaddr}, {oaddr}, {o_ptr};")
+    sto = ""
+    if ragged:
+        prow = a.r("p")
+        a(f"setp.lt.u32 {prow}, {grow0}, {seq};")         # rows past S are not stored
+        sto = f"@{prow} "
     for c in range(D // 32):
         src = a.r()
         a(f"add.u32 {src}, {ocol}, {32 * c};")
@@ -1081,8 +1112,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             a(f"mul.f32 {regs[2 * k + 1]}, {regs[2 * k + 1]}, {inv};")
             a(f"cvt.rn.bf16x2.f32 {w}, {regs[2 * k + 1]}, {regs[2 * k]};")
             words.append(w)
-        a(f"st.global.v8.b32 [{oaddr}+{64 * c}], {{{', '.join(words[:8])}}};")
-        a(f"st.global.v8.b32 [{oaddr}+{64 * c + 32}], {{{', '.join(words[8:])}}};")
+        a(f"{sto}st.global.v8.b32 [{oaddr}+{64 * c}], {{{', '.join(words[:8])}}};")
+        a(f"{sto}st.global.v8.b32 [{oaddr}+{64 * c + 32}], {{{', '.join(words[8:])}}};")
     a.label(l_noepi)
 
     # ---------------- teardown ---------------------------------------------------------------

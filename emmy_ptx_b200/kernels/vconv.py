@@ -6,7 +6,8 @@ loads and stores, 256 threads) into a scratch tensor of the same shape, and the 
 whether it fits: 0 when every |v| is at most 65,280 (the largest bf16 value below the f16 overflow
 threshold), 1 otherwise.  The attention kernel then loads each block from the f16 copy or, for a
 flagged block, from V itself with P as two bf16 parts.  Each CTA writes its own flag, so nothing needs
-zeroing first.
+zeroing first.  When S is no multiple of 64 each (batch, head) ends with a partial block: its rows past
+S are neither read nor written, and its flag covers the rows it has.
 """
 from __future__ import annotations
 
@@ -29,16 +30,18 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
     value block (64, or 128 for the 128-row kernel): one CTA and one flag per block."""
     if block_rows not in (64, 128):
         raise ValueError("the value pre-pass converts 64- or 128-row blocks")
-    if seq % block_rows:
-        raise ValueError(f"the value pre-pass needs S % {block_rows} == 0")
+    ragged = seq % block_rows != 0
+    if ragged and block_rows != BLOCK_ROWS:
+        raise ValueError(f"the {block_rows}-row value pre-pass needs S % {block_rows} == 0")
     if dim not in (64, 128):
         raise ValueError("the value pre-pass converts head dim 64 or 128")
     block_bytes = block_rows * dim * 2
     bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
     if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):
         raise ValueError(f"bh_range {bh_range} outside the {batch * heads} (batch, head) pairs")
-    blocks = nbh * (seq // block_rows)
-    first = bh0 * (seq // block_rows)
+    per_bh = -(-seq // block_rows)          # blocks per (batch, head); the last one partial when ragged
+    blocks = nbh * per_bh
+    first = bh0 * per_bh
     vec = block_bytes // 16 // THREADS      # 16-byte vectors per thread
     grid = blocks if not ctas else min(blocks, int(ctas))
     a = Asm()
@@ -58,7 +61,21 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
         a(f"setp.ge.u32 {pend}, {blk}, {first + blocks};")
         a(f"@{pend} bra {l_done};")
     off = a.r("rd")
-    a(f"mul.wide.u32 {off}, {blk}, {block_bytes};")
+    lim = None
+    if ragged:
+        # block j of pair bh starts at row bh*S + 64*j; its rows past S are neither read nor written
+        # (lim = the block's valid bytes, compared with each 16-byte vector's offset in the block)
+        bhr, jr, rows_, lim = a.r(), a.r(), a.r(), a.r()
+        a(f"div.u32 {bhr}, {blk}, {per_bh};")
+        a(f"rem.u32 {jr}, {blk}, {per_bh};")
+        a(f"mul.lo.u32 {rows_}, {jr}, {block_rows};")
+        a(f"sub.u32 {lim}, {seq}, {rows_};")
+        a(f"min.u32 {lim}, {lim}, {block_rows};")
+        a(f"mul.lo.u32 {lim}, {lim}, {dim * 2};")
+        a(f"mad.lo.u32 {rows_}, {bhr}, {seq}, {rows_};")
+        a(f"mul.wide.u32 {off}, {rows_}, {dim * 2};")
+    else:
+        a(f"mul.wide.u32 {off}, {blk}, {block_bytes};")
     t16 = a.r("rd")
     a(f"mul.wide.u32 {t16}, {tid}, 16;")
     a(f"add.s64 {off}, {off}, {t16};")
@@ -67,10 +84,19 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
     a(f"add.s64 {dst}, {p16}, {off};")
     m = a.r()
     a(f"mov.u32 {m}, 0;")
-    ws_all = []
+    ws_all, preds = [], []
     for v in range(vec):
         ws = [a.r() for _ in range(4)]
-        a(f"ld.global.nc.v4.b32 {{{', '.join(ws)}}}, [{src}+{v * THREADS * 16}];")
+        g = ""
+        if ragged:
+            pin, boff = a.r("p"), a.r()
+            a(f"mad.lo.u32 {boff}, {tid}, 16, {v * THREADS * 16};")
+            a(f"setp.lt.u32 {pin}, {boff}, {lim};")
+            for w in ws:
+                a(f"mov.u32 {w}, 0;")
+            g = f"@{pin} "
+        preds.append(g)
+        a(f"{g}ld.global.nc.v4.b32 {{{', '.join(ws)}}}, [{src}+{v * THREADS * 16}];")
         ws_all.append(ws)
     for v, ws in enumerate(ws_all):
         out = []
@@ -82,7 +108,7 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
             a(f"and.b32 {hi_}, {w}, -65536;")
             a(f"cvt.rn.f16x2.f32 {f_}, {hi_}, {lo_};")
             out.append(f_)
-        a(f"st.global.v4.b32 [{dst}+{v * THREADS * 16}], {{{', '.join(out)}}};")
+        a(f"{preds[v]}st.global.v4.b32 [{dst}+{v * THREADS * 16}], {{{', '.join(out)}}};")
     mlo, mhi, p1, p2, ovf = a.r(), a.r(), a.r("p"), a.r("p"), a.r("p")
     a(f"and.b32 {mlo}, {m}, 65535;")
     a(f"shr.u32 {mhi}, {m}, 16;")
@@ -110,5 +136,5 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
         "grid": [grid, 1, 1], "block": [THREADS, 1, 1], "dyn_smem": 0,
         "align": {vn: 16, v16n: 16, fn: 4}, "zero_outputs": [],
         "scratch": [{"name": v16n, "dtype": "f16", "shape": [batch, heads, seq, dim]},
-                    {"name": fn, "dtype": "i32", "shape": [batch * heads * (seq // block_rows)]}],
+                    {"name": fn, "dtype": "i32", "shape": [batch * heads * per_bh]}],
     }

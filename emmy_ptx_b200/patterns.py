@@ -15,7 +15,9 @@ structural and fails closed — anything not recognised exactly is left to the C
 * every Accum is ``add`` of a product of one value loaded from X's buffer and one from Y's,
   seeded with 0; every Write goes to the output and writes only accumulators; nothing else is
   written to global memory;
-* the tile sizes divide the shapes (M % 128, N % 256, K % 64).
+* the GEMM's N and K are multiples of 8 (16-byte TMA rows; partial 128 x 256 edge tiles are
+  zero-filled on load and clipped on store); attention has head dim 64 or 128 and S >= 128 (rows
+  and keys past S in the last 256-row query chunk are zero-filled, masked and not stored).
 
 Those checks find the operands, shapes and (for attention) the mask and scale.  The final gate is
 stricter: the kernel body must equal, up to the buffer names, the canonical CUDA-core nest for those
@@ -374,10 +376,11 @@ def try_lower(graph, node, kmeta, prefix, options):
     if hit is not None:
         Q, K, V, O, bt, hd, seq, dim, causal, scale = hit
         from .kernels import tc_attention
-        if dim not in (64, 128) or seq % (tc_attention.BQ * tc_attention.TILES):
+        if dim not in (64, 128) or seq < tc_attention.BQ:
             return None
-        if dim != tc_attention.D:
-            # head dim 64: the default schedule only (the other forms are built for 128)
+        if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES):
+            # head dim 64, or S no multiple of 256: the default schedule only (the other forms are
+            # built for head dim 128 and whole 256-row query chunks)
             options = {k: v for k, v in options.items()
                        if k not in ("attn_persistent", "attn_kv128", "attn_overlap")}
         precise = bool(options.get("attn_precise", True))

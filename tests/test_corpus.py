@@ -70,7 +70,8 @@ def test_corpus_assembles_for_sm100a(key, tmp_path):
     r = subprocess.run([PTXAS, "-arch=sm_100a", str(src), "-o", str(tmp_path / "k.cubin")],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
-    entries = [rec["entry"] for rec in mod.kernels]
+    # a tensor-core attention adds its value pre-pass launch before the kernel's own entry
+    entries = [rec["entry"] for rec in mod.kernels if rec.get("kind") != "value_prepass"]
     want = [ln[0] for ln in getattr(p, "launches", [])] or [p.entry]
     assert entries == want
 

@@ -156,3 +156,28 @@ def test_attention_head_dim_64(causal):
         if causal:
             s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
         compare(got["O"][b, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"d64 ({b},{h})", rms_floor=True)
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 2, 320, 128), True), ((1, 1, 200, 128), False),
+                                          ((1, 4, 128, 64), False), ((2, 1, 300, 64), True)])
+def test_attention_ragged_sequence(shape, causal):
+    """S no multiple of 256 on the tensor cores: small cases against the oracle, and [1, 4, 1000, 128]
+    (a partial last key block, rows past S that would land in the next head's rows if stored) against
+    float64 on every head."""
+    import math
+    p = irgen.attention_ir(*shape, causal)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"ragged {shape} causal={causal}", rms_floor=True)
+    p = irgen.attention_ir(1, 4, 1000, 128, causal)
+    t = data.make_inputs(p)
+    got, ex = _run_ours(p, t)
+    assert ex.error_code() == 0
+    for h in range(4):
+        q, k, v = (t[n][0, h].double() for n in ("Q", "K", "V"))
+        s_ = (q @ k.T) / math.sqrt(128)
+        if causal:
+            s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
+        compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"S=1000 head {h}", rms_floor=True)

@@ -49,6 +49,14 @@ def test_attention_head_dim_64_pipeline_completes():
     _run_all(txt, rec)
 
 
+@pytest.mark.parametrize("seq,causal", [(320, True), (200, True), (200, False), (700, False)])
+def test_attention_ragged_sequence_pipeline_completes(seq, causal):
+    # S no multiple of 256 (or 64): the same hand-overs, with the key-limit mask and the rows past S
+    # skipped at the store
+    txt, rec = _attention(seq=seq, causal=causal)
+    _run_all(txt, rec)
+
+
 def test_attention_flagged_blocks_take_the_bf16_path():
     # every value block flagged as not fitting f16: the producer loads V itself and the MMA issuers
     # and softmax take the two-part P path; the hand-overs are the same

@@ -168,3 +168,19 @@ def test_gemm_from_the_unscheduled_matmul_emulated():
     # the thread-per-element matmul nest lowered to the tcgen05 GEMM; the oracle interprets the nest
     p = irgen.bmm_naive_ir(1, 128, 256, 64)
     _check(p, data.make_inputs(p), {"sms": 1}, "tcgen05_gemm")
+
+
+@pytest.mark.parametrize("shape,causal,opts", [
+    ((1, 2, 320, 128), True, {}),                 # S % 64 == 0, not % 256: a half-empty last chunk
+    ((1, 1, 200, 128), True, {}),                 # a partial last key block on the causal diagonal
+    ((1, 1, 200, 128), False, {}),                # keys past S masked in the last block
+    ((1, 2, 130, 64), False, {"attn_half": False}),
+    ((1, 4, 128, 64), False, {}),                 # the reference's a_sdpa_big shape: tile 1 all past S
+    ((2, 1, 300, 64), True, {"attn_pingpong": False}),
+])
+def test_attention_ragged_sequence_emulated(shape, causal, opts):
+    """S no multiple of the 256-row query chunk: TMA zero-fills query and key rows past S, a full
+    launch masks the keys past S, rows past S are not stored, and the value pre-pass neither reads
+    nor writes past S (the emulator raises on an access outside an allocation)."""
+    p = irgen.attention_ir(*shape, causal)
+    _check(p, data.make_inputs(p), opts, "tcgen05_attention")
