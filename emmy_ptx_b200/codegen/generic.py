@@ -21,7 +21,7 @@ from __future__ import annotations
 import math
 import os
 
-from ..ir import dim_int, dt_name, dt_bytes, IRError
+from ..ir import dim_int, dt_name, dt_bytes, IRError, walk
 from .affine import Affine, Atom, reg_atom, div_const, rem_const, recombine, INT_MAX
 from .ptx import PtxBuilder, f32_imm
 from . import mathlib
@@ -122,6 +122,13 @@ class KernelEmitter:
                 raise Unsupported(f"the fused exchange needs a one-element output, not {x.get('partial')!r}")
             if x.get("dtype") not in ("f32", "i32") or dt_name(self.dtypes[x["partial"]]) != x["dtype"]:
                 raise Unsupported("the fused exchange adds an f32 or i32 partial of the output's type")
+        # outputs that accumulate in a scratch the kernel zeroes itself (option ``self_zeroing``; the
+        # fused exchange's partial always does): see _last_block_epilogue
+        self.acc_outs: dict[str, int] = {}
+        if self.opts.get("self_zeroing") or self.exchange:
+            self.acc_outs = self._self_zeroing_outputs()
+            if self.exchange and self.exchange["partial"] not in self.acc_outs:
+                raise Unsupported("the fused exchange needs a partial that only atomic adds write")
         self.err = None
         self.tma = None
         if self.opts.get("tma_stripes", True) is not False and self.T:
@@ -131,6 +138,36 @@ class KernelEmitter:
                 # one 8-byte mbarrier per commit group that can be in flight
                 self.smem[TMA_BARS] = ((2 * self.tma["nbar"],), "i32", 16)
         self._plan_smem()
+
+    def _self_zeroing_outputs(self) -> dict:
+        """Byte offsets in the accumulator scratch of the outputs that can skip the zeroing before the
+        launch: listed in ``zero_outputs``, written only by atomic adds (scalar 32-bit, the only atomic
+        writes the emitter makes), never read by the kernel, at most 32 elements (warp 0 of the last
+        block moves them), and a 1-D launch whose grid size is known.  Word 0 of the scratch is the
+        block ticket; the accumulators start at byte 16, each 16-byte aligned."""
+        if not self.G or not self.T:
+            return {}
+        cand = [n for n in (self.kmeta.get("zero_outputs") or []) if n in self.params]
+        stmts = []
+        walk(self.op.body, stmts.append)
+        for st in stmts:
+            cls = type(st).__name__
+            if cls == "Write" and st.output in cand and not getattr(st, "atomic", False):
+                cand.remove(st.output)
+            elif cls == "Load" and st.input in cand:
+                cand.remove(st.input)
+            elif cls == "CpAsyncCopy" and st.src in cand:
+                cand.remove(st.src)
+        out, off = {}, 16
+        for n in cand:
+            elems = 1
+            for x in self.shapes.get(n, (0,)):
+                elems *= int(x)
+            if not 1 <= elems <= 32 or dt_name(self.dtypes[n]) not in ("f32", "i32", "u32"):
+                continue
+            out[n] = off
+            off += (4 * elems + 15) // 16 * 16
+        return out
 
     def _scan(self, body) -> None:
         for st in body or ():
@@ -226,6 +263,19 @@ class KernelEmitter:
                 self.err = b.reg("b64")
                 b.emit(f"ld.param.u64 {self.err}, [p_err];")
                 b.emit(f"cvta.to.global.u64 {self.err}, {self.err};")
+        if self.acc_outs:
+            # the atomic adds of these outputs go to their accumulators in the scratch; the output
+            # pointers are kept for the last block's stores
+            self.acc = b.reg("b64")
+            b.emit(f"ld.param.u64 {self.acc}, [p_acc];")
+            b.emit(f"cvta.to.global.u64 {self.acc}, {self.acc};")
+            self.real_out = {}
+            for n, off in self.acc_outs.items():
+                r = b.reg("b64")
+                b.emit(f"add.s64 {r}, {self.acc}, {off};")
+                self.real_out[n] = self.preg[n]
+                self.preg[n] = r
+                self.palign[n] = 16
             self.tid_reg = tid
 
     # ---- integers -------------------------------------------------------------------------
@@ -1091,13 +1141,15 @@ class KernelEmitter:
         self.grp = b.reg("b32")
         b.emit(f"mov.u32 {self.grp}, 0;")
 
-    def _exchange_epilogue(self) -> None:
-        """The multi-GPU sum's exchange, fused after the reduction: every block meets at a barrier (its
-        atomic adds to the partial are issued), thread 0 releases them and takes a ticket from the
-        exchange buffer; in the block whose ticket is the last, warp 0 resets the ticket, acquires
-        the other blocks' adds and runs the peer exchange (kernels/peer_sum.py), which leaves the
-        rank-ordered total of every rank's partial in the output."""
-        from ..kernels import peer_sum
+    def _last_block_epilogue(self) -> None:
+        """Self-zeroing accumulators, and the multi-GPU sum's exchange fused after the reduction.
+
+        Every block meets at a barrier (its atomic adds are issued); thread 0 releases them and takes a
+        ticket (word 0 of the accumulator scratch).  In the block whose ticket is the last, warp 0
+        resets the ticket, acquires the other blocks' adds, takes each accumulator with an atomic
+        exchange against 0 (so the scratch is zero again for the next launch) and stores it to the
+        output.  With the exchange option it then runs the peer exchange (kernels/peer_sum.py), which
+        replaces this rank's partial in the output by the rank-ordered total of every rank's."""
         b, x = self.b, self.exchange
         end = b.label("_xend")
         lane, w, tk = b.reg("b32"), b.reg("b32"), b.reg("b32")
@@ -1110,16 +1162,32 @@ class KernelEmitter:
         b.emit(f"setp.eq.u32 {p0}, {lane}, 0;")
         b.emit(f"mov.u32 {tk}, 0;")
         b.emit(f"@{p0} fence.acq_rel.gpu;")
-        b.emit(f"@{p0} atom.global.add.u32 {tk}, [{self.xch}+{peer_sum.TICKET}], 1;")
+        b.emit(f"@{p0} atom.global.add.u32 {tk}, [{self.acc}], 1;")
         b.emit(f"shfl.sync.idx.b32 {tk}, {tk}, 0, 31, -1;")
         b.emit(f"setp.ne.u32 {plast}, {tk}, {self.G - 1};")
         b.emit(f"@{plast} bra {end};")
-        b.emit(f"@{p0} st.global.u32 [{self.xch}+{peer_sum.TICKET}], 0;")
-        b.emit(f"@{p0} fence.acq_rel.gpu;")
-        out = self.preg[x["partial"]]
-        peer_sum.emit_exchange(lambda line: b.place(line[:-1]) if line.endswith(":") else b.emit(line),
-                               b.reg, lambda tag: b.label("_" + tag), lane, out, self.xch, self.peers,
-                               self.err, int(x["rank"]), int(x["world"]), x["dtype"])
+        b.emit(f"@{p0} st.global.u32 [{self.acc}], 0;")
+        b.emit("fence.acq_rel.gpu;")
+        for n, off in self.acc_outs.items():
+            elems = 1
+            for d in self.shapes[n]:
+                elems *= int(d)
+            skip = b.label("_accdone")
+            pin, a_acc, a_out, v = b.reg("pred"), b.reg("b64"), b.reg("b64"), b.reg("b32")
+            b.emit(f"setp.ge.u32 {pin}, {lane}, {elems};")
+            b.emit(f"@{pin} bra {skip};")
+            b.emit(f"mul.wide.u32 {a_acc}, {lane}, 4;")
+            b.emit(f"add.s64 {a_out}, {a_acc}, {self.real_out[n]};")
+            b.emit(f"add.s64 {a_acc}, {a_acc}, {self.preg[n]};")
+            b.emit(f"atom.global.exch.b32 {v}, [{a_acc}], 0;")
+            b.emit(f"st.global.b32 [{a_out}], {v};")
+            b.place(skip)
+        b.emit("bar.warp.sync -1;")
+        if x:
+            from ..kernels import peer_sum
+            peer_sum.emit_exchange(lambda line: b.place(line[:-1]) if line.endswith(":") else b.emit(line),
+                                   b.reg, lambda tag: b.label("_" + tag), lane, self.real_out[x["partial"]],
+                                   self.xch, self.peers, self.err, int(x["rank"]), int(x["world"]), x["dtype"])
         b.place(end)
 
     def _tma_bar(self, group: str) -> str:
@@ -1529,8 +1597,8 @@ class KernelEmitter:
         self.prepare()
         self.prologue()
         self.stmts(self.op.body)
-        if self.exchange:
-            self._exchange_epilogue()
+        if self.acc_outs:
+            self._last_block_epilogue()
         body, decls = self.b.lines(), self.b.reg_decls()
         if self.opts.get("regalloc", os.environ.get("EMMY_B200_REGALLOC", "1") != "0"):
             from .regalloc import allocate
@@ -1538,6 +1606,17 @@ class KernelEmitter:
             body, counts = allocate(body)
             by_prefix = {pre[1:]: ty for pre, ty in REG_CLASSES.values()}
             decls = [f"\t.reg {by_prefix[c]} %{c}<{k + 1}>;" for c, k in sorted(counts.items())]
+        extra = []
+        if self.exchange:
+            extra += [{"name": "__xch", "kind": "buffer", "param": "p_xch"},
+                      {"name": "__peers", "kind": "buffer", "param": "p_peers"}]
+        acc_name, acc_words = f"{self.prefix}{self.name}__acc", 0
+        if self.acc_outs:
+            # the accumulator scratch: the runtime allocates it zeroed once; every launch leaves it zero
+            acc_words = max(16 + 4 * 32, max(self.acc_outs.values()) + 4 * 32) // 4
+            extra.append({"name": acc_name, "kind": "buffer", "param": "p_acc"})
+        if self.tma is not None or self.exchange:
+            extra.append({"name": "__err", "kind": "errword"})
         return {
             "name": self.name,
             "params": list(self.params),
@@ -1552,12 +1631,11 @@ class KernelEmitter:
             "grid": self.kmeta.get("grid") or [],
             "reqntid": self.T,
             "align": dict(self.palign),
-            "zero_outputs": list(self.kmeta.get("zero_outputs") or []),
+            "zero_outputs": [n for n in (self.kmeta.get("zero_outputs") or []) if n not in self.acc_outs],
             "pdl": self.pdl,
             **({"tmaps": self.tma["tmaps"]} if self.tma is not None else {}),
-            **({"extra": ([{"name": "__xch", "kind": "buffer", "param": "p_xch"},
-                           {"name": "__peers", "kind": "buffer", "param": "p_peers"}] if self.exchange else [])
-                + [{"name": "__err", "kind": "errword"}]}
-               if self.tma is not None or self.exchange else {}),
+            **({"extra": extra} if extra else {}),
+            **({"scratch": [{"name": acc_name, "dtype": "i32", "shape": [acc_words], "zeroed": True}],
+                "self_zeroing": sorted(self.acc_outs)} if self.acc_outs else {}),
             **({"exchange": dict(self.exchange)} if self.exchange else {}),
         }

@@ -46,7 +46,7 @@ def launch_record(b: dict) -> dict:
         "zero_outputs": b.get("zero_outputs", []),
         "kind": b.get("kind", "generic"),
     }
-    for k in ("tmaps", "cluster", "extra", "pdl", "scratch", "stream", "after", "exchange"):
+    for k in ("tmaps", "cluster", "extra", "pdl", "scratch", "stream", "after", "exchange", "self_zeroing"):
         if b.get(k):
             rec[k] = b[k]
     if b.get("carveout") is not None:

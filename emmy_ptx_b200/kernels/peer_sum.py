@@ -4,9 +4,8 @@ Config 2 at N GPUs: each rank reduces its shard into a one-element partial, then
 total.  Instead of a one-element ``ncclAllReduce`` the partials go through an exchange buffer that every
 rank allocates and maps into every other rank's process (CUDA IPC, ``dist.PeerAllReduce``):
 
-* the buffer of rank q holds a step counter and a block ticket (only rank q touches them), two slots
-  per source rank (``DATA``, double-buffered by the step's parity) and one flag per source rank
-  (``FLAGS``);
+* the buffer of rank q holds a step counter (only rank q touches it), two slots per source rank
+  (``DATA``, double-buffered by the step's parity) and one flag per source rank (``FLAGS``);
 * one warp per rank: lane 0 advances the step counter to e; lane r (< N) writes this rank's partial into
   slot [e & 1][rank] of rank r's buffer and then, with a release store at system scope, e into flag
   [rank] of that buffer;
@@ -21,13 +20,13 @@ read step e's slots.  All loads and stores are plain peer accesses; no multicast
 
 :func:`peer_sum_entry` is the exchange as its own kernel, launched right after the reduction.
 :func:`emit_exchange` writes the same steps into another kernel: the generic emitter's ``exchange``
-option appends them to the reduction kernel, run by warp 0 of the block that finishes last (a ticket
-counter in the exchange buffer picks it), so the reduction and the exchange are one launch.
+option appends them to the reduction kernel, run by warp 0 of the block that finishes last (the ticket
+of the reduction's self-zeroing accumulator scratch picks it), so the reduction and the exchange are one
+launch and the partial needs no zeroing before it.
 """
 from __future__ import annotations
 
 STEP = 0                 # u32 step counter (written by the owning rank only)
-TICKET = 16              # u32 block ticket of the fused form (reset by the last block)
 DATA = 256               # u64 slots [2][MAX_RANKS]
 FLAGS = 1024             # u32 flags [MAX_RANKS]
 MAX_RANKS = 32

@@ -58,6 +58,9 @@ class Executable:
             for spec in rec.get("scratch", []):
                 if spec["name"] not in self.scratch:
                     self.scratch[spec["name"]] = self._device_tensor(tuple(spec["shape"]), torch_dtype(spec["dtype"]))
+                    if spec.get("zeroed"):
+                        # a self-zeroing accumulator: zero once here, every launch leaves it zero
+                        self.scratch[spec["name"]].zero_()
         self.side = None
         names = [rec["entry"] for rec in compiled.kernels]
         for i, rec in enumerate(compiled.kernels):

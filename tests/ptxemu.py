@@ -550,9 +550,11 @@ class Emulator:
         v = val(ops[1] if op.startswith("red") else ops[2])
         size, fmt = _TY[ty]
         old = int.from_bytes(mem.load(a, size), "little")
-        if ".add" not in op:
+        if ".exch" in op:
+            new = v & ((1 << (8 * size)) - 1)
+        elif ".add" not in op:
             raise NotImplementedError(op)
-        if ty == "f32":
+        elif ty == "f32":
             new = f2b(b2f(old) + b2f(v))
         else:
             new = (old + v) & ((1 << (8 * size)) - 1)

@@ -201,7 +201,9 @@ def _emulate_fused(world, rank, dtype, peers_by_step, launches=2):
     mod = compile_graph(Graph.from_dict(p.graph), p.meta(),
                         {"exchange": {"rank": rank, "world": world, "partial": "out", "dtype": dtype}})
     rec = mod.kernels[0]
-    assert [s["name"] for s in rec["extra"]] == ["__xch", "__peers", "__err"]
+    acc_spec = rec["scratch"][0]
+    assert [s["name"] for s in rec["extra"]] == ["__xch", "__peers", acc_spec["name"], "__err"]
+    assert rec["zero_outputs"] == [] and rec["self_zeroing"] == ["out"] and acc_spec["zeroed"]
     t = data.make_inputs(p)
     npdt = np.float32 if dtype == "f32" else np.int32
     mem = Memory()
@@ -209,17 +211,19 @@ def _emulate_fused(world, rank, dtype, peers_by_step, launches=2):
     bufs = [mem.alloc(np.zeros(peer_sum.BUF_BYTES, np.uint8)) for _ in range(world)]
     table = mem.alloc(np.array(bufs, np.uint64))
     err = mem.alloc(np.zeros(4, np.int32))
+    acc = mem.alloc(np.zeros(acc_spec["shape"][0], np.int32))  # zeroed once, as the runtime does
     own = mem.array(bufs[rank], np.uint8, (-1,))
     got = []
     for e in range(1, launches + 1):
         for k, v in peers_by_step[e - 1].items():
             _publish(own, world, e, k, v, dtype)
-        out = mem.alloc(np.zeros(1, npdt))                      # the runtime zeroes the output
+        out = mem.alloc(np.full(1, 0x7F7F7F7F, np.uint32).view(npdt))   # not zeroed: the kernel writes it
         Emulator(mod.ptx, rec["entry"]).run(rec["grid"][0], rec["block"][0],
                                             {"p_x": x, "p_out": out, "p_xch": bufs[rank], "p_peers": table,
-                                             "p_err": err}, mem, rec.get("dyn_smem", 0))
+                                             "p_acc": acc, "p_err": err}, mem, rec.get("dyn_smem", 0))
         got.append(mem.array(out, npdt, (1,))[0])
-    assert struct.unpack("<I", bytes(own[peer_sum.TICKET:peer_sum.TICKET + 4]))[0] == 0   # reset each launch
+        # the ticket and the accumulator are zero again for the next launch
+        assert not mem.array(acc, np.int32, (acc_spec["shape"][0],)).any()
     return t, got, int(mem.array(err, np.int32, (4,))[0])
 
 
