@@ -113,7 +113,7 @@ TRAFFIC = {
     "c2": (268.443904e6 + 4.902912e6) * 4,       # 2^26 -> 2^28 elements
     "c2i": (268.443904e6 + 4.902912e6) * 4,      # same kernel shape, i32 elements
     "c3": (201.394176e6 + 44.741632e6) * 2,      # 4096 -> 8192 rows
-    "c4": (192.727040e6 + 105.907456e6) * 8,     # 2 -> 16 batches
+    "c4": (195.336192e6 + 104.641024e6) * 8,     # 2 -> 16 batches (the CTA-pair kernel)
     "c1": 16.793088e6 + 0.0,                     # captured at full size (y stays in L2 at kernel end)
     "c5": (143.738112e6 + 14.620416e6) * 8 + 2 * 268.435456e6,   # 32 -> 256 (b,h) pairs, + pre-pass
 }

@@ -314,8 +314,11 @@ class TcEmulator(Emulator):
             if a + 16 > len(smem):
                 raise IndexError(f"TMA box past shared memory ({a})")
             smem[a:a + 16] = out[off:off + 16]
+        self._complete_tx(mb, len(out))
+
+    def _complete_tx(self, mb, nbytes):
         b = self.mbars[mb]
-        b.tx -= len(out)
+        b.tx -= nbytes
         if b.tx < 0:
             raise RuntimeError("TMA delivered more bytes than the mbarrier expects")
         self._settle(mb, b)

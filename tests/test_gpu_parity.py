@@ -116,7 +116,7 @@ def test_tensor_core_gemm_many_tiles_per_cta():
     p = irgen.SMALL["c4tc"]()
     t = data.make_inputs(p)
     want = oracle_outputs(p, t)
-    got, ex = _run_ours(p, t, sms=2)
+    got, ex = _run_ours(p, t, sms=2, gemm_pair=False)
     assert ex.records[0]["kind"] == "tcgen05_gemm" and ex.records[0]["grid"] == [2, 1, 1]
     assert ex.error_code() == 0
     compare(got["C"], want["C"], "f32", 1e-4, "c4tc sms=2")
@@ -129,7 +129,7 @@ def test_full_bmm_tensor_core_sampled():
     B = (torch.randn(p.spec("B").shape, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
     C = torch.empty(p.spec("C").shape, dtype=torch.float32, device="cuda")
     mod = compile_graph(Graph.from_dict(p.graph), p.meta())
-    assert mod.kernels[0]["kind"] == "tcgen05_gemm"
+    assert mod.kernels[0]["kind"] == "tcgen05_gemm_pair"
     ex = Executable(mod)
     ex({"A": A, "B": B, "C": C})
     torch.cuda.synchronize()

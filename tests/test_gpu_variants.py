@@ -92,8 +92,11 @@ def test_gemm_from_the_unscheduled_matmul():
     t = data.make_inputs(p)
     want = oracle_outputs(p, t)
     got, ex = _run_ours(p, t)
-    assert ex.records[0]["kind"] == "tcgen05_gemm" and ex.error_code() == 0
+    assert ex.records[0]["kind"] == "tcgen05_gemm_pair" and ex.error_code() == 0
     compare(got["C"], want["C"], "f32", rtol_for(p), "bmm naive")
+    got, ex = _run_ours(p, t, gemm_pair=False)
+    assert ex.records[0]["kind"] == "tcgen05_gemm" and ex.error_code() == 0
+    compare(got["C"], want["C"], "f32", rtol_for(p), "bmm naive, one CTA per tile")
 
 
 @pytest.mark.parametrize("shape", [(2, 200, 264, 72), (1, 130, 8, 16), (3, 1000, 1000, 1000)])
@@ -103,7 +106,7 @@ def test_gemm_edge_tiles(shape):
     kernel skips, or one it writes past, shows."""
     p = irgen.bmm_naive_ir(*shape)
     t = data.make_inputs(p)
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"gemm_pair": False})
     assert mod.kernels[0]["kind"] == "tcgen05_gemm"
     ex = Executable(mod)
     td = {k: v.cuda() for k, v in t.items()}

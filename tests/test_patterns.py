@@ -25,16 +25,18 @@ def test_bmm_ir_is_recognised_as_a_contraction():
 
 def test_tile_multiples_select_the_tensor_core_kernel():
     p = irgen.FULL["c4"]()
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta())
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"gemm_pair": False})
     rec = mod.kernels[0]
     assert rec["kind"] == "tcgen05_gemm" and rec["entry"] == "bmm_bf16"
     assert rec["params"] == ["A", "B", "C"] and rec["block"] == [192, 1, 1]
+    pair = compile_graph(Graph.from_dict(p.graph), p.meta()).kernels[0]
+    assert pair["kind"] == "tcgen05_gemm_pair" and pair["cluster"] == [2, 1, 1] and pair["grid"] == [148, 1, 1]
     for ins in ("tcgen05.mma.cta_group::1.kind::f16", "tcgen05.alloc", "tcgen05.dealloc",
                 "cp.async.bulk.tensor.3d", "tcgen05.ld.sync.aligned.32x32b.x32", "mbarrier.try_wait.parity"):
         assert ins in mod.ptx
     assert "multicast" not in mod.ptx
     small = irgen.SMALL["c4"]()          # N = 128, half of the 256-wide tile: one edge tile in N
-    assert compile_graph(Graph.from_dict(small.graph), small.meta()).kernels[0]["kind"] == "tcgen05_gemm"
+    assert compile_graph(Graph.from_dict(small.graph), small.meta()).kernels[0]["kind"] == "tcgen05_gemm_pair"
     odd_k = irgen.bmm_naive_ir(1, 64, 64, 36)     # K % 8 != 0: A's rows are no whole 16-byte TMA units
     assert compile_graph(Graph.from_dict(odd_k.graph), odd_k.meta()).kernels[0]["kind"] == "generic"
     odd_n = irgen.bmm_naive_ir(1, 64, 20, 64)     # N % 8 != 0: B's rows likewise
@@ -207,10 +209,10 @@ def test_unscheduled_matmul_reaches_the_tensor_cores():
     p = irgen.bmm_naive_ir(1, 128, 256, 64)
     g, k = _kernel(p)
     assert match_bmm(g, k) is not None
-    assert compile_graph(g, p.meta()).kernels[0]["kind"] == "tcgen05_gemm"
+    assert compile_graph(g, p.meta()).kernels[0]["kind"] == "tcgen05_gemm_pair"
     edge = irgen.bmm_naive_ir(1, 100, 256, 64)
     g1, _ = _kernel(edge)
-    assert compile_graph(g1, edge.meta()).kernels[0]["kind"] == "tcgen05_gemm"
+    assert compile_graph(g1, edge.meta()).kernels[0]["kind"] == "tcgen05_gemm_pair"
     odd = irgen.bmm_naive_ir(1, 100, 256, 60)
     g2, k2 = _kernel(odd)
     assert compile_graph(g2, odd.meta()).kernels[0]["kind"] == "generic"

@@ -73,7 +73,7 @@ def test_attention_long_delays():
 def test_gemm_pipeline_completes():
     p = irgen.SMALL["c4tc"]()
     for sms in (1, 3, 4):
-        mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": sms})
+        mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": sms, "gemm_pair": False})
         rec = mod.kernels[0]
         assert rec["kind"] == "tcgen05_gemm"
         _run_all(mod.ptx, rec, seeds=(0, 1))
@@ -83,7 +83,7 @@ def test_gemm_edge_tiles_pipeline_completes():
     # edge tiles in M, N and K: the same hand-overs as full tiles (the masking is in the stores only)
     p = irgen.bmm_naive_ir(1, 200, 264, 72)
     for sms in (1, 3):
-        mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": sms})
+        mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": sms, "gemm_pair": False})
         rec = mod.kernels[0]
         assert rec["kind"] == "tcgen05_gemm"
         _run_all(mod.ptx, rec, seeds=(0,))
@@ -113,7 +113,7 @@ def test_planted_wrong_arrival_count_deadlocks():
 
 def test_planted_missing_commit_deadlocks():
     p = irgen.SMALL["c4tc"]()
-    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": 2})
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {"sms": 2, "gemm_pair": False})
     lines = mod.ptx.splitlines()
     k = next(i for i, ln in enumerate(lines) if "tcgen05.commit" in ln)
     _expect_deadlock("\n".join(lines[:k] + lines[k + 1:]), mod.kernels[0])

@@ -17,6 +17,7 @@ from oracle.run import oracle_outputs
 from tests.checks import compare, rms_floor_for, rtol_for
 from tests.ptxemu import Memory
 from tests.tcemu import TcEmulator
+from tests.tcemu_pair import PairEmulator
 
 _BYTES = {"f16": 2, "bf16": 2, "f32": 4, "i32": 4}
 
@@ -38,7 +39,8 @@ def run_emulated(p, t, opts, defer=False, mod=None):
     err = mem.alloc(np.zeros(16, np.uint8))
     for rec in mod.kernels:
         tm = {f"p_{spec['name']}": (addr[spec["tensor"]], spec) for spec in rec.get("tmaps", [])}
-        emu = TcEmulator(mod.ptx, rec["entry"], tm, defer=defer)
+        cls = PairEmulator if list(rec.get("cluster", [1]))[0] == 2 else TcEmulator
+        emu = cls(mod.ptx, rec["entry"], tm, defer=defer)
         plain = [q for q in emu.params if not q.startswith("p_tm") and q not in ("p_err", "p_trace")]
         args = dict(zip(plain, [addr[n] for n in rec["params"]]))
         args.update(emu.tmap_args())
@@ -105,7 +107,7 @@ def test_attention_value_range_fallback_emulated(persistent):
 @pytest.mark.parametrize("sms", [1, 2, 3])
 def test_gemm_emulated_matches_oracle(sms):
     p = irgen.SMALL["c4tc"]()
-    _check(p, data.make_inputs(p), {"sms": sms}, "tcgen05_gemm")
+    _check(p, data.make_inputs(p), {"sms": sms, "gemm_pair": False}, "tcgen05_gemm")
 
 
 @pytest.mark.parametrize("key,opts", [
@@ -124,7 +126,7 @@ def test_attention_with_late_completions(key, opts):
 
 def test_gemm_with_late_completions():
     p = irgen.SMALL["c4tc"]()
-    _check(p, data.make_inputs(p), {"sms": 2}, "tcgen05_gemm", defer=True)
+    _check(p, data.make_inputs(p), {"sms": 2, "gemm_pair": False}, "tcgen05_gemm", defer=True)
 
 
 def test_late_completions_expose_a_planted_early_release():
@@ -161,13 +163,13 @@ def test_gemm_edge_tiles_emulated(shape):
     """Shapes that are not tile multiples: TMA zero-fills past M, N and K, the epilogue stores rows
     below M and 8-column groups below N (a store past the output would raise in the emulator)."""
     p = irgen.bmm_naive_ir(*shape)
-    _check(p, data.make_inputs(p), {}, "tcgen05_gemm")
+    _check(p, data.make_inputs(p), {"gemm_pair": False}, "tcgen05_gemm")
 
 
 def test_gemm_from_the_unscheduled_matmul_emulated():
     # the thread-per-element matmul nest lowered to the tcgen05 GEMM; the oracle interprets the nest
     p = irgen.bmm_naive_ir(1, 128, 256, 64)
-    _check(p, data.make_inputs(p), {"sms": 1}, "tcgen05_gemm")
+    _check(p, data.make_inputs(p), {"sms": 1, "gemm_pair": False}, "tcgen05_gemm")
 
 
 @pytest.mark.parametrize("shape,causal,opts", [
