@@ -20,14 +20,16 @@ structural and fails closed — anything not recognised exactly is left to the C
   and keys past S in the last 256-row query chunk are zero-filled, masked and not stored).
 
 Those checks find the operands, shapes and (for attention) the mask and scale.  The final gate is
-stricter: the kernel body must equal, up to the buffer names, the canonical CUDA-core nest for those
-parameters (:func:`.irgen.bmm_ir`, :func:`.irgen.attention_ir`).  A structural check alone let a
+stricter: the kernel body must equal the canonical CUDA-core nest for those parameters
+(:func:`.irgen.bmm_ir`, :func:`.irgen.bmm_naive_ir`, :func:`.irgen.attention_ir`), up to the buffer
+names, the names of local values and the operand order of commutative f32 operations.  A structural check alone let a
 store to C[b, j, i] or two swapped accumulators through; with the equality gate no variation of the
 nest can reach a tensor-core kernel that computes something else, and every other form runs, correctly,
 on the CUDA cores.
 """
 from __future__ import annotations
 
+import json
 import os
 
 from .ir import Graph, dt_name, walk
@@ -47,17 +49,61 @@ def _body_data(node, rename=None) -> list:
     return ren(data) if rename else data
 
 
+# Strings the IR gives meaning to (everything else a bare string holds is an SSA or buffer name):
+# class names, types, operator spellings, and the names of elementwise / reduction / builtin /
+# called functions.
+_SEMANTIC_KEYS = frozenset({"kind", "dtype", "value_dtype", "swizzle", "op"})
+_SEMANTIC_NAME = frozenset({"ElementwiseImpl", "ReduceOp", "Builtin", "FuncCallExpr"})
+_COMMUTATIVE = frozenset({"add", "multiply", "maximum", "minimum"})
+
+
+def _alpha(data, fixed: frozenset):
+    """``data`` with every SSA name replaced by its rank of first appearance, buffer names in
+    ``fixed`` kept, and the two arguments of a commutative Assign in a canonical order.  Two bodies
+    equal after this differ only in what they call their local values (and the operand order of
+    f32 add / multiply / max / min, which IEEE arithmetic does not depend on), so they compute the
+    same thing."""
+    names: dict[str, str] = {}
+
+    def canon(v: str) -> str:
+        if v in fixed:
+            return v
+        if v not in names:
+            names[v] = f"%{len(names)}"
+        return names[v]
+
+    def go(v, key=None, kind=None):
+        if isinstance(v, str):
+            if key in _SEMANTIC_KEYS or (key == "name" and kind in _SEMANTIC_NAME) or (
+                    key == "value" and kind in ("Literal", "Dim")):
+                return v
+            return canon(v)
+        if isinstance(v, list):
+            return [go(x, key, kind) for x in v]
+        if isinstance(v, dict):
+            k2 = v.get("kind")
+            out = {k: go(x, k, k2) for k, x in v.items()}
+            if (k2 == "Assign" and isinstance(v.get("op"), dict) and v["op"].get("name") in _COMMUTATIVE
+                    and len(out.get("args") or []) == 2):
+                out["args"] = sorted(out["args"], key=lambda a: json.dumps(a, sort_keys=True))
+            return out
+        return v
+    return go(data)
+
+
 def is_canonical(node, template, rename: dict) -> bool:
     """True when ``node``'s body, its buffers renamed by ``rename``, equals the body of the single
     kernel of ``template`` (a problem from :mod:`.irgen`, or a callable making one: a generator that
-    has no form for these parameters raises ValueError, and then nothing matches)."""
+    has no form for these parameters raises ValueError, and then nothing matches), up to the names
+    of local values and the operand order of commutative f32 operations."""
     if callable(template):
         try:
             template = template()
         except ValueError:
             return False
     tnode = Graph.from_dict(template.graph).kernels()[0]
-    return _body_data(node, rename) == _body_data(tnode)
+    fixed = frozenset(rename.values()) | frozenset(tnode.inputs) | frozenset(v.name for v in tnode.outputs)
+    return _alpha(_body_data(node, rename), fixed) == _alpha(_body_data(tnode), fixed)
 
 
 def _names_in(e, out: set) -> set:

@@ -222,3 +222,56 @@ def test_unscheduled_matmul_reaches_the_tensor_cores():
             st["index"][1], st["index"][2] = st["index"][2], st["index"][1]
     g3, k3 = _mutated(p, "bmm_naive", transpose_store)
     assert match_bmm(g3, k3) is None
+
+
+def _rename_locals(p, entry, keep):
+    """Every SSA name of the kernel (not the buffers in ``keep``, not an operator or type) prefixed
+    with ``t_``: the same program under other local names."""
+    d = copy.deepcopy(p.graph)
+    semantic = {"kind", "dtype", "value_dtype", "swizzle", "op"}
+
+    def go(v, key=None, kind=None):
+        if isinstance(v, str):
+            if key in semantic or (key == "name" and kind in ("ElementwiseImpl", "ReduceOp", "Builtin")) or v in keep:
+                return v
+            return "t_" + v
+        if isinstance(v, list):
+            return [go(x, key, kind) for x in v]
+        if isinstance(v, dict):
+            return {k: go(x, k, v.get("kind")) for k, x in v.items()}
+        return v
+    body = d["nodes"][entry]["op_fields"]["body"]
+    d["nodes"][entry]["op_fields"]["body"] = go(body)
+    g = Graph.from_dict(d)
+    return g, g.kernels()[0]
+
+
+def test_renamed_locals_and_commuted_products_still_match():
+    # the gate compares bodies up to local value names and the operand order of commutative f32
+    # operations: an Emmy lowering that names its values differently still reaches the tensor cores
+    p = irgen.SMALL["c4tc"]()
+    g, k = _rename_locals(p, "bmm_bf16", {"A", "B", "C"})
+    assert match_bmm(g, k) is not None
+    assert compile_graph(g, p.meta()).kernels[0]["kind"] == "tcgen05_gemm_pair"
+
+    def commute(st):
+        if st.get("kind") == "Assign" and st["op"]["name"] == "multiply":
+            st["args"].reverse()
+    g, k = _mutated(p, "bmm_bf16", commute)
+    assert match_bmm(g, k) is not None
+    q = irgen.SMALL["c5tc"]()
+    g, k = _rename_locals(q, "attention_causal", {"Q", "K", "V", "O"})
+    assert match_attention(g, k) is not None
+    assert compile_graph(g, q.meta()).kernels[-1]["kind"] == "tcgen05_attention"
+
+
+def test_commuting_a_subtraction_is_refused():
+    # operand order matters for subtract: exp(m - s) is not exp(s - m)
+    p = irgen.SMALL["c5tc"]()
+
+    def flip(st):
+        if st.get("kind") == "Assign" and st["op"]["name"] == "subtract":
+            st["args"].reverse()
+    g, k = _mutated(p, "attention_causal", flip)
+    assert match_attention(g, k) is None
+    assert [r["kind"] for r in compile_graph(g, p.meta()).kernels] == ["generic"]
