@@ -46,11 +46,11 @@ THREADS = 192
 TMEM_COLS = 512
 EPI_ARRIVALS = 8                   # tmem_empty: the 4 epilogue warps of each CTA
 
-ERR_PRODUCER = 21
-ERR_MMA_FULL = 22
-ERR_MMA_TMEM = 23
-ERR_EPILOGUE = 24
-ERR_DRAIN = 25
+ERR_PRODUCER = 61
+ERR_MMA_FULL = 62
+ERR_MMA_TMEM = 63
+ERR_EPILOGUE = 64
+ERR_DRAIN = 65
 
 # barrier offsets from the barrier area
 FULL = 0
