@@ -48,6 +48,7 @@ def _run(p, mod, defer=False):
     ((3, 130, 520, 200), False),
     ((2, 256, 512, 512), True),        # completions deferred until no thread can run
     ((1, 200, 264, 136), True),
+    ((1, 1, 8, 8), False),             # one row, one 8-column group, one K step of 8
 ])
 def test_pair_gemm_emulated_matches_oracle(shape, defer):
     p = irgen.bmm_naive_ir(*shape)
@@ -90,7 +91,8 @@ def test_pair_kernel_uses_no_multicast_and_assembles():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape", [(1, 256, 256, 128), (2, 512, 512, 256), (1, 300, 264, 72), (3, 1000, 1000, 1000)])
+@pytest.mark.parametrize("shape", [(1, 256, 256, 128), (2, 512, 512, 256), (1, 300, 264, 72), (3, 1000, 1000, 1000),
+                                   (1, 1, 8, 8), (5, 257, 264, 520), (1, 4096, 8, 4096), (2, 130, 4096, 64)])
 def test_pair_gemm_on_the_gpu(shape):
     from emmy_ptx_b200.runtime import Executable
     p = irgen.bmm_naive_ir(*shape)
