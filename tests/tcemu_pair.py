@@ -22,6 +22,8 @@ the single-CTA emulator.  Test infrastructure only.
 """
 from __future__ import annotations
 
+import random
+
 import numpy as np
 
 from tests.ptxemu import _M32, _Thread
@@ -44,6 +46,14 @@ class _Cta:
 
 
 class PairEmulator(TcEmulator):
+    def __init__(self, ptx: str, entry: str, tmaps: dict | None = None, defer: bool = False, seed=None):
+        # seed: completions in random order and amounts (half the TMA loads land at issue, so a
+        # partner's bytes can reach a barrier before its owner's expect_tx; of the rest any subset lands
+        # at a time; the tensor core runs a random number of its queued MMAs and commits, in issue
+        # order), and the threads stepped in a random order each round
+        super().__init__(ptx, entry, tmaps, defer=defer or seed is not None)
+        self.rng = random.Random(seed) if seed is not None else None
+
     def run(self, grid: int, block: int, args: dict, mem, dyn_smem: int = 0, max_steps: int = 400_000_000):
         if grid % 2:
             raise ValueError("clusters of two CTAs need an even grid")
@@ -83,7 +93,10 @@ class PairEmulator(TcEmulator):
             warps.setdefault((th.rank, th.warp), []).append(th)
         while True:
             progressed = False
-            for th in threads:
+            order = list(threads)
+            if self.rng is not None:
+                self.rng.shuffle(order)
+            for th in order:
                 if th.state != "run":
                     continue
                 self._use(th.rank)
@@ -197,7 +210,7 @@ class PairEmulator(TcEmulator):
                     raise NotImplementedError("a TMA load into the partner's shared memory")
                 dst &= 0xFFFFFF
             mbt = self._abs(mb)
-            if self.defer:
+            if self.defer and not (self.rng is not None and self.rng.random() < 0.5):
                 self.queue_tma.append((self.rank, dst, tm, cs, mbt, mem))
             else:
                 self._tma_write(dst, tm, cs, mbt, smem, mem)
@@ -221,12 +234,22 @@ class PairEmulator(TcEmulator):
     def _drain_async(self) -> bool:
         if not (self.queue_tma or self.queue_mma):
             return False
-        tmas, self.queue_tma = self.queue_tma, []
+        if self.rng is not None and self.queue_tma:
+            # any subset of the loads in flight lands now (at least one), the rest later
+            k = self.rng.randint(1, len(self.queue_tma))
+            pick = set(self.rng.sample(range(len(self.queue_tma)), k))
+            tmas = [x for i, x in enumerate(self.queue_tma) if i in pick]
+            self.queue_tma = [x for i, x in enumerate(self.queue_tma) if i not in pick]
+        else:
+            tmas, self.queue_tma = self.queue_tma, []
         for rank, dst, tm, cs, mb, mem in tmas:
             self._use(rank)
             self._tma_write(dst, tm, cs, mb, self.ctas[rank].smem, mem)
+        budget = self.rng.randint(1, 8) if self.rng is not None and tmas == [] else None
         woke = False
-        while self.queue_mma and not woke:
+        while self.queue_mma and not woke and (budget is None or budget > 0):
+            if budget is not None:
+                budget -= 1
             item = self.queue_mma.pop(0)
             if item[0] == "rank":
                 self._use(item[1])

@@ -27,14 +27,14 @@ from tests.test_tc_emulated import _np
 OPTS = {"gemm_pair": True, "sms": 4}
 
 
-def _run(p, mod, defer=False):
+def _run(p, mod, defer=False, seed=None):
     rec = mod.kernels[0]
     t = data.make_inputs(p)
     mem = Memory()
     addr = {n: mem.alloc(_np(x).copy()) for n, x in t.items()}
     err = mem.alloc(np.zeros(16, np.uint8))
     tm = {f"p_{s['name']}": (addr[s["tensor"]], s) for s in rec["tmaps"]}
-    emu = PairEmulator(mod.ptx, rec["entry"], tm, defer=defer)
+    emu = PairEmulator(mod.ptx, rec["entry"], tm, defer=defer, seed=seed)
     args = {"p_A": addr["A"], "p_B": addr["B"], "p_C": addr["C"], **emu.tmap_args(), "p_err": err}
     emu.run(rec["grid"][0], rec["block"][0], args, mem, rec["dyn_smem"])
     got = torch.from_numpy(mem.array(addr["C"], np.float32, tuple(t["C"].shape)).copy())
@@ -60,6 +60,17 @@ def test_pair_gemm_emulated_matches_oracle(shape, defer):
     compare(got, oracle_outputs(p, t)["C"], "f32", 1e-4, f"pair {shape}")
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_pair_gemm_random_orders(seed):
+    # threads stepped in a random order, loads landing in random subsets, the tensor core running a
+    # random number of its queued MMAs and commits at a time: the same result every time
+    p = irgen.bmm_naive_ir(2, 256, 512, 512) if seed % 2 == 0 else irgen.bmm_naive_ir(1, 300, 264, 200)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), OPTS)
+    t, got, code = _run(p, mod, seed=seed)
+    assert code == 0
+    compare(got, oracle_outputs(p, t)["C"], "f32", 1e-4, f"pair seed {seed}")
+
+
 def test_planted_missing_commit_to_the_partner_deadlocks():
     p = irgen.bmm_naive_ir(2, 256, 512, 512)
     mod = compile_graph(Graph.from_dict(p.graph), p.meta(), OPTS)
@@ -69,6 +80,22 @@ def test_planted_missing_commit_to_the_partner_deadlocks():
     bad = "\n".join(lines[:commits[1]] + lines[commits[1] + 1:])   # CTA 1's empty barrier never arrives
     with pytest.raises(RuntimeError, match="deadlock"):
         _run(p, CompiledModule(bad, mod.kernels))
+
+
+def test_planted_full_barrier_expecting_one_half_fails():
+    # CTA 0's full barrier armed for its own half only: in random orders the accounting breaks
+    # (the stage completes before the partner's bytes, or a later phase never completes)
+    p = irgen.bmm_naive_ir(2, 256, 512, 512)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), OPTS)
+    bad = mod.ptx.replace(f", {gp.TX_PAIR};", f", {gp.TX_PAIR // 2};")
+    assert bad != mod.ptx
+    for seed in range(3):
+        try:
+            t, got, code = _run(p, CompiledModule(bad, mod.kernels), seed=seed)
+        except RuntimeError:
+            continue
+        want = oracle_outputs(p, t)["C"]
+        assert code != 0 or (got.double() - want.double()).abs().max().item() > 1e-2
 
 
 def test_pair_kernel_uses_no_multicast_and_assembles():
