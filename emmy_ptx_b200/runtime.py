@@ -128,6 +128,10 @@ class Executable:
             tensors = {**self.scratch, **tensors}
         rec = self.records[i]
         fn = self.funcs[i]
+        if grid is not None and (rec.get("self_zeroing") or rec.get("exchange")) and list(grid) != list(rec["grid"]):
+            # the last block is the one whose ticket is grid - 1 of the compiled grid
+            raise ValueError(f"kernel {rec['entry']!r} counts its blocks: launch it with its compiled grid "
+                             f"{rec['grid']}, not {list(grid)}")
         if zero:
             self.zero_outputs(i, tensors, stream)
         g = grid or rec["grid"]

@@ -84,3 +84,17 @@ def test_sum_without_zeroing_on_the_gpu(dtype):
         acc = next(iter(ex.scratch.values()))
         assert not acc.any().item()
     ex.close()
+
+
+def test_runtime_refuses_another_grid_for_a_ticket_kernel():
+    # the last block is found by counting to the compiled grid: another launch grid would leave the
+    # accumulators unread and unzeroed, so the runtime refuses it before touching the device
+    from emmy_ptx_b200.runtime import Executable
+    p = irgen.sum_ir(1 << 12, "f32", blocks=5, threads=128)
+    rec = _compile(p, {"self_zeroing": True}).kernels[0]
+    fake = Executable.__new__(Executable)
+    fake.compiled = type("M", (), {"kernels": [rec]})()
+    fake.scratch = {}
+    fake.funcs = [None]
+    with pytest.raises(ValueError, match="compiled grid"):
+        fake.launch(0, {}, 0, grid=[4, 1, 1], zero=False)
