@@ -13,7 +13,7 @@ single-CTA kernel's 128 x 256 tile for the same arithmetic (8 KiB instead of 12 
 * 192 threads per CTA: warp 0 issues TMA loads (both CTAs, each its own halves), warp 1 allocates
   tensor memory (both CTAs, ``tcgen05.alloc.cta_group::2``) and, in CTA 0 only, issues the MMAs
   from one thread; warps 2-5 of each CTA drain that CTA's 128 accumulator rows;
-* a 6-stage ring of 32 KiB stages per CTA (A 128 x 64 K-major, B 64 x 128 MN-major, 128-byte
+* a 7-stage ring of 32 KiB stages per CTA (A 128 x 64 K-major, B 64 x 128 MN-major, 128-byte
   swizzle).  Both CTAs' loads of a stage complete the transaction bytes of CTA 0's ``full`` barrier
   (``cp.async.bulk.tensor ... .cta_group::2`` with CTA 0's barrier address); CTA 0's producer
   expects both halves.  The MMA issuer's ``tcgen05.commit.cta_group::2`` arrives on the ``empty``
@@ -37,7 +37,7 @@ from .ptxasm import Asm, idesc_f16, smem_desc_hi, wait_bar as _wait, wait_bar_wa
 
 BM, BN, BK = 256, 256, 64          # the pair's output tile and K block
 HM, HN = BM // 2, BN // 2          # one CTA's rows of A and columns of B
-STAGES = 6
+STAGES = 7                         # 7 x 32 KiB + barriers fill the 227 KiB (measured 2-7 % over 6)
 A_STAGE = HM * BK * 2              # 16 KiB
 B_STAGE = BK * HN * 2              # 16 KiB
 B_BOX = BK * 64 * 2                # one 64-column TMA box of B: 8 KiB
@@ -67,13 +67,20 @@ def supported(m: int, n: int, k: int) -> bool:
 
 
 def gemm_pair_entry(name: str, batch: int, m: int, n: int, k: int, pairs: int = 74,
-                    names=("A", "B", "C"), prefix: str = "") -> dict:
+                    names=("A", "B", "C"), prefix: str = "", stages: int = STAGES) -> dict:
     """The build record of the CTA-pair GEMM (``pairs`` clusters of two CTAs at most; the runtime
     may launch fewer, the tile loop strides by the launched cluster count).  Shapes that are not
     tile multiples run as edge tiles, as in the single-CTA kernel: TMA zero-fills past the tensor,
     the epilogue stores rows below M and 8-column groups below N."""
     if not supported(m, n, k):
         raise ValueError("tcgen05 GEMM needs N % 8 == 0 and K % 8 == 0")
+    if not 2 <= stages <= 7:
+        raise ValueError("the pair GEMM's ring holds 2-7 stages of 32 KiB (227 KiB of shared memory)")
+    STAGES = stages
+    EMPTY = 8 * STAGES
+    TFULL = 16 * STAGES
+    TEMPTY = TFULL + 16
+    SLOT = TEMPTY + 16
     mt, nt, nk = -(-m // BM), -(-n // BN), -(-k // BK)
     edge_m, edge_n = m % BM != 0, n % BN != 0
     tiles = batch * mt * nt

@@ -420,7 +420,8 @@ def try_lower(graph, node, kmeta, prefix, options):
             # tcgen05.mma.cta_group::2 (kernels/tc_gemm_pair.py); gemm_pair=False keeps one CTA per tile
             from .kernels import tc_gemm_pair
             return tc_gemm_pair.gemm_pair_entry(node.op.name, bt, m, n, k, pairs=int(options.get("sms", 148)) // 2,
-                                                names=(X.name, Y.name, C.name), prefix=prefix)
+                                                names=(X.name, Y.name, C.name), prefix=prefix,
+                                                stages=int(options.get("gemm_stages", tc_gemm_pair.STAGES)))
         b = tc_gemm.gemm_entry(node.op.name, bt, m, n, k, sms=int(options.get("sms", 148)),
                                names=(X.name, Y.name, C.name), prefix=prefix)
         return b

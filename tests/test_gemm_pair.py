@@ -43,7 +43,7 @@ def _run(p, mod, defer=False, seed=None):
 
 @pytest.mark.parametrize("shape,defer", [
     ((1, 256, 256, 128), False),
-    ((2, 512, 512, 256), False),       # 8 tiles over 2 clusters, the 6-stage ring wraps
+    ((2, 512, 512, 256), False),       # 8 tiles over 2 clusters, the 7-stage ring wraps
     ((1, 300, 264, 72), False),        # edge tiles in M, N and K
     ((3, 130, 520, 200), False),
     ((2, 256, 512, 512), True),        # completions deferred until no thread can run
@@ -58,6 +58,15 @@ def test_pair_gemm_emulated_matches_oracle(shape, defer):
     t, got, code = _run(p, mod, defer)
     assert code == 0
     compare(got, oracle_outputs(p, t)["C"], "f32", 1e-4, f"pair {shape}")
+
+
+@pytest.mark.parametrize("stages", [2, 7])
+def test_pair_gemm_ring_depths(stages):
+    p = irgen.bmm_naive_ir(2, 256, 512, 512)
+    mod = compile_graph(Graph.from_dict(p.graph), p.meta(), {**OPTS, "gemm_stages": stages})
+    t, got, code = _run(p, mod, seed=stages)
+    assert code == 0
+    compare(got, oracle_outputs(p, t)["C"], "f32", 1e-4, f"pair stages {stages}")
 
 
 @pytest.mark.parametrize("seed", range(6))
