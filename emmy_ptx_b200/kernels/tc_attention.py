@@ -91,7 +91,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
                     pingpong: bool = True, f16_int: int = 0, pack_after_turn: bool = False,
                     defer_sum: bool = False, bh_range: tuple[int, int] | None = None,
                     scratch_names: tuple[str, str] | None = None, prefetch_next: int = 0,
-                    pack_in_turn: bool = False, pair_poly: int = 0, dim: int = 128) -> dict:
+                    pack_in_turn: bool = False, pair_poly: int = 0, dim: int = 128,
+                    mask_name: str | None = None) -> dict:
     """The kernel's launch record and PTX.  ``trace`` adds a ``__trace`` buffer parameter of
     grid x 66 x 24 u64 clock64 stamps (a pipeline timeline probe, see :func:`trace_events`).
     ``pingpong`` makes the two tiles' softmax warpgroups take turns on the MUFU exps.
@@ -101,7 +102,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     keeps all of a block's f16 packing inside its MUFU turn.  ``pair_poly`` = n (0-4) takes n of every
     4 score pairs of the f16 path off the MUFU: a cubic exp2 on the FMA pipe, two scores per f32x2
     instruction (the MUFU ``ex2`` and the f16 ``cvt`` packing share the XU pipe, which bounds the exp
-    phase)."""
+    phase).  ``mask_name`` adds an explicit boolean mask M [S, S] (u8, nonzero = the key takes part, as
+    torch's ``attn_mask``): each softmax thread reads its row's 64 bytes per key block and sets the
+    masked scores to -inf; a row whose keys so far are all masked keeps a running max of -inf and
+    exponentiates against 0, and a row with every key masked ends as 0 / 0 = NaN, as in torch."""
     if dim not in (64, 128):
         raise ValueError("tcgen05 attention takes head dim 64 or 128")
     # the head dim sets the tile sizes: a Q tile or K/V block is dim / 64 TMA boxes of 64 columns
@@ -129,6 +133,9 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     if trace and spad // BKV + 1 >= TRACE_SLOTS:
         raise ValueError("trace supports at most 64 key/value blocks")
     half = half and precise
+    mask = mask_name is not None
+    if mask and seq % BKV:
+        raise ValueError("the masked attention reads 64-byte mask rows: S % 64 == 0")
     if pack_in_turn and (pack_after_turn or not pingpong):
         raise ValueError("pack_in_turn applies to the default split packing with turns")
     if defer_sum and (poly_every or not pack_after_turn):
@@ -629,6 +636,20 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     else:
         a(f"sub.u32 {last}, {nb}, 1;")
     a(f"mad.lo.u32 {grow0}, {ti}, {BQ}, {row0};")
+    mrow = prow_m = None
+    if mask:
+        # M + q * S for this thread's query row q (its 64 bytes of block jj start 64 * jj further on)
+        mrow, mq = a.r("rd"), a.r("rd")
+        a(f"ld.param.u64 {mrow}, [p_M];")
+        a(f"cvta.to.global.u64 {mrow}, {mrow};")
+        growm = a.r()
+        a(f"mad.lo.u32 {growm}, {ti}, {BQ}, {row0};")
+        a(f"add.u32 {growm}, {growm}, {rowl};")
+        a(f"mul.wide.u32 {mq}, {growm}, {seq};")
+        a(f"add.s64 {mrow}, {mrow}, {mq};")
+        if ragged:
+            prow_m = a.r("p")
+            a(f"setp.lt.u32 {prow_m}, {growm}, {seq};")   # rows past S have no mask row
     a(f"add.u32 {grow0}, {grow0}, {rowl};")                # this thread's query row
     sfb0, pfb0, pfr0 = a.r(), a.r(), a.r()
     a(f"mad.lo.u32 {sfb0}, {ti}, 16, {bars};")
@@ -735,6 +756,21 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     a(f"shr.u32 {par_s}, {jj}, 1;")
     a(f"and.b32 {par_s}, {par_s}, 1;")
     a(f"mad.lo.u32 {scol}, {bsel}, {BKV}, {scol0};")
+    mw = None
+    if mask:
+        # this row's mask bytes for block jj, loaded before the wait for the scores so the load's
+        # latency overlaps it (rows past S: every key kept)
+        mw = [a.r() for _ in range(BKV // 4)]
+        ma, mo = a.r("rd"), a.r("rd")
+        a(f"mul.wide.u32 {mo}, {jj}, {BKV};")
+        a(f"add.s64 {ma}, {mrow}, {mo};")
+        g_ = ""
+        if prow_m is not None:
+            for w_ in mw:
+                a(f"mov.u32 {w_}, 0x01010101;")
+            g_ = f"@{prow_m} "
+        for i_ in range(BKV // 16):
+            a(f"{g_}ld.global.nc.v4.u32 {{{', '.join(mw[4 * i_:4 * i_ + 4])}}}, [{ma}+{16 * i_}];")
     wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_drain)
     p16 = None
     if half:
@@ -781,6 +817,13 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         for c in range(seq % BKV, BKV):
             a(f"mov.b32 {s_[c]}, 0fFF800000;")
         a.label(l_nokey)
+    if mask:
+        # the explicit mask: a zero byte removes its key
+        for c in range(BKV):
+            t_, pz = a.r(), a.r("p")
+            a(f"and.b32 {t_}, {mw[c // 4]}, {0xFF << (8 * (c % 4))};")
+            a(f"setp.eq.u32 {pz}, {t_}, 0;")
+            a(f"@{pz} mov.b32 {s_[c]}, 0fFF800000;")
     # row max in the scaled log2 domain: 8 independent chains of three-input maxima (columns k,
     # k+8, ...), then 8 -> 3 -> 1
     lvl = [a.r("f") for _ in range(8)]
@@ -819,6 +862,12 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     dm = a.r("f")
     a(f"sub.f32 {dm}, {mref}, {mnew};")
     a(f"ex2.approx.ftz.f32 {alpha}, {dm};")
+    if mask:
+        # a row whose keys are all masked so far (max still -inf) while another row of the warp
+        # rescales: nothing to rescale (its O and sum are 0), and -inf - -inf must not make a NaN
+        pm_inf = a.r("p")
+        a(f"setp.eq.f32 {pm_inf}, {mnew}, 0fFF800000;")
+        a(f"@{pm_inf} mov.b32 {alpha}, 0f3F800000;")
     a(f"mov.b32 {mref}, {mnew};")
     a(f"mul.f32 {lsum}, {lsum}, {alpha};")
     a.label(l_norescale)
@@ -830,6 +879,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     # p = 2^(s*c - m), row sum, and P back over S's TMEM columns as bf16 pairs (hi, then lo)
     negm = a.r("f")
     a(f"neg.f32 {negm}, {mref};")
+    if mask:
+        # every key so far masked: the running max is -inf; exponentiate against 0 (p = 0) instead
+        pninf = a.r("p")
+        a(f"setp.eq.f32 {pninf}, {mref}, 0fFF800000;")
+        a(f"@{pninf} mov.b32 {negm}, 0f00000000;")
     parts = [a.r("f") for _ in range(4)]
     for pp in parts:
         a(f"mov.b32 {pp}, 0f00000000;")
@@ -1132,6 +1186,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
 
     dyn = TILES * Q_BYTES + STAGES * KV_BYTES + BAR_BYTES + 1024
     params = ["\t.param .u64 p_Q,", "\t.param .u64 p_K,", "\t.param .u64 p_V,", "\t.param .u64 p_O,"]
+    if mask:
+        params.append("\t.param .u64 p_M,")
     if half:
         params += ["\t.param .u64 p_V16,", "\t.param .u64 p_vflag,"]
     params += ["\t.param .align 64 .b8 p_tmQ[128],", "\t.param .align 64 .b8 p_tmK[128],",
@@ -1151,7 +1207,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
               "box": [64, BQ, 1, 1], "swizzle": "128B"}]
     tmaps += [{"name": f"tm{x}", "tensor": nm, "dtype": "bf16", "dims": dims, "strides": strides,
                "box": [64, BKV, 1, 1], "swizzle": "128B"} for x, nm in (("K", kn), ("V", vn))]
-    uparams = [qn, kn, vn, on]
+    uparams = [qn, kn, vn, on] + ([mask_name] if mask else [])
     if half:
         v16n, vfn = scratch_names or (f"{prefix}{name}__v16", f"{prefix}{name}__vflag")
         uparams += [v16n, vfn]
@@ -1164,7 +1220,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         "name": name, "kind": "tcgen05_attention", "params": uparams,
         "raw_entry": entry, "raw_decls": [f".extern .shared .align 1024 .b8 {smem_sym}[];"],
         "grid": [grid, 1, 1], "block": [threads, 1, 1], "dyn_smem": dyn,
-        "align": {qn: 16, kn: 16, vn: 16, on: 32, **({uparams[4]: 16, uparams[5]: 4} if half else {})},
+        "align": {qn: 16, kn: 16, vn: 16, on: 32, **({mask_name: 16} if mask else {}),
+                  **({uparams[-2]: 16, uparams[-1]: 4} if half else {})},
         "zero_outputs": [], "tmaps": tmaps,
         "extra": extra,
     }

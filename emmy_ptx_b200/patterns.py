@@ -266,26 +266,36 @@ def _index_vars(index) -> list:
 
 
 def match_attention(graph, node):
-    """(Q, K, V, O, batch, heads, seq, dim, causal, scale) when the kernel is the online-softmax
-    attention nest, else None.
+    """(Q, K, V, O, batch, heads, seq, dim, causal, scale, M) when the kernel is the online-softmax
+    attention nest, else None; M is the explicit u8 mask [S, S] or None.
 
     Recognised form (the attention IR): a Tile over (b, h, q, lane); Q loaded at [b, h, q, d0]; one
     kv loop from 0 to S with step 1 whose body loads K and V at [b, h, kv, d0], reduces the lane
     products of Q and K with an ``add`` WarpShuffle, multiplies by a float literal (the scale), masks
     with a Select whose first branch is ``kv > q -> -inf`` (causal) or has no mask, keeps the running
     max as ``Accum(maximum)`` and the row sum / output as ``Accum(add, base=...)``; after the loop
-    every written value is ``divide(o, l)`` to O at [b, h, q, d0]."""
+    every written value is ``divide(o, l)`` to O at [b, h, q, d0].  With an explicit mask the kv
+    loop also loads M at [q, kv] and masks a zero byte to -inf."""
     op = node.op
     vals = graph.values()
-    if len(node.outputs) != 1 or len(node.inputs) != 3:
+    if len(node.outputs) != 1 or len(node.inputs) not in (3, 4):
         return None
     O = node.outputs[0]
-    ins = [vals.get(n) for n in node.inputs]
-    if any(v is None or dt_name(v.dtype) != "bf16" or tuple(v.shape) != tuple(O.shape) for v in ins):
-        return None
     if dt_name(O.dtype) != "bf16" or len(O.shape) != 4:
         return None
     bt, hd, seq, dim = O.shape
+    ins = [vals.get(n) for n in node.inputs]
+    if any(v is None for v in ins):
+        return None
+    M = None
+    if len(ins) == 4:
+        masks = [v for v in ins if dt_name(v.dtype) == "u8" and tuple(v.shape) == (seq, seq)]
+        if len(masks) != 1:
+            return None
+        M = masks[0]
+        ins = [v for v in ins if v is not M]
+    if any(dt_name(v.dtype) != "bf16" or tuple(v.shape) != tuple(O.shape) for v in ins):
+        return None
     tiles = [st for st in op.body if type(st).__name__ == "Tile"]
     if len(tiles) != 1 or len(tiles[0].axes) != 4:
         return None
@@ -306,6 +316,10 @@ def match_attention(graph, node):
     inner = []
     walk(lp.body, inner.append)
     loads_in = {st.input: st for st in inner if type(st).__name__ == "Load"}
+    if M is not None:
+        if M.name not in loads_in:
+            return None
+        loads_in.pop(M.name)             # its form ([q, kv], a zero byte -> -inf) is the canonical check's
     loads_out = [st for st in stmts if type(st).__name__ == "Load" and st not in inner]
     if len(loads_in) != 2 or len(loads_out) != 1:
         return None
@@ -364,21 +378,16 @@ def match_attention(graph, node):
         return None
     sels = [st for st in inner if type(st).__name__ == "Select"]
     causal = False
-    if len(sels) > 1:
+    if len(sels) > (2 if M is not None else 1):
         return None
-    if sels and len(sels[0].branches) == 1:
-        sels = []                        # only the catch-all branch: no mask
-    if sels:
-        if len(sels[0].branches) != 2:
-            return None
-        br = sels[0].branches[0]
+    for sel in sels:
+        br = sel.branches[0]
         c = br.select
         v = br.value
-        if not (type(c).__name__ == "BinaryExpr" and c.op == ">" and _is_var(c.left, kv) and _is_var(c.right, ax[2])):
-            return None
-        if not (type(v).__name__ == "Literal" and float(v.value) == float("-inf")):
-            return None
-        causal = True
+        if (type(c).__name__ == "BinaryExpr" and c.op == ">" and _is_var(c.left, kv) and _is_var(c.right, ax[2])
+                and type(v).__name__ == "Literal" and float(v.value) == float("-inf")):
+            causal = True                # the first branch masks kv > q: causal (the canonical check
+            #                              below confirms every branch)
     accs = [st for st in inner if type(st).__name__ == "Accum"]
     ops = sorted((getattr(a.op, "name", None) or str(a.op)) for a in accs)
     if ops.count("maximum") != 1 or ops.count("add") != 1 + dim // 32:
@@ -393,10 +402,11 @@ def match_attention(graph, node):
     K = vals[kname]
     V = vals[vname]
     from .irgen import attention_ir
-    if not is_canonical(node, lambda: attention_ir(bt, hd, seq, dim, causal, scale=scale),
-                        {Q.name: "Q", K.name: "K", V.name: "V", O.name: "O"}):
+    rename = {Q.name: "Q", K.name: "K", V.name: "V", O.name: "O", **({M.name: "M"} if M is not None else {})}
+    if not is_canonical(node, lambda: attention_ir(bt, hd, seq, dim, causal, scale=scale, mask=M is not None),
+                        rename):
         return None
-    return Q, K, V, O, bt, hd, seq, dim, causal, scale
+    return Q, K, V, O, bt, hd, seq, dim, causal, scale, M
 
 
 def _flat(body):
@@ -427,15 +437,21 @@ def try_lower(graph, node, kmeta, prefix, options):
         return b
     hit = match_attention(graph, node)
     if hit is not None:
-        Q, K, V, O, bt, hd, seq, dim, causal, scale = hit
+        Q, K, V, O, bt, hd, seq, dim, causal, scale, M = hit
         from .kernels import tc_attention
         if dim not in (64, 128) or seq < tc_attention.BQ:
             return None
-        if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES):
-            # head dim 64, or S no multiple of 256: the default schedule only (the other forms are
-            # built for head dim 128 and whole 256-row query chunks)
+        if M is not None and seq % tc_attention.BKV:
+            return None                  # the mask is read in 64-byte rows per key block
+        if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES) or M is not None:
+            # head dim 64, S no multiple of 256, or an explicit mask: the default schedule only (the
+            # other forms are built for head dim 128, whole 256-row query chunks and no mask)
             options = {k: v for k, v in options.items()
                        if k not in ("attn_persistent", "attn_kv128", "attn_overlap")}
+        if M is not None:
+            # the cubic exp2 variants clamp at 2^-120 instead of reaching 0, so a fully masked row
+            # would sum to a tiny positive number instead of 0 (and end as 0, not NaN): MUFU only
+            options = {k: v for k, v in options.items() if k not in ("attn_poly", "attn_pair_poly")}
         precise = bool(options.get("attn_precise", True))
         half = bool(options.get("attn_half", True)) and precise
         name = node.op.name
@@ -448,7 +464,8 @@ def try_lower(graph, node, kmeta, prefix, options):
                   defer_sum=bool(options.get("attn_defer_sum", False)),
                   prefetch_next=int(options.get("attn_prefetch_next", 0)),
                   pack_in_turn=bool(options.get("attn_pack_in_turn", False)),
-                  pair_poly=int(options.get("attn_pair_poly", 0)), dim=dim)
+                  pair_poly=int(options.get("attn_pair_poly", 0)), dim=dim,
+                  mask_name=M.name if M is not None else None)
         if options.get("attn_kv128", False):
             # 128-row key/value blocks: QK^T bound by the tensor core instead of shared memory
             from .kernels import tc_attention_kv128 as t128, vconv

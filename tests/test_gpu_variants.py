@@ -184,3 +184,33 @@ def test_attention_ragged_sequence(shape, causal):
         if causal:
             s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
         compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"S=1000 head {h}", rms_floor=True)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_explicit_mask(causal):
+    """An explicit boolean mask on the tensor cores: the small case against the oracle (with rows whose
+    first key blocks are all masked, and one row with every key masked: NaN, as in torch), and
+    [1, 4, 1024, 128] with a random mask against float64 on every head."""
+    import math
+    p = irgen.attention_ir(1, 2, 256, 128, causal, mask=True)
+    t = data.make_inputs(p)
+    m = t["M"]
+    m[7, :] = 0
+    m[40:60, :128] = 0
+    t["M"] = m
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"mask causal={causal}", rms_floor=True)
+    p = irgen.attention_ir(1, 4, 1024, 128, causal, mask=True)
+    t = data.make_inputs(p)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    keep = t["M"].bool()
+    for h in range(4):
+        q, k, v = (t[n][0, h].double() for n in ("Q", "K", "V"))
+        s_ = (q @ k.T) / math.sqrt(128)
+        if causal:
+            s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
+        s_ = s_.masked_fill(~keep, float("-inf"))
+        compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"mask S=1024 head {h}", rms_floor=True)

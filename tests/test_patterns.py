@@ -83,7 +83,8 @@ def test_attention_ir_is_recognised():
         g, k = _kernel(p)
         hit = match_attention(g, k)
         assert hit is not None, key
-        Q, K, V, O, bt, hd, seq, dim, c, scale = hit
+        Q, K, V, O, bt, hd, seq, dim, c, scale, M = hit
+        assert M is None
         assert (Q.name, K.name, V.name, O.name) == ("Q", "K", "V", "O")
         assert (bt, hd, seq, dim, c) == (p.params["batch"], p.params["heads"], p.params["seq"], p.params["dim"], causal)
         assert abs(scale - p.params["scale"]) < 1e-7
@@ -189,7 +190,7 @@ def test_attention_with_another_scale_is_lowered_with_it():
             st["args"][1]["value"] = 0.1
     g, k = _mutated(p, "attention_causal", other_scale)
     hit = match_attention(g, k)
-    assert hit is not None and abs(hit[-1] - 0.1) < 1e-9
+    assert hit is not None and abs(hit[9] - 0.1) < 1e-9
 
 
 def test_renamed_buffers_still_match():

@@ -130,3 +130,10 @@ def test_attention_writes_every_row_once():
         for _, addr in sim.run(ctaid=cta, seed=cta)["stores"]:
             rows[addr // 256] += 1
     assert set(rows) == set(range(0, 1024, 32)) and set(rows.values()) == {8}
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_with_mask_pipeline_completes(causal):
+    # the mask adds global loads and per-column selects to the softmax threads, no hand-over
+    txt, rec = _attention(seq=512, causal=causal, mask_name="M")
+    _run_all(txt, rec)

@@ -186,3 +186,29 @@ def test_attention_ragged_sequence_emulated(shape, causal, opts):
     nor writes past S (the emulator raises on an access outside an allocation)."""
     p = irgen.attention_ir(*shape, causal)
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
+
+
+@pytest.mark.parametrize("shape,causal,opts", [
+    ((1, 2, 256, 128), True, {}),
+    ((1, 1, 256, 128), False, {"attn_half": False}),
+    ((1, 1, 320, 64), False, {}),                 # the mask with a ragged sequence at head dim 64
+])
+def test_attention_explicit_mask_emulated(shape, causal, opts):
+    """An explicit u8 mask [S, S] on the tensor cores: each softmax thread reads its row's 64 mask bytes
+    per key block and masks the zero bytes (a random mask: half the keys of every row)."""
+    p = irgen.attention_ir(*shape, causal, mask=True)
+    _check(p, data.make_inputs(p), opts, "tcgen05_attention")
+
+
+def test_attention_mask_with_fully_masked_blocks_and_rows():
+    # rows whose first key blocks are all masked keep a running max of -inf and exponentiate against 0;
+    # a row with every key masked is 0 / 0 = NaN, as in torch and in the IR's own semantics
+    p = irgen.attention_ir(1, 1, 256, 128, False, mask=True)
+    t = data.make_inputs(p)
+    m = t["M"]
+    m[5, :] = 0                                   # every key masked: NaN
+    m[10:20, :128] = 0                            # the first two key blocks masked
+    m[30, :] = 0
+    m[30, 255] = 1                                # only the last key
+    t["M"] = m
+    _check(p, t, {}, "tcgen05_attention")
