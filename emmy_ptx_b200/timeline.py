@@ -1,5 +1,8 @@
 """Clock64 timeline of the tensor-core attention: where each 64-row key/value block's cycles go.
 
+This is the package's tracing tool: a user-run probe of a kernel's pipeline. Nothing on the compile or
+launch path imports it, and the kernel carries the stamps only when it is built with ``trace=True``.
+
 ``python -m emmy_ptx_b200.timeline [--no-pingpong] [--bf16]`` runs config 5 (causal bf16 attention
 [8, 32, 4096, 128]) once untraced for timing, then once with the kernel's trace option
 (``attention_entry(..., trace=True)``: one u64 ``clock64`` stamp per event per kv block per CTA, taken
