@@ -154,7 +154,7 @@ def test_late_completions_expose_a_planted_early_release():
 def test_attention_head_dim_64_emulated(causal, opts):
     """Head dim 64: a Q tile and a K/V block are one 64-column TMA box, PV has N=64 and O takes 64
     TMEM columns per tile."""
-    p = irgen.attention_ir(1, 2, 512, 64, causal)
+    p = irgen.attention_ir(1, 1, 512, 64, causal)
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
 
 
