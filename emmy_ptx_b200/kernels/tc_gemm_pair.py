@@ -240,16 +240,20 @@ def gemm_pair_entry(name: str, batch: int, m: int, n: int, k: int, pairs: int = 
     a(f"add.u32 {t}, {t}, {nclu};")
     a(f"bra {l_pt};")
     a.label(l_pdone)
-    # drain: every stage this thread filled has been consumed (its empty barrier completed the
-    # round's phase: the MMAs that read both halves are done, so both CTAs' loads have landed)
+    # drain, so that no load of this thread is in flight when the CTA can finish.  CTA 0 waits for the
+    # full barrier of each stage's last round: it completes once both CTAs' bytes have landed, whether
+    # or not the MMAs ran.  CTA 1's loads complete CTA 0's barrier, so CTA 1 waits for its empty barrier
+    # instead: the MMAs that read the round are done, so its bytes had landed.  CTA 0 arrives at the
+    # final cluster barrier only after its own drain.
     for s in range(STAGES):
         skip = a.L("dskip")
         pn = a.r("p")
         a(f"setp.eq.u32 {pn}, {armed[s]}, 2;")
         a(f"@{pn} bra {skip};")
-        ebs = a.r()
-        a(f"add.u32 {ebs}, {bars}, {EMPTY + 8 * s};")
-        _wait(a, ebs, armed[s], err, ERR_DRAIN, skip)
+        dbs = a.r()
+        a(f"add.u32 {dbs}, {bars}, {EMPTY + 8 * s};")
+        a(f"@{lead} add.u32 {dbs}, {bars}, {FULL + 8 * s};")
+        _wait(a, dbs, armed[s], err, ERR_DRAIN, skip)
         a.label(skip)
     a(f"bra {l_end};")
 
