@@ -157,8 +157,10 @@ int emmy_nccl_init(int rank, int nranks, const char uid[128]);
 int emmy_allreduce_sum(uint64_t buf, size_t count, int dtype, void* stream);
 int emmy_nccl_destroy(void);
 
-/* Runs the tensor-core batched matmul (a launch record of kind "tcgen05_gemm": parameters A, B, C, the
- * two TMA descriptors, then a scratch pointer) without allocating device memory, for callers that cannot
+/* Runs the tensor-core batched matmul (a launch record of kind "tcgen05_gemm", the one-CTA-per-tile kernel
+ * that compile option gemm_pair=false builds: parameters A, B, C, the two TMA descriptors, then a scratch
+ * pointer; the default CTA-pair kernel needs a cluster launch and is not taken here) without allocating
+ * device memory, for callers that cannot
  * allocate when they launch: a host whose own pool already owns the GPU's memory, or a latency-critical
  * path where cudaMalloc/cudaFree may synchronise the device.  No counterpart in the reference.
  *  - function: the kernel, loaded with emmy_module_load_ptx / emmy_get_function; tmap_a / tmap_b: its
