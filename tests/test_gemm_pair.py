@@ -159,3 +159,21 @@ def test_pair_gemm_full_size_sampled():
         want = t["A"][b].double() @ t["B"][b].double()
         compare(t["C"][b], want, "f32", 1e-4, f"pair c4 batch {b}")
     ex.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("opts", [{"gemm_stages": 2}, {"sms": 4}, {"sms": 6, "gemm_stages": 3}])
+def test_pair_gemm_ring_and_cluster_counts_on_the_gpu(opts):
+    """The shallowest ring, and two or three clusters walking many tiles each (the tile loop strides by
+    the launched cluster count), against float64."""
+    from emmy_ptx_b200.runtime import Executable
+    p = irgen.bmm_naive_ir(3, 520, 776, 264)
+    ex = Executable(compile_graph(Graph.from_dict(p.graph), p.meta(), {"gemm_pair": True, **opts}))
+    t_cpu = data.make_inputs(p)
+    t = {k: v.cuda() for k, v in t_cpu.items()}
+    t["C"].fill_(float("nan"))
+    ex(t)
+    torch.cuda.synchronize()
+    assert ex.error_code() == 0
+    compare(t["C"].cpu(), t_cpu["A"].double() @ t_cpu["B"].double(), "f32", 1e-4, f"pair {opts}")
+    ex.close()

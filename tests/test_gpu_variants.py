@@ -214,3 +214,13 @@ def test_attention_explicit_mask(causal):
             s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
         s_ = s_.masked_fill(~keep, float("-inf"))
         compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"mask S=1024 head {h}", rms_floor=True)
+
+
+def test_attention_explicit_mask_head_dim_64_ragged():
+    """The mask with head dim 64 and S = 320 (a half-empty last query chunk) against the oracle."""
+    p = irgen.attention_ir(1, 2, 320, 64, False, mask=True)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), "mask d64 S=320", rms_floor=True)
