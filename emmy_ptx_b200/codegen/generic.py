@@ -150,16 +150,17 @@ class KernelEmitter:
         cand = [n for n in (self.kmeta.get("zero_outputs") or []) if n in self.params]
         stmts = []
         walk(self.op.body, stmts.append)
+        out_of = set()                           # outputs some statement disqualifies
         for st in stmts:
             cls = type(st).__name__
-            if cls == "Write" and st.output in cand and not getattr(st, "atomic", False):
-                cand.remove(st.output)
-            elif cls == "Load" and st.input in cand:
-                cand.remove(st.input)
-            elif cls == "CpAsyncCopy" and st.src in cand:
-                cand.remove(st.src)
+            if cls == "Write" and not getattr(st, "atomic", False):
+                out_of.add(st.output)
+            elif cls == "Load":
+                out_of.add(st.input)
+            elif cls == "CpAsyncCopy":
+                out_of.add(st.src)
         out, off = {}, 16
-        for n in cand:
+        for n in (c for c in cand if c not in out_of):
             elems = 1
             for x in self.shapes.get(n, (0,)):
                 elems *= int(x)

@@ -98,3 +98,15 @@ def test_runtime_refuses_another_grid_for_a_ticket_kernel():
     fake.funcs = [None]
     with pytest.raises(ValueError, match="compiled grid"):
         fake.launch(0, {}, 0, grid=[4, 1, 1], zero=False)
+
+
+def test_an_output_written_plainly_twice_is_left_alone():
+    # two plain Writes of a zeroed output (and a Load of it) disqualify it without tripping the check
+    from emmy_ptx_b200.irgen import TensorSpec, Tile, Axis, Load, Write, V, _graph, Problem
+    args = [TensorSpec("x", (64,), "f32", ("normal", 1.0)), TensorSpec("y", (64,), "f32", output=True)]
+    body = [Tile([Axis("i", 64)], [Load(["a"], "x", [V("i")], "f32"), Write("y", ["a"], [V("i")], "f32"),
+                                   Write("y", ["a"], [V("i")], "f32")])]
+    p = Problem("twice", "corpus", "twice", _graph("twice", args, body), args, grid=1, block=64,
+                zero_outputs=["y"])
+    rec = _compile(p, {"self_zeroing": True}).kernels[0]
+    assert rec["zero_outputs"] == ["y"] and "self_zeroing" not in rec
