@@ -119,11 +119,12 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         raise ValueError("pair_poly takes 0-4 of every 4 score pairs")
     if pair_poly and poly_every:
         raise ValueError("pair_poly and poly_every are alternatives")
-    if seq < BQ:
-        raise ValueError(f"tcgen05 attention needs S >= {BQ} (one whole Q tile box inside the tensor)")
+    if seq < 1:
+        raise ValueError("tcgen05 attention needs S >= 1")
     # a sequence that is no multiple of the CTA's 256 query rows: the last CTA's rows past S (and the
-    # key rows past S of its blocks) are zero-filled by TMA; their results are not stored, and a full
-    # (non-causal) launch masks the keys past S in the last block
+    # key rows past S of its blocks) are zero-filled by TMA, also when a whole box reaches past the
+    # tensor (S < 128 or 64); their results are not stored, and a full (non-causal) launch masks the keys
+    # past S in the last block
     nt = -(-seq // (BQ * TILES))
     spad = nt * BQ * TILES
     nblk = -(-seq // BKV)                        # key/value blocks holding data (value flags)

@@ -16,8 +16,9 @@ structural and fails closed — anything not recognised exactly is left to the C
   seeded with 0; every Write goes to the output and writes only accumulators; nothing else is
   written to global memory;
 * the GEMM's N and K are multiples of 8 (16-byte TMA rows; partial 128 x 256 edge tiles are
-  zero-filled on load and clipped on store); attention has head dim 64 or 128 and S >= 128 (rows
-  and keys past S in the last 256-row query chunk are zero-filled, masked and not stored).
+  zero-filled on load and clipped on store); attention has head dim 64 or 128 and any S (rows
+  and keys past S in the last 256-row query chunk are zero-filled, masked and not stored; that holds for
+  S below one tile too).
 
 Those checks find the operands, shapes and (for attention) the mask and scale.  The final gate is
 stricter: the kernel body must equal the canonical CUDA-core nest for those parameters
@@ -439,7 +440,7 @@ def try_lower(graph, node, kmeta, prefix, options):
     if hit is not None:
         Q, K, V, O, bt, hd, seq, dim, causal, scale, M = hit
         from .kernels import tc_attention
-        if dim not in (64, 128) or seq < tc_attention.BQ:
+        if dim not in (64, 128):
             return None
         if M is not None and seq % tc_attention.BKV:
             return None                  # the mask is read in 64-byte rows per key block

@@ -224,3 +224,16 @@ def test_attention_explicit_mask_head_dim_64_ragged():
     got, ex = _run_ours(p, t)
     assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
     compare(got["O"], want["O"], "bf16", rtol_for(p), "mask d64 S=320", rms_floor=True)
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 2, 64, 64), False), ((1, 2, 64, 64), True), ((1, 1, 48, 128), False),
+                                          ((2, 3, 16, 64), True)])
+def test_attention_shorter_than_one_tile(shape, causal):
+    """S below one 128-row query tile on the tensor cores: the Q boxes and the last K/V box reach past the
+    tensor and TMA reads zeros there; against the oracle."""
+    p = irgen.attention_ir(*shape, causal)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"short {shape} causal={causal}", rms_floor=True)

@@ -212,3 +212,12 @@ def test_attention_mask_with_fully_masked_blocks_and_rows():
     m[30, 255] = 1                                # only the last key
     t["M"] = m
     _check(p, t, {}, "tcgen05_attention")
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 2, 64, 64), False), ((1, 2, 64, 64), True), ((1, 1, 48, 128), False),
+                                          ((1, 1, 16, 64), True)])
+def test_attention_shorter_than_one_tile_emulated(shape, causal):
+    """S below one 128-row query tile (the reference's a_sdpa and a_sdpa_causal shapes): every Q box and
+    the last K/V box reach past the tensor and read zeros there; the keys past S are masked."""
+    p = irgen.attention_ir(*shape, causal)
+    _check(p, data.make_inputs(p), {}, "tcgen05_attention")
