@@ -28,14 +28,14 @@ def idesc_f16(m: int, n: int, a_mn_major: bool, b_mn_major: bool, half: bool = F
     return d
 
 
-def smem_desc_hi(lbo: int, sbo: int) -> int:
-    """Bits 16..63 of a shared-memory matrix descriptor (SWIZZLE_128B, version 1); the start
-    address (>>4) is added into bits 0..13 at run time."""
+def smem_desc_hi(lbo: int, sbo: int, swizzle: int = 128) -> int:
+    """Bits 16..63 of a shared-memory matrix descriptor (SWIZZLE_128B, or SWIZZLE_64B with
+    ``swizzle=64``; version 1); the start address (>>4) is added into bits 0..13 at run time."""
     d = 0
     d |= ((lbo >> 4) & 0x3FFF) << 16
     d |= ((sbo >> 4) & 0x3FFF) << 32
     d |= 1 << 46                 # descriptor version for sm_100
-    d |= 2 << 61                 # layout: SWIZZLE_128B
+    d |= {128: 2, 64: 4}[swizzle] << 61      # layout type: 2 SWIZZLE_128B, 4 SWIZZLE_64B
     return d
 
 

@@ -1,6 +1,7 @@
 """Causal / full attention on the 5th-generation tensor cores: QK^T and PV with tcgen05, S, P and O in TMEM.
 
-O = softmax(Q K^T * scale [+ causal mask]) V for Q, K, V, O bf16 [batch, heads, S, 128] — the online-softmax
+O = softmax(Q K^T * scale [+ causal mask]) V for Q, K, V, O bf16 [batch, heads, S, D] (D = 128 below; 64 and
+32 shrink the tiles, see ``attention_entry``) — the online-softmax
 Accum loop nest of the attention IR (config 5).  One CTA owns 256 query rows of one (batch, head) as two
 128-row tiles and walks the key/value sequence in 64-row blocks:
 
@@ -106,14 +107,18 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     torch's ``attn_mask``): each softmax thread reads its row's 64 bytes per key block and sets the
     masked scores to -inf; a row whose keys so far are all masked keeps a running max of -inf and
     exponentiates against 0, and a row with every key masked ends as 0 / 0 = NaN, as in torch."""
-    if dim not in (64, 128):
-        raise ValueError("tcgen05 attention takes head dim 64 or 128")
-    # the head dim sets the tile sizes: a Q tile or K/V block is dim / 64 TMA boxes of 64 columns
+    if dim not in (32, 64, 128):
+        raise ValueError("tcgen05 attention takes head dim 32, 64 or 128")
+    # the head dim sets the tile sizes: a Q tile or K/V block is dim / BOXC TMA boxes of BOXC columns,
+    # 64 columns (128-byte rows, SWIZZLE_128B) or, at head dim 32, 32 columns (64-byte rows, SWIZZLE_64B)
     D = dim
+    BOXC = min(D, 64)
+    SW = 2 * BOXC                 # row bytes of a box = the swizzle span
+    KPB = BOXC // 16              # K=16 MMA steps per box
     Q_BYTES = BQ * D * 2
-    Q_HALF = BQ * 64 * 2
+    Q_HALF = BQ * BOXC * 2        # one TMA box of a Q tile
     KV_BYTES = BKV * D * 2
-    KV_HALF = BKV * 64 * 2
+    KV_HALF = BKV * BOXC * 2      # one TMA box of a K/V block
     S_COL0 = TILES * D
     if not 0 <= pair_poly <= 4:
         raise ValueError("pair_poly takes 0-4 of every 4 score pairs")
@@ -150,8 +155,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     idesc_qk = idesc_f16(BQ, BKV, False, False)
     idesc_pv = idesc_f16(BQ, D, False, True)
     idesc_pv16 = idesc_f16(BQ, D, False, True, half=True)
-    kdesc_hi = smem_desc_hi(16, 1024)            # K-major SW128 (Q, K): 8-row groups 1 KiB apart
-    vdesc_hi = smem_desc_hi(KV_HALF, 1024)       # MN-major SW128 (V): 64-column atoms 8 KiB apart
+    kdesc_hi = smem_desc_hi(16, 8 * SW, SW)      # K-major (Q, K): 8-row groups of SW-byte rows
+    vdesc_hi = smem_desc_hi(KV_HALF, 8 * SW, SW)  # MN-major (V): BOXC-column atoms KV_HALF apart
     cscale = _f32(scale * LOG2E)
 
     tid, warp, lane, cta = a.r(), a.r(), a.r(), a.r()
@@ -319,10 +324,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     for i in range(TILES):
         r_i = a.r()
         a(f"add.u32 {r_i}, {row0}, {BQ * i};")
-        for hb in range(D // 64):
+        for hb in range(D // BOXC):
             d_ = a.r()
             a(f"add.u32 {d_}, {sQ}, {Q_BYTES * i + Q_HALF * hb};")
-            tma4(d_, tq, 64 * hb, r_i, qb)
+            tma4(d_, tq, BOXC * hb, r_i, qb)
     n_, stage, phase = a.r(), a.r(), a.r()
     armed = [a.r() for _ in range(STAGES)]
     for r_ in armed:
@@ -369,10 +374,10 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     else:
         a(f"selp.b64 {tsel}, {tv}, {tk}, {isv};")
     tma4(dst, tsel, 0, kvrow, fb)
-    if D == 128:
+    for hb in range(1, D // BOXC):
         dst2 = a.r()
-        a(f"add.u32 {dst2}, {dst}, {KV_HALF};")
-        tma4(dst2, tsel, 64, kvrow, fb)
+        a(f"add.u32 {dst2}, {dst}, {KV_HALF * hb};")
+        tma4(dst2, tsel, BOXC * hb, kvrow, fb)
     pw = a.r("p")
     a(f"add.u32 {stage}, {stage}, 1;")
     a(f"setp.eq.u32 {pw}, {stage}, {STAGES};")
@@ -402,11 +407,11 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         for i in range(TILES):
             r_i = a.r()
             a(f"add.u32 {r_i}, {rown}, {BQ * i};")
-            for hb in range(D // 64):
-                a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tq}, {{{64 * hb}, {r_i}, {hhn}, {bbn}}}];")
+            for hb in range(D // BOXC):
+                a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tq}, {{{BOXC * hb}, {r_i}, {hhn}, {bbn}}}];")
         for tmn in (tk, tv16 if half else tv):
-            for hb in range(D // 64):
-                a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tmn}, {{{64 * hb}, 0, {hhn}, {bbn}}}];")
+            for hb in range(D // BOXC):
+                a(f"cp.async.bulk.prefetch.tensor.4d.L2.global.tile [{tmn}, {{{BOXC * hb}, 0, {hhn}, {bbn}}}];")
         a.label(l_nopf)
     for s in range(STAGES):
         skip = a.L("dskip")
@@ -476,7 +481,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         qb_i = a.r()
         a(f"add.u32 {qb_i}, {sQ}, {Q_BYTES * i};")
         q0 = base_desc(qb_i, khi)
-        qdesc = [plus(q0, (k // 4) * Q_HALF + (k % 4) * 32) for k in range(D // 16)]
+        qdesc = [plus(q0, (k // KPB) * Q_HALF + (k % KPB) * 32) for k in range(D // 16)]
         kd, vd = [], []
         for st_ in range(STAGES):
             sb = a.r()
@@ -498,7 +503,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             P (block j-2) was read by a PV issued earlier from this thread, and the tensor core runs
             one thread's MMAs in order."""
             for k in range(D // 16):
-                db = plus(kd[stage_c], (k // 4) * KV_HALF + (k % 4) * 32)
+                db = plus(kd[stage_c], (k // KPB) * KV_HALF + (k % KPB) * 32)
                 a(f"tcgen05.mma.cta_group::1.kind::f16 [{scol_c[buf_c]}], {qdesc[k]}, {db}, {iqk}, "
                   f"{ptrue if k else pfalse};")
             a(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
@@ -512,7 +517,7 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
             With the f16 path the block's flag (from the value pre-pass) picks the MMAs: f16 P (columns
             0-31, two f16 per column) times the f16 copy of V in one pass, or, when V_j did not fit
             f16, bf16 P_hi (columns 0-31) and P_lo (32-63) times V itself."""
-            vds = [plus(vd[stage_c], 2048 * k) for k in range(BKV // 16)]
+            vds = [plus(vd[stage_c], 16 * SW * k) for k in range(BKV // 16)]      # 16 rows of SW bytes
             pacc = a.r("p")
             a(f"setp.ne.u32 {pacc}, {jreg}, 0;")
             p16 = None
@@ -1205,15 +1210,15 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
     dims = [D, seq, heads, batch]
     strides = [D * 2, seq * D * 2, heads * seq * D * 2]
     tmaps = [{"name": "tmQ", "tensor": qn, "dtype": "bf16", "dims": dims, "strides": strides,
-              "box": [64, BQ, 1, 1], "swizzle": "128B"}]
+              "box": [BOXC, BQ, 1, 1], "swizzle": f"{SW}B"}]
     tmaps += [{"name": f"tm{x}", "tensor": nm, "dtype": "bf16", "dims": dims, "strides": strides,
-               "box": [64, BKV, 1, 1], "swizzle": "128B"} for x, nm in (("K", kn), ("V", vn))]
+               "box": [BOXC, BKV, 1, 1], "swizzle": f"{SW}B"} for x, nm in (("K", kn), ("V", vn))]
     uparams = [qn, kn, vn, on] + ([mask_name] if mask else [])
     if half:
         v16n, vfn = scratch_names or (f"{prefix}{name}__v16", f"{prefix}{name}__vflag")
         uparams += [v16n, vfn]
         tmaps.append({"name": "tmV16", "tensor": v16n, "dtype": "f16", "dims": dims, "strides": strides,
-                      "box": [64, BKV, 1, 1], "swizzle": "128B"})
+                      "box": [BOXC, BKV, 1, 1], "swizzle": f"{SW}B"})
     extra = [{"name": "__err", "kind": "errword"}]
     if trace:
         extra.append({"name": "__trace", "kind": "buffer"})

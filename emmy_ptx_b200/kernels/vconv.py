@@ -33,8 +33,8 @@ def vconv_entry(name: str, batch: int, heads: int, seq: int, names=("V", "__v16"
     ragged = seq % block_rows != 0
     if ragged and block_rows != BLOCK_ROWS:
         raise ValueError(f"the {block_rows}-row value pre-pass needs S % {block_rows} == 0")
-    if dim not in (64, 128):
-        raise ValueError("the value pre-pass converts head dim 64 or 128")
+    if dim not in (32, 64, 128):
+        raise ValueError("the value pre-pass converts head dim 32, 64 or 128")
     block_bytes = block_rows * dim * 2
     bh0, nbh = bh_range if bh_range is not None else (0, batch * heads)
     if not (0 <= bh0 and nbh > 0 and bh0 + nbh <= batch * heads):

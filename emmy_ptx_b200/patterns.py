@@ -16,7 +16,7 @@ structural and fails closed — anything not recognised exactly is left to the C
   seeded with 0; every Write goes to the output and writes only accumulators; nothing else is
   written to global memory;
 * the GEMM's N and K are multiples of 8 (16-byte TMA rows; partial 128 x 256 edge tiles are
-  zero-filled on load and clipped on store); attention has head dim 64 or 128 and any S (rows
+  zero-filled on load and clipped on store); attention has head dim 32, 64 or 128 and any S (rows
   and keys past S in the last 256-row query chunk are zero-filled, masked and not stored; that holds for
   S below one tile too).
 
@@ -440,13 +440,13 @@ def try_lower(graph, node, kmeta, prefix, options):
     if hit is not None:
         Q, K, V, O, bt, hd, seq, dim, causal, scale, M = hit
         from .kernels import tc_attention
-        if dim not in (64, 128):
+        if dim not in (32, 64, 128):
             return None
         if M is not None and seq % tc_attention.BKV:
             return None                  # the mask is read in 64-byte rows per key block
         if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES) or M is not None:
-            # head dim 64, S no multiple of 256, or an explicit mask: the default schedule only (the
-            # other forms are built for head dim 128, whole 256-row query chunks and no mask)
+            # head dim 32 or 64, S no multiple of 256, or an explicit mask: the default schedule only
+            # (the other forms are built for head dim 128, whole 256-row query chunks and no mask)
             options = {k: v for k, v in options.items()
                        if k not in ("attn_persistent", "attn_kv128", "attn_overlap")}
         if M is not None:

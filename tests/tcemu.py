@@ -311,6 +311,8 @@ class TcEmulator(Emulator):
             a = dst + off
             if sw == "128B":
                 a ^= ((a >> 7) & 7) << 4
+            elif sw == "64B":
+                a ^= ((a >> 7) & 3) << 4
             if a + 16 > len(smem):
                 raise IndexError(f"TMA box past shared memory ({a})")
             smem[a:a + 16] = out[off:off + 16]
@@ -353,15 +355,19 @@ class TcEmulator(Emulator):
         start = (desc & 0x3FFF) << 4
         lbo = ((desc >> 16) & 0x3FFF) << 4
         sbo = ((desc >> 32) & 0x3FFF) << 4
-        if ((desc >> 61) & 7) != 2:
-            raise NotImplementedError("only the 128-byte swizzle is emulated")
+        layout = (desc >> 61) & 7
+        if layout not in (2, 4):
+            raise NotImplementedError("only the 128- and 64-byte swizzles are emulated")
+        span = 128 if layout == 2 else 64        # bytes of one swizzled row
         i = np.arange(rows)[:, None]
         kk = np.arange(k)[None, :]
         if not mn_major:
-            a = start + (i // 8) * sbo + (i % 8) * 128 + kk * 2
+            a = start + (i // 8) * sbo + (i % 8) * span + kk * 2
         else:
-            a = start + (i // 64) * lbo + (kk // 8) * sbo + (kk % 8) * 128 + (i % 64) * 2
-        a = self._sw(a.astype(np.int64))
+            per = span // 2
+            a = start + (i // per) * lbo + (kk // 8) * sbo + (kk % 8) * span + (i % per) * 2
+        a = a.astype(np.int64)
+        a = self._sw(a) if layout == 2 else a ^ (((a >> 7) & 3) << 4)
         sm = np.frombuffer(bytes(smem), dtype=np.uint8)
         bits = sm[a].astype(np.uint16) | (sm[a + 1].astype(np.uint16) << 8)
         return _halves_to_float(bits, fmt)

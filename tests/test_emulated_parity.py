@@ -156,9 +156,9 @@ def test_small_cuda_core_bmm_and_attention():
 
 
 def test_attention_the_tensor_core_lowering_declines():
-    # head dim 32 and 48 rows (not a multiple of the 256-row query tile pair): the attention pattern
-    # declines it with the default options, so the CUDA-core form runs (every record generic)
-    p = irgen.attention_ir(1, 1, 48, 32, True)
+    # head dim 256 has no tensor-core form (32, 64 and 128 do): the attention pattern declines it, so
+    # the CUDA-core form runs (every record generic)
+    p = irgen.attention_ir(1, 1, 16, 256, True)
     t, got = _run_ours(p)
     _check(p, t, got, f"emu:{p.name}")
 

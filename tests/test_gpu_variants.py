@@ -237,3 +237,27 @@ def test_attention_shorter_than_one_tile(shape, causal):
     got, ex = _run_ours(p, t)
     assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
     compare(got["O"], want["O"], "bf16", rtol_for(p), f"short {shape} causal={causal}", rms_floor=True)
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 2, 256, 32), True), ((1, 1, 320, 32), False), ((1, 4, 48, 32), False),
+                                          ((2, 3, 16, 32), False)])
+def test_attention_head_dim_32(shape, causal):
+    """Head dim 32 on the tensor cores (64-byte rows, the 64-byte swizzle): small cases against the oracle,
+    and [1, 4, 1024, 32] against float64 on every head."""
+    import math
+    p = irgen.attention_ir(*shape, causal)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"d32 {shape} causal={causal}", rms_floor=True)
+    p = irgen.attention_ir(1, 4, 1024, 32, causal)
+    t = data.make_inputs(p)
+    got, ex = _run_ours(p, t)
+    assert ex.error_code() == 0
+    for h in range(4):
+        q, k, v = (t[n][0, h].double() for n in ("Q", "K", "V"))
+        s_ = (q @ k.T) / math.sqrt(32)
+        if causal:
+            s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
+        compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"d32 S=1024 head {h}", rms_floor=True)

@@ -122,9 +122,11 @@ def test_attention_with_a_different_mask_is_refused():
 
 
 def test_small_head_dim_stays_on_cuda_cores():
-    # head dim 32 has no tensor-core form (Q, K and V rows of 64 bytes); 64 and 128 do, at any S
-    p = irgen.attention_ir(1, 2, 64, 32, False)
+    # head dim 256 has no tensor-core form; 32, 64 and 128 do, at any S
+    p = irgen.attention_ir(1, 1, 16, 256, False)
     assert compile_graph(Graph.from_dict(p.graph), p.meta()).kernels[0]["kind"] == "generic"
+    d32 = irgen.attention_ir(1, 2, 64, 32, False)
+    assert compile_graph(Graph.from_dict(d32.graph), d32.meta()).kernels[-1]["kind"] == "tcgen05_attention"
     short = irgen.SMALL["c5nc"]()             # D = 64, S = 32: below one query tile, on the tensor cores
     assert compile_graph(Graph.from_dict(short.graph), short.meta()).kernels[-1]["kind"] == "tcgen05_attention"
 

@@ -221,3 +221,18 @@ def test_attention_shorter_than_one_tile_emulated(shape, causal):
     the last K/V box reach past the tensor and read zeros there; the keys past S are masked."""
     p = irgen.attention_ir(*shape, causal)
     _check(p, data.make_inputs(p), {}, "tcgen05_attention")
+
+
+@pytest.mark.parametrize("shape,causal,opts", [
+    ((1, 2, 256, 32), True, {}),
+    ((1, 1, 320, 32), False, {}),
+    ((1, 1, 256, 32), True, {"attn_half": False}),
+    ((1, 4, 48, 32), False, {}),                  # the reference's a_sdpa_scale shape (scale 1/sqrt(32) here)
+    ((1, 2, 32, 32), False, {}),                  # a_sdpa_short
+])
+def test_attention_head_dim_32_emulated(shape, causal, opts):
+    """Head dim 32: Q, K and V rows of 64 bytes, TMA boxes of 32 columns with the 64-byte swizzle, and
+    SWIZZLE_64B shared-memory descriptors (K-major for Q and K, MN-major for V: one 32-column atom,
+    16 rows of 64 bytes per MMA); PV has N=32 and O takes 32 TMEM columns per tile."""
+    p = irgen.attention_ir(*shape, causal)
+    _check(p, data.make_inputs(p), opts, "tcgen05_attention")
