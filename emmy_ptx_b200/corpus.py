@@ -636,7 +636,7 @@ def sdpa(batch, heads, seq, dim, causal, scale=None, mask=False):
     """scaled_dot_product_attention of bf16 Q, K, V [batch, heads, seq, dim] (optionally causal, with
     an explicit scale): the online-softmax nest of the attention IR at the small shapes of the
     reference's attention cases.  Head dim 32, 64 or 128 runs on the tensor cores at any S (the mask
-    also needs S % 64 == 0); other head dims run on the CUDA cores."""
+    also needs S % 16 == 0); other head dims run on the CUDA cores."""
     from .irgen import attention_ir
     base = attention_ir(batch, heads, seq, dim, causal, scale=scale, mask=mask)
     return Problem(f"sdpa_{batch}x{heads}x{seq}x{dim}{'_causal' if causal else ''}{'_mask' if mask else ''}",

@@ -140,8 +140,8 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         raise ValueError("trace supports at most 64 key/value blocks")
     half = half and precise
     mask = mask_name is not None
-    if mask and seq % BKV:
-        raise ValueError("the masked attention reads 64-byte mask rows: S % 64 == 0")
+    if mask and seq % 16:
+        raise ValueError("the masked attention reads its mask rows in 16-byte pieces: S % 16 == 0")
     if pack_in_turn and (pack_after_turn or not pingpong):
         raise ValueError("pack_in_turn applies to the default split packing with turns")
     if defer_sum and (poly_every or not pack_after_turn):
@@ -770,12 +770,26 @@ def attention_entry(name: str, batch: int, heads: int, seq: int, causal: bool, s
         ma, mo = a.r("rd"), a.r("rd")
         a(f"mul.wide.u32 {mo}, {jj}, {BKV};")
         a(f"add.s64 {ma}, {mrow}, {mo};")
-        g_ = ""
-        if prow_m is not None:
+        partial = seq % BKV != 0            # the last block's 16-byte pieces past S are not read
+        if prow_m is not None or partial:
             for w_ in mw:
-                a(f"mov.u32 {w_}, 0x01010101;")
-            g_ = f"@{prow_m} "
+                a(f"mov.u32 {w_}, 0x01010101;")   # kept; keys past S are masked by the key limit
+        kv0m = None
+        if partial:
+            kv0m = a.r()
+            a(f"shl.b32 {kv0m}, {jj}, 6;")
         for i_ in range(BKV // 16):
+            g_ = ""
+            if partial and seq - 16 * i_ <= 0:
+                continue                        # a piece past S in every block (S < 64)
+            if partial:
+                pp_ = a.r("p")
+                a(f"setp.lt.u32 {pp_}, {kv0m}, {seq - 16 * i_};")   # 64*jj + 16*i < S
+                if prow_m is not None:
+                    a(f"and.pred {pp_}, {pp_}, {prow_m};")
+                g_ = f"@{pp_} "
+            elif prow_m is not None:
+                g_ = f"@{prow_m} "
             a(f"{g_}ld.global.nc.v4.u32 {{{', '.join(mw[4 * i_:4 * i_ + 4])}}}, [{ma}+{16 * i_}];")
     wait_bar_warp(a, sfb, par_s, err, ERR_SOFTMAX, l_drain)
     p16 = None

@@ -442,8 +442,8 @@ def try_lower(graph, node, kmeta, prefix, options):
         from .kernels import tc_attention
         if dim not in (32, 64, 128):
             return None
-        if M is not None and seq % tc_attention.BKV:
-            return None                  # the mask is read in 64-byte rows per key block
+        if M is not None and seq % 16:
+            return None                  # the mask rows are read in 16-byte pieces
         if dim != tc_attention.D or seq % (tc_attention.BQ * tc_attention.TILES) or M is not None:
             # head dim 32 or 64, S no multiple of 256, or an explicit mask: the default schedule only
             # (the other forms are built for head dim 128, whole 256-row query chunks and no mask)

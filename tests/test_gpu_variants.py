@@ -261,3 +261,15 @@ def test_attention_head_dim_32(shape, causal):
         if causal:
             s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
         compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4, f"d32 S=1024 head {h}", rms_floor=True)
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 2, 16, 32), False), ((1, 1, 80, 64), True), ((1, 1, 208, 128), False)])
+def test_attention_mask_short_and_ragged(shape, causal):
+    """The explicit mask with S a multiple of 16 but not of 64 (the reference's a_mask shape first), against
+    the oracle: the last key block reads only the 16-byte mask pieces below S."""
+    p = irgen.attention_ir(*shape, causal, mask=True)
+    t = data.make_inputs(p)
+    want = oracle_outputs(p, t)
+    got, ex = _run_ours(p, t)
+    assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
+    compare(got["O"], want["O"], "bf16", rtol_for(p), f"mask {shape}", rms_floor=True)

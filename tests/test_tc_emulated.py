@@ -236,3 +236,11 @@ def test_attention_head_dim_32_emulated(shape, causal, opts):
     16 rows of 64 bytes per MMA); PV has N=32 and O takes 32 TMEM columns per tile."""
     p = irgen.attention_ir(*shape, causal)
     _check(p, data.make_inputs(p), opts, "tcgen05_attention")
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 2, 16, 32), False), ((1, 1, 80, 64), True), ((1, 1, 208, 128), False)])
+def test_attention_mask_short_and_ragged_emulated(shape, causal):
+    """The explicit mask when S is a multiple of 16 but not of 64 (the reference's a_mask shape first):
+    the last key block reads only its 16-byte mask pieces below S."""
+    p = irgen.attention_ir(*shape, causal, mask=True)
+    _check(p, data.make_inputs(p), {}, "tcgen05_attention")
