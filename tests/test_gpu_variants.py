@@ -273,3 +273,30 @@ def test_attention_mask_short_and_ragged(shape, causal):
     got, ex = _run_ours(p, t)
     assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0
     compare(got["O"], want["O"], "bf16", rtol_for(p), f"mask {shape}", rms_floor=True)
+
+
+def test_attention_random_shapes_against_float64():
+    """Twelve seeded random shapes (head dim 32, 64 or 128; S from 16 to 700; causal or not; a random
+    mask where S allows it) on the tensor cores, each against float64 torch on every head."""
+    import math
+    import random
+    rng = random.Random(20261202)
+    for n in range(12):
+        dim = rng.choice([32, 64, 128])
+        seq = rng.choice([16, 48, 64, 96, 130, 200, 256, 320, 512, 700])
+        causal = rng.random() < 0.5
+        mask = seq % 16 == 0 and rng.random() < 0.4
+        heads = rng.choice([1, 2, 3])
+        p = irgen.attention_ir(1, heads, seq, dim, causal, mask=mask)
+        t = data.make_inputs(p)
+        got, ex = _run_ours(p, t)
+        assert ex.records[-1]["kind"] == "tcgen05_attention" and ex.error_code() == 0, (dim, seq, causal, mask)
+        for h in range(heads):
+            q, k, v = (t[nm][0, h].double() for nm in ("Q", "K", "V"))
+            s_ = (q @ k.T) / math.sqrt(dim)
+            if causal:
+                s_ = s_.masked_fill(torch.ones_like(s_, dtype=torch.bool).triu(1), float("-inf"))
+            if mask:
+                s_ = s_.masked_fill(~t["M"].bool(), float("-inf"))
+            compare(got["O"][0, h], torch.softmax(s_, -1) @ v, "bf16", 1e-4,
+                    f"random #{n} d{dim} S{seq} causal={causal} mask={mask} head {h}", rms_floor=True)
