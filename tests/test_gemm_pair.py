@@ -177,3 +177,24 @@ def test_pair_gemm_ring_and_cluster_counts_on_the_gpu(opts):
     assert ex.error_code() == 0
     compare(t["C"].cpu(), t_cpu["A"].double() @ t_cpu["B"].double(), "f32", 1e-4, f"pair {opts}")
     ex.close()
+
+
+@pytest.mark.gpu
+def test_pair_gemm_random_shapes_against_float64():
+    """Fifteen seeded random shapes (any M, N and K multiples of 8) through the default GEMM lowering."""
+    import random
+    from emmy_ptx_b200.runtime import Executable
+    rng = random.Random(1202)
+    for n in range(15):
+        shape = (rng.randint(1, 3), rng.randint(1, 700), 8 * rng.randint(1, 90), 8 * rng.randint(1, 90))
+        p = irgen.bmm_naive_ir(*shape)
+        ex = Executable(compile_graph(Graph.from_dict(p.graph), p.meta()))
+        assert ex.records[0]["kind"] == "tcgen05_gemm_pair"
+        t_cpu = data.make_inputs(p)
+        t = {k: v.cuda() for k, v in t_cpu.items()}
+        t["C"].fill_(float("nan"))
+        ex(t)
+        torch.cuda.synchronize()
+        assert ex.error_code() == 0, shape
+        compare(t["C"].cpu(), t_cpu["A"].double() @ t_cpu["B"].double(), "f32", 1e-4, f"random pair {shape}")
+        ex.close()
